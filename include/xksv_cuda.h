@@ -1,0 +1,110 @@
+/*
+ * xksv_cuda.h -- C ABI of the B200 slab decoder (libxksv_cuda.so).
+ *
+ * Part 1 keeps the reference's GPU entry points: same names, signatures,
+ * argument meaning and return codes, so ctypes callers of the reference
+ * library (python/runtime.py:40-44, 251-255; python/tune.py:16-19) load this
+ * library unchanged through XKSV_CUDA_LIBRARY.  `input` is a HOST pointer to
+ * one encoded slab; `output`, `x` are DEVICE pointers on the current device.
+ * Each call is synchronous and returns 0 on success, 1 on any failure
+ * (null pointer, bad header or size, invalid codebook or bit stream, CUDA
+ * error).  Outputs are written only through device kernels of this library.
+ *
+ * Part 2 adds a device-resident batched interface (no counterpart in the
+ * reference): a plan describes many slabs of one payload buffer already in
+ * device memory; decode / GEMV / GEMM are enqueued on a caller stream
+ * without host synchronisation, and errors are collected in a device status
+ * word read back by xksv_plan_status().
+ */
+#ifndef XKSV_CUDA_H
+#define XKSV_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------- Part 1: reference-compatible entry points ------------- */
+
+/* Serial-codec ("bf16-huffman-tile16") slab -> BF16 row-major [rows, cols]
+ * at output.  Replaces reference cuda/decode.cu:85-87 (validation :47-66). */
+int xksv_cuda_decode(const void* input, size_t size, size_t rows, size_t cols, void* output);
+
+/* Serial-codec slab fused with y = W x: x is FP32 [cols], output FP32 [rows]
+ * (overwritten).  Replaces reference cuda/decode.cu:89-92. */
+int xksv_cuda_gemv(const void* input, size_t size, size_t rows, size_t cols, const float* x,
+                   float* output);
+
+/* Serial-codec slab fused with Y = W X: x is FP32 row-major [cols, batch],
+ * output FP32 row-major [rows, batch] (overwritten).  Replaces reference
+ * cuda/decode.cu:94-98. */
+int xksv_cuda_gemm(const void* input, size_t size, size_t rows, size_t cols, size_t batch,
+                   const float* x, float* output);
+
+/* Parallel-codec ("bf16-huffman-parallel32", XKSP2) slab -> BF16 row-major
+ * [rows, cols] (dimensions read from the slab header).  Replaces reference
+ * cuda/parallel.cu:68-70 (validation :33-53). */
+int xksv_cuda_decode_parallel(const void* input, size_t n, void* output);
+
+/* Parallel-codec slab fused with y = W x, x FP32 [cols], output FP32 [rows]
+ * (overwritten).  Replaces reference cuda/parallel.cu:71-74. */
+int xksv_cuda_gemv_parallel(const void* input, size_t n, const float* x, float* output);
+
+/* ---------------- Part 2: batched, device-resident interface ------------ */
+
+enum {
+  XKSV_CODEC_RAW = 0,        /* block stores the source bytes unchanged */
+  XKSV_CODEC_TILE16 = 1,     /* "bf16-huffman-tile16" (serial codec) */
+  XKSV_CODEC_PARALLEL32 = 2  /* "bf16-huffman-parallel32" (XKSP2) */
+};
+
+/* One archive block, as listed in the archive index (src/compile.cpp:459-470):
+ * where its bytes sit in the payload buffer, its slab shape, and where its
+ * result goes.  For decode, dst_offset is a byte offset into the output.
+ * For GEMV/GEMM, dst_offset is the first output row and x_offset the element
+ * offset of this slab's column 0 inside x (so one plan can serve several
+ * weight matrices).  Raw blocks used by GEMV/GEMM must give rows and cols
+ * (BF16 row-major data); raw blocks used by decode only need src_size. */
+typedef struct xksv_slab {
+  uint64_t src_offset;
+  uint64_t src_size;
+  uint64_t rows;
+  uint64_t cols;
+  uint64_t dst_offset;
+  uint64_t x_offset;
+  uint32_t codec;
+  uint32_t flags; /* must be 0 */
+} xksv_slab;
+
+typedef struct xksv_plan xksv_plan;
+
+/* Validates the host table, copies it to the current device and groups it by
+ * codec.  Returns 0 and a plan, or 1. */
+int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** plan);
+void xksv_plan_destroy(xksv_plan* plan);
+
+/* Enqueues decode of every slab of the plan from d_payload (device) into
+ * d_out (device) on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Returns 1 only for launch errors; stream errors are found by
+ * xksv_plan_status(). */
+int xksv_plan_decode(const xksv_plan* plan, const void* d_payload, void* d_out, void* stream);
+
+/* Enqueues Y[dst_offset + r, b] = sum_c W[r, c] * X[x_offset + c, b] for every
+ * slab, X FP32 row-major [*, batch] and Y FP32 row-major [*, batch] (rows of
+ * Y not covered by a slab are left untouched). */
+int xksv_plan_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y,
+                   size_t batch, void* stream);
+
+/* Synchronises `stream`, returns 0 when no slab reported an error since the
+ * last call (then clears the word), else 1. */
+int xksv_plan_status(const xksv_plan* plan, void* stream);
+
+/* Number of kernel launches the last xksv_plan_decode / xksv_plan_gemm call
+ * enqueued (for accounting in benchmarks). */
+int xksv_plan_launches(const xksv_plan* plan);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* XKSV_CUDA_H */

@@ -1,0 +1,381 @@
+// C ABI of libxksv_cuda.so (declared in include/xksv_cuda.h).
+//
+// The five reference entry points keep the reference's validation order and
+// 0/1 return contract (cuda/decode.cu:47-98, cuda/parallel.cu:33-74).  Unlike
+// the reference they do not cudaMalloc/cudaFree per call: each device keeps a
+// growable staging buffer, a one-entry slab table and a status word, guarded
+// by a mutex (calls stay synchronous on the legacy default stream, like the
+// reference).  The batched plan interface enqueues work on a caller stream.
+#include <algorithm>
+#include <cstring>
+#include <limits>
+#include <mutex>
+#include <vector>
+
+#include "../../include/xksv_cuda.h"
+#include "kernels.h"
+
+namespace xksv {
+namespace {
+
+constexpr size_t kMaxDevices = 64;
+constexpr uint64_t kMax = std::numeric_limits<uint64_t>::max();
+
+uint64_t get64(const uint8_t* p) {
+  uint64_t v = 0;
+  for (int i = 0; i < 8; ++i) v |= uint64_t(p[i]) << (8 * i);
+  return v;
+}
+
+// Canonical assignment succeeds iff the Kraft sum of the lengths is <= 1
+// (src/codec.cpp:11-29 / cuda/decode.cu:52-66 fail exactly on carry-out).
+bool lengths_ok(const uint8_t* lens) {
+  uint32_t cnt[256] = {0};
+  int maxlen = 0;
+  for (int s = 0; s < 256; ++s)
+    if (lens[s]) {
+      ++cnt[lens[s]];
+      maxlen = std::max(maxlen, int(lens[s]));
+    }
+  int64_t avail = 1;
+  for (int l = 1; l <= maxlen; ++l) {
+    avail = 2 * avail - cnt[l];
+    if (avail < 0) return false;
+    avail = std::min<int64_t>(avail, 4096);
+  }
+  return true;
+}
+
+// cuda/decode.cu:49-66 for a host slab.
+bool serial_header_ok(const uint8_t* p, size_t size, size_t rows, size_t cols, size_t batch) {
+  if (!p || size < kHdr || !rows || !cols || !batch || cols > kMax / rows || batch > kMax / rows ||
+      batch > kMax / cols)
+    return false;
+  uint64_t n = get64(p), nbits = get64(p + 8);
+  if (n != uint64_t(rows) * cols || n > size - kHdr || nbits / 8 + (nbits % 8 != 0) != size - kHdr - n)
+    return false;
+  return lengths_ok(p + 16);
+}
+
+// cuda/parallel.cu:34-53 for a host slab; returns rows/cols.
+bool parallel_header_ok(const uint8_t* p, size_t n, uint64_t* rows_out, uint64_t* cols_out) {
+  if (!p || n < 32 || std::memcmp(p, "XKSP2\0\0\0", 8)) return false;
+  uint64_t rows = get64(p + 8), cols = get64(p + 16), count = get64(p + 24);
+  if (!rows || rows > 16 || !cols || !count || count > 32 || cols > kMax / rows ||
+      count > rows * cols || rows * cols > n || rows * cols > kMax / 32 || n < 32 + 8 * count)
+    return false;
+  size_t pos = 32 + 8 * count;
+  for (uint64_t k = 0; k < count; ++k) {
+    uint64_t len = get64(p + 32 + 8 * k);
+    if (len < kHdr || len > n - pos) return false;
+    uint64_t elements = get64(p + pos), bits = get64(p + pos + 8);
+    uint64_t start = rows * cols * k / count;
+    if (elements != rows * cols * (k + 1) / count - start || elements > len - kHdr ||
+        bits / 8 + (bits % 8 != 0) != len - kHdr - elements)
+      return false;
+    if (!lengths_ok(p + pos + 16)) return false;
+    pos += len;
+  }
+  if (pos != n) return false;
+  *rows_out = rows;
+  *cols_out = cols;
+  return true;
+}
+
+struct DevCtx {
+  std::mutex mu;
+  bool init = false;
+  uint8_t* stage = nullptr;
+  size_t cap = 0;
+  Slab* d_slab = nullptr;
+  int* d_status = nullptr;
+  int* h_status = nullptr;  // pinned
+  int sms = 148;
+};
+DevCtx g_ctx[kMaxDevices];
+
+DevCtx* ctx_current() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || size_t(dev) >= kMaxDevices) return nullptr;
+  DevCtx& c = g_ctx[dev];
+  if (!c.init) {
+    if (cudaMalloc(&c.d_slab, sizeof(Slab)) != cudaSuccess) return nullptr;
+    if (cudaMalloc(&c.d_status, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMallocHost(&c.h_status, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaDeviceGetAttribute(&c.sms, cudaDevAttrMultiProcessorCount, dev);
+    c.init = true;
+  }
+  return &c;
+}
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+enum class Kind { Serial, Parallel };
+
+// Stages one slab, launches the kernel on the legacy default stream, and
+// returns the reference's 0/1 result.
+int run_single(Kind kind, const void* input, size_t size, uint64_t rows, uint64_t cols,
+               void* output, const float* x, size_t batch, bool gemm) {
+  DevCtx* c = ctx_current();
+  if (!c) return 1;
+  std::lock_guard<std::mutex> lock(c->mu);
+  cudaStream_t st = 0;
+  const uint8_t* payload;
+  if (is_device_ptr(input)) {
+    payload = static_cast<const uint8_t*>(input);
+  } else {
+    if (size > c->cap) {
+      if (c->stage) cudaFree(c->stage);
+      size_t cap = std::max<size_t>(size + 64, c->cap * 2);
+      if (cudaMalloc(&c->stage, cap) != cudaSuccess) {
+        c->stage = nullptr;
+        c->cap = 0;
+        return 1;
+      }
+      c->cap = cap;
+    }
+    if (cudaMemcpyAsync(c->stage, input, size, cudaMemcpyHostToDevice, st) != cudaSuccess) return 1;
+    payload = c->stage;
+  }
+  Slab s{0, size, rows, cols, 0, 0};
+  if (cudaMemcpyAsync(c->d_slab, &s, sizeof(Slab), cudaMemcpyHostToDevice, st) != cudaSuccess) return 1;
+  if (cudaMemsetAsync(c->d_status, 0, sizeof(int), st) != cudaSuccess) return 1;
+  cudaError_t e = cudaSuccess;
+  if (!gemm) {
+    e = kind == Kind::Serial
+            ? launch_serial_decode(c->d_slab, 1, payload, static_cast<uint8_t*>(output), c->d_status, 1, st)
+            : launch_parallel_decode(c->d_slab, 1, payload, static_cast<uint8_t*>(output), c->d_status, 1, st);
+  } else {
+    float* y = static_cast<float*>(output);
+    for (size_t b0 = 0; b0 < batch && e == cudaSuccess; b0 += 8) {
+      uint32_t nb = uint32_t(std::min<size_t>(8, batch - b0));
+      e = kind == Kind::Serial
+              ? launch_serial_gemm(c->d_slab, 1, payload, x, y, uint32_t(batch), uint32_t(b0), nb, c->d_status, 1, st)
+              : launch_parallel_gemm(c->d_slab, 1, payload, x, y, uint32_t(batch), uint32_t(b0), nb, c->d_status, 1, st);
+    }
+  }
+  if (e != cudaSuccess) return 1;
+  if (cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return 1;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return 1;
+  return *c->h_status == 0 ? 0 : 1;
+}
+
+}  // namespace
+}  // namespace xksv
+
+struct xksv_plan {
+  int device = 0;
+  xksv::Slab* d_slabs = nullptr;  // [serial | parallel | raw]
+  uint32_t n_ser = 0, n_par = 0, n_raw = 0;
+  bool raw_gemm_ok = true;
+  uint64_t max_batch_rows = 0;
+  int* d_status = nullptr;
+  int* h_status = nullptr;
+  int grid_ser = 148, grid_par = 148, grid_raw = 148;
+  int launches = 0;
+};
+
+using namespace xksv;
+
+extern "C" {
+
+int xksv_cuda_decode(const void* input, size_t size, size_t rows, size_t cols, void* output) {
+  const uint8_t* p = static_cast<const uint8_t*>(input);
+  if (!p || !output) return 1;
+  if (!is_device_ptr(input) && !serial_header_ok(p, size, rows, cols, 1)) return 1;
+  if (is_device_ptr(input) && (size < kHdr || !rows || !cols || cols > kMax / rows)) return 1;
+  return run_single(Kind::Serial, input, size, rows, cols, output, nullptr, 1, false);
+}
+
+int xksv_cuda_gemv(const void* input, size_t size, size_t rows, size_t cols, const float* x,
+                   float* output) {
+  return xksv_cuda_gemm(input, size, rows, cols, 1, x, output);
+}
+
+int xksv_cuda_gemm(const void* input, size_t size, size_t rows, size_t cols, size_t batch,
+                   const float* x, float* output) {
+  const uint8_t* p = static_cast<const uint8_t*>(input);
+  if (!x || !p || !output) return 1;
+  if (batch > std::numeric_limits<uint32_t>::max()) return 1;
+  if (!is_device_ptr(input) && !serial_header_ok(p, size, rows, cols, batch)) return 1;
+  if (is_device_ptr(input) && (size < kHdr || !rows || !cols || !batch || cols > kMax / rows)) return 1;
+  return run_single(Kind::Serial, input, size, rows, cols, output, x, batch, true);
+}
+
+int xksv_cuda_decode_parallel(const void* input, size_t n, void* output) {
+  const uint8_t* p = static_cast<const uint8_t*>(input);
+  if (!p || !output) return 1;
+  uint64_t rows = 0, cols = 0;
+  if (is_device_ptr(input)) {
+    uint8_t h[32];
+    if (n < 32 || cudaMemcpy(h, input, 32, cudaMemcpyDeviceToHost) != cudaSuccess) return 1;
+    rows = get64(h + 8);
+    cols = get64(h + 16);
+  } else if (!parallel_header_ok(p, n, &rows, &cols)) {
+    return 1;
+  }
+  return run_single(Kind::Parallel, input, n, rows, cols, output, nullptr, 1, false);
+}
+
+int xksv_cuda_gemv_parallel(const void* input, size_t n, const float* x, float* output) {
+  const uint8_t* p = static_cast<const uint8_t*>(input);
+  if (!x || !p || !output) return 1;
+  uint64_t rows = 0, cols = 0;
+  if (is_device_ptr(input)) {
+    uint8_t h[32];
+    if (n < 32 || cudaMemcpy(h, input, 32, cudaMemcpyDeviceToHost) != cudaSuccess) return 1;
+    rows = get64(h + 8);
+    cols = get64(h + 16);
+  } else if (!parallel_header_ok(p, n, &rows, &cols)) {
+    return 1;
+  }
+  return run_single(Kind::Parallel, input, n, rows, cols, output, x, 1, true);
+}
+
+int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
+  if (!out || (!slabs && n) || n > std::numeric_limits<uint32_t>::max()) return 1;
+  *out = nullptr;
+  std::vector<Slab> ser, par, raw;
+  bool raw_gemm_ok = true;
+  for (size_t i = 0; i < n; ++i) {
+    const xksv_slab& s = slabs[i];
+    if (s.flags || s.src_offset > kMax - s.src_size) return 1;
+    Slab d{s.src_offset, s.src_size, s.rows, s.cols, s.dst_offset, s.x_offset};
+    switch (s.codec) {
+      case XKSV_CODEC_TILE16:
+        if (!s.rows || !s.cols || s.cols > kMax / s.rows || s.src_size < kHdr) return 1;
+        ser.push_back(d);
+        break;
+      case XKSV_CODEC_PARALLEL32:
+        if (!s.rows || s.rows > 16 || !s.cols || s.src_size < 32) return 1;
+        par.push_back(d);
+        break;
+      case XKSV_CODEC_RAW:
+        if (!s.rows || !s.cols || s.cols > kMax / s.rows || s.rows * s.cols * 2 != s.src_size)
+          raw_gemm_ok = false;
+        raw.push_back(d);
+        break;
+      default:
+        return 1;
+    }
+  }
+  auto* p = new xksv_plan();
+  cudaGetDevice(&p->device);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
+  (void)sms;
+  // one CTA per slab (per PWARPS slabs for the parallel codec): the block
+  // scheduler balances slabs of different cost
+  p->grid_ser = 1 << 30;
+  p->grid_par = 1 << 30;
+  p->grid_raw = 1 << 30;
+  p->n_ser = uint32_t(ser.size());
+  p->n_par = uint32_t(par.size());
+  p->n_raw = uint32_t(raw.size());
+  p->raw_gemm_ok = raw_gemm_ok;
+  std::vector<Slab> all;
+  all.reserve(n);
+  all.insert(all.end(), ser.begin(), ser.end());
+  all.insert(all.end(), par.begin(), par.end());
+  all.insert(all.end(), raw.begin(), raw.end());
+  bool ok = cudaMalloc(&p->d_status, sizeof(int)) == cudaSuccess &&
+            cudaMallocHost(&p->h_status, sizeof(int)) == cudaSuccess &&
+            cudaMemset(p->d_status, 0, sizeof(int)) == cudaSuccess;
+  if (ok && n) {
+    ok = cudaMalloc(&p->d_slabs, n * sizeof(Slab)) == cudaSuccess &&
+         cudaMemcpy(p->d_slabs, all.data(), n * sizeof(Slab), cudaMemcpyHostToDevice) == cudaSuccess;
+  }
+  if (!ok) {
+    xksv_plan_destroy(p);
+    return 1;
+  }
+  *out = p;
+  return 0;
+}
+
+void xksv_plan_destroy(xksv_plan* p) {
+  if (!p) return;
+  if (p->d_slabs) cudaFree(p->d_slabs);
+  if (p->d_status) cudaFree(p->d_status);
+  if (p->h_status) cudaFreeHost(p->h_status);
+  delete p;
+}
+
+int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, void* stream) {
+  auto* p = const_cast<xksv_plan*>(pc);
+  if (!p || !d_payload || !d_out) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* pay = static_cast<const uint8_t*>(d_payload);
+  uint8_t* out = static_cast<uint8_t*>(d_out);
+  p->launches = 0;
+  cudaError_t e = cudaSuccess;
+  if (p->n_ser) {
+    e = launch_serial_decode(p->d_slabs, p->n_ser, pay, out, p->d_status, p->grid_ser, st);
+    ++p->launches;
+  }
+  if (e == cudaSuccess && p->n_par) {
+    e = launch_parallel_decode(p->d_slabs + p->n_ser, p->n_par, pay, out, p->d_status, p->grid_par, st);
+    ++p->launches;
+  }
+  if (e == cudaSuccess && p->n_raw) {
+    e = launch_raw_decode(p->d_slabs + p->n_ser + p->n_par, p->n_raw, pay, out, p->grid_raw, st);
+    ++p->launches;
+  }
+  return e == cudaSuccess ? 0 : 1;
+}
+
+int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x, float* d_y,
+                   size_t batch, void* stream) {
+  auto* p = const_cast<xksv_plan*>(pc);
+  if (!p || !d_payload || !d_x || !d_y || !batch || batch > std::numeric_limits<uint32_t>::max())
+    return 1;
+  if (p->n_raw && !p->raw_gemm_ok) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* pay = static_cast<const uint8_t*>(d_payload);
+  p->launches = 0;
+  cudaError_t e = cudaSuccess;
+  const uint32_t ld = uint32_t(batch);
+  for (size_t b0 = 0; b0 < batch && e == cudaSuccess; b0 += 8) {
+    const uint32_t nb = uint32_t(std::min<size_t>(8, batch - b0));
+    if (p->n_ser) {
+      e = launch_serial_gemm(p->d_slabs, p->n_ser, pay, d_x, d_y, ld, uint32_t(b0), nb, p->d_status,
+                             p->grid_ser, st);
+      ++p->launches;
+    }
+    if (e == cudaSuccess && p->n_par) {
+      e = launch_parallel_gemm(p->d_slabs + p->n_ser, p->n_par, pay, d_x, d_y, ld, uint32_t(b0), nb,
+                               p->d_status, p->grid_par, st);
+      ++p->launches;
+    }
+    if (e == cudaSuccess && p->n_raw) {
+      e = launch_raw_gemm(p->d_slabs + p->n_ser + p->n_par, p->n_raw, pay, d_x, d_y, ld, uint32_t(b0),
+                          nb, p->grid_raw, st);
+      ++p->launches;
+    }
+  }
+  return e == cudaSuccess ? 0 : 1;
+}
+
+int xksv_plan_status(const xksv_plan* pc, void* stream) {
+  auto* p = const_cast<xksv_plan*>(pc);
+  if (!p) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(p->h_status, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return 1;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return 1;
+  int v = *p->h_status;
+  if (cudaMemsetAsync(p->d_status, 0, sizeof(int), st) != cudaSuccess) return 1;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return 1;
+  return v == 0 ? 0 : 1;
+}
+
+int xksv_plan_launches(const xksv_plan* p) { return p ? p->launches : 0; }
+
+}  // extern "C"

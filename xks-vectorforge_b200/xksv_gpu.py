@@ -1,0 +1,124 @@
+"""ctypes binding of libxksv_cuda.so (include/xksv_cuda.h).
+
+``load()`` returns the CDLL with the argument types the reference's own
+callers declare for the five GPU entry points (python/runtime.py:40-44 and
+251-255, python/tune.py:16-19, tests/test_cuda.py:11-12, 24-25, 35-36, 48-49,
+66-67), plus the batched plan interface.  ``Plan`` wraps a plan for torch
+callers.  There is no fallback: a missing library raises.
+"""
+import ctypes
+import os
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+DEFAULT_LIB = HERE / "libxksv_cuda.so"
+
+CODEC_RAW, CODEC_TILE16, CODEC_PARALLEL32 = 0, 1, 2
+CODEC_BY_NAME = {"raw": CODEC_RAW, "bf16-huffman-tile16": CODEC_TILE16,
+                 "bf16-huffman-parallel32": CODEC_PARALLEL32}
+
+
+class Slab(ctypes.Structure):
+    _fields_ = [("src_offset", ctypes.c_uint64), ("src_size", ctypes.c_uint64),
+                ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64),
+                ("dst_offset", ctypes.c_uint64), ("x_offset", ctypes.c_uint64),
+                ("codec", ctypes.c_uint32), ("flags", ctypes.c_uint32)]
+
+
+_SIGS = {
+    "xksv_cuda_decode": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                          ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_gemv": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                        ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_gemm": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                        ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_decode_parallel": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_gemv_parallel": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                 ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_create": ([ctypes.POINTER(Slab), ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)],
+                         ctypes.c_int),
+    "xksv_plan_destroy": ([ctypes.c_void_p], None),
+    "xksv_plan_decode": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
+                         ctypes.c_int),
+    "xksv_plan_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                        ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
+}
+
+EXPORTS = tuple(_SIGS)
+_lib = None
+
+
+def library_path():
+    return Path(os.environ.get("XKSV_CUDA_LIBRARY", DEFAULT_LIB))
+
+
+def load(path=None):
+    """Loads (once) and returns the CDLL with argtypes/restype set."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else library_path()
+    if not p.exists():
+        raise FileNotFoundError(f"{p} is missing: build it with xks-vectorforge_b200/build.py")
+    lib = ctypes.CDLL(str(p))
+    for name, (args, res) in _SIGS.items():
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = res
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def slab_table(entries):
+    """entries: iterable of dicts/tuples with the xksv_slab fields."""
+    entries = list(entries)
+    arr = (Slab * max(1, len(entries)))()
+    for i, e in enumerate(entries):
+        if isinstance(e, dict):
+            arr[i] = Slab(e["src_offset"], e["src_size"], e.get("rows", 0), e.get("cols", 0),
+                          e.get("dst_offset", 0), e.get("x_offset", 0), e["codec"], 0)
+        else:
+            arr[i] = Slab(*e)
+    return arr, len(entries)
+
+
+class Plan:
+    """A device-resident plan over one payload buffer (see include/xksv_cuda.h)."""
+
+    def __init__(self, entries, lib=None):
+        self.lib = lib or load()
+        arr, n = slab_table(entries)
+        h = ctypes.c_void_p()
+        if self.lib.xksv_plan_create(arr, n, ctypes.byref(h)):
+            raise ValueError("xksv_plan_create rejected the slab table")
+        self.handle = h
+        self.n = n
+
+    def decode(self, d_payload, d_out, stream=0):
+        if self.lib.xksv_plan_decode(self.handle, d_payload, d_out, stream):
+            raise RuntimeError("xksv_plan_decode launch failed")
+
+    def gemm(self, d_payload, d_x, d_y, batch, stream=0):
+        if self.lib.xksv_plan_gemm(self.handle, d_payload, d_x, d_y, batch, stream):
+            raise RuntimeError("xksv_plan_gemm launch failed")
+
+    def status(self, stream=0):
+        """0 when no slab reported an error since the last call, else 1."""
+        return self.lib.xksv_plan_status(self.handle, stream)
+
+    def launches(self):
+        return self.lib.xksv_plan_launches(self.handle)
+
+    def close(self):
+        if self.handle:
+            self.lib.xksv_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
