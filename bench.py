@@ -1,0 +1,512 @@
+#!/usr/bin/env python3
+"""Benchmark of the .xksv slab-decode hot path on B200.
+
+Workload: a Llama-1.1B-shaped checkpoint (hidden
+2048, 22 layers, 32 q / 4 kv heads of dim 64, FFN 5632, vocab 32000, untied
+lm_head; linear weights and embeddings BF16 N(0, 0.02), norms 1.0, seeded),
+compiled with the `dfloat11-parallel` codec into the compiler's slabs (16-row,
+1 MiB slabs; raw when encoding does not shrink a slab), and decoded whole to
+BF16 on each GPU.  A step is one decode of the whole checkpoint from
+HBM-resident compressed slabs (value); `e2e` repeats it through the public C
+ABI with the compressed payload in pinned host memory, host->device copy
+inside the timed region.  Secondary (`fused_gemv`): batch-1 fused decode+GEMV
+over every linear of a Llama-3-8B-shaped model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "xks-vectorforge_b200"))
+
+METRIC = "decode GB/s (BF16 out) vs HBM roofline; fused-GEMV tok/s Llama-8B b=1"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def llama_tensors(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, tied=False):
+    """(name, rows, cols, kind) in checkpoint order; 1-D norms are 1 x hidden
+    slabs, as the compiler lays out 1-D BF16 tensors of <= 4096 elements."""
+    out = [("model.embed_tokens.weight", vocab, hidden, "w")]
+    for i in range(layers):
+        p = f"model.layers.{i}."
+        out += [(p + "self_attn.q_proj.weight", q_heads * head_dim, hidden, "w"),
+                (p + "self_attn.k_proj.weight", kv_heads * head_dim, hidden, "w"),
+                (p + "self_attn.v_proj.weight", kv_heads * head_dim, hidden, "w"),
+                (p + "self_attn.o_proj.weight", hidden, q_heads * head_dim, "w"),
+                (p + "mlp.gate_proj.weight", ffn, hidden, "w"),
+                (p + "mlp.up_proj.weight", ffn, hidden, "w"),
+                (p + "mlp.down_proj.weight", hidden, ffn, "w"),
+                (p + "input_layernorm.weight", 1, hidden, "norm"),
+                (p + "post_attention_layernorm.weight", 1, hidden, "norm")]
+    out.append(("model.norm.weight", 1, hidden, "norm"))
+    if not tied:
+        out.append(("lm_head.weight", vocab, hidden, "w"))
+    return out
+
+
+CONFIG2 = dict(hidden=2048, layers=22, q_heads=32, kv_heads=4, head_dim=64, ffn=5632, vocab=32000)
+CONFIG3 = dict(hidden=4096, layers=32, q_heads=32, kv_heads=8, head_dim=128, ffn=14336, vocab=128256)
+
+
+def host_threads(world):
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return max(1, n // max(1, world))
+
+
+def build_archive(tensors, codec, sigma, seed, device, threads, only_kinds=("w", "norm")):
+    """Generates the seeded BF16 tensors on the GPU, compiles them on the host
+    with the library's encoder, returns (payload uint8 numpy, slabs, out_bytes,
+    per-tensor info)."""
+    import numpy as np
+    import torch
+    import xksv_gpu
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    parts, slabs, info = [], [], []
+    src = dst = 0
+    for name, rows, cols, kind in tensors:
+        if kind not in only_kinds:
+            continue
+        if kind == "norm":
+            t = torch.ones(rows, cols, dtype=torch.bfloat16, device=device)
+        else:
+            t = (torch.randn(rows, cols, generator=gen, device=device) * sigma).to(torch.bfloat16)
+        h = t.view(torch.int16).cpu().numpy()
+        pay, sl = xksv_gpu.host_pack_tensor(h.ctypes.data, h.nbytes, rows, cols, codec,
+                                            threads=threads, dst_base=dst)
+        for s in sl:
+            s["src_offset"] += src
+        info.append(dict(name=name, rows=rows, cols=cols, dst=dst, first=len(slabs), n=len(sl)))
+        slabs += sl
+        parts.append(pay)
+        src += pay.nbytes
+        dst += h.nbytes
+    return np.concatenate(parts), slabs, dst, info
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+        except Exception:
+            pass
+    return HBM_FALLBACK_GBS, "fallback (no MEASURED_PEAKS.json)"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=mx or None,
+                    reasons=sorted(reasons), samples=len(sm))
+
+
+def time_steps(fn, steps, stream):
+    import torch
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    stop.record(stream)
+    stop.synchronize()
+    return start.elapsed_time(stop) / 1e3
+
+
+def cpu_reference_decode(payload, slabs, seconds, threads):
+    """Times the reference CPU codec (oracle/_ref, compiled from the reference
+    sources) -- or the oracle port when that build is absent -- over slabs of
+    the workload on `threads` host threads for about `seconds`.  Returns
+    (GB/s of BF16 out, kind, cores, sample description)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle.oracle import Oracle, Reference
+
+    try:
+        lib, kind = Reference(), "reference"
+        unpack, unpack_par, free = (lib.lib.xksv_unpack, lib.lib.xksv_unpack_parallel, lib.lib.xksv_free)
+    except OSError:
+        lib, kind = Oracle(), "port"
+        unpack, unpack_par, free = (lib.lib.oracle_unpack, lib.lib.oracle_unpack_parallel, lib.lib.oracle_free)
+    base = payload.ctypes.data
+    work = [s for s in slabs if s["codec"] != 0]
+
+    def one(s):
+        out, size = ctypes.c_void_p(), ctypes.c_size_t()
+        p = ctypes.c_void_p(base + s["src_offset"])
+        if s["codec"] == 2:
+            rc = unpack_par(p, s["src_size"], ctypes.byref(out), ctypes.byref(size))
+        else:
+            rc = unpack(p, s["src_size"], s["rows"], s["cols"], ctypes.byref(out), ctypes.byref(size))
+        if rc:
+            raise RuntimeError("CPU decode failed")
+        free(out)
+        return size.value
+
+    done = 0
+    n = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        i = 0
+        while i < len(work) and time.perf_counter() - t0 < seconds:
+            batch = work[i:i + 4 * threads]
+            done += sum(ex.map(one, batch))
+            n += len(batch)
+            i += len(batch)
+    dt = time.perf_counter() - t0
+    return done / dt / 1e9, kind, threads, f"{n} of {len(work)} coded slabs ({done / 1e9:.3f} GB BF16 out) in {dt:.1f} s"
+
+
+def run_reference(args, rank, world):
+    import numpy as np
+    import torch
+    if rank != 0:
+        return
+    dev = "cuda:0" if torch.cuda.is_available() else "cpu"
+    tensors = llama_tensors(**CONFIG2)
+    payload, slabs, out_bytes, _ = build_archive(tensors, 2, 0.02, 1, dev, host_threads(1))
+    threads = host_threads(1)
+    vals = []
+    for _ in range(max(1, args.warmup_cpu)):
+        cpu_reference_decode(payload, slabs, 2.0, threads)
+    for _ in range(args.steps):
+        v, kind, cores, sample = cpu_reference_decode(payload, slabs, args.cpu_seconds, threads)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = dict(metric=METRIC, value=round(value, 3), unit="GB/s", impl="reference", n_gpus=world,
+                steps=args.steps, warmup=args.warmup, higher_is_better=True, scaling="weak",
+                vs_baseline=None, dtype="bf16", data="synthetic",
+                config=dict(workload="configs[1]: Llama-1.1B-shaped checkpoint, dfloat11-parallel, whole-checkpoint decode",
+                            out_bytes=out_bytes),
+                cpu_baseline=dict(value=round(value, 3), unit="GB/s", cores=cores, kind=kind, sample=sample),
+                e2e=dict(value=round(value, 3), unit="GB/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def fused_gemv(args, dev, stream, threads):
+    """Batch-1 fused decode+GEMV over every linear of a Llama-3-8B-shaped
+    model (lm_head excluded, as the reference runtime does, runtime.py:258);
+    one plan per layer group so each layer's four dependent GEMV launches
+    (qkv, o, gate+up, down) run in order, all captured in one CUDA graph."""
+    import numpy as np
+    import torch
+    import xksv_gpu
+
+    cfg = CONFIG3
+    tensors = [t for t in llama_tensors(**cfg) if t[3] == "w" and ("layers." in t[0])]
+    payload, slabs, _, info = build_archive(tensors, 1, 0.02, 2, dev, threads)
+    d_payload = torch.from_numpy(payload).to(dev)
+    comp_bytes = payload.nbytes
+    # x segments: one FP32 vector per linear input; y rows per linear
+    groups = []  # per layer: [qkv], [o], [gate, up], [down]
+    xs, ys = 0, 0
+    plans = []
+    name_to = {i["name"]: i for i in info}
+    for L in range(cfg["layers"]):
+        p = f"model.layers.{L}."
+        for members in ([p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight", p + "self_attn.v_proj.weight"],
+                        [p + "self_attn.o_proj.weight"],
+                        [p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"],
+                        [p + "mlp.down_proj.weight"]):
+            cols = name_to[members[0]]["cols"]
+            entries = []
+            for m in members:
+                t = name_to[m]
+                for s in slabs[t["first"]:t["first"] + t["n"]]:
+                    e = dict(s)
+                    e["dst_offset"] = ys + (s["dst_offset"] - t["dst"]) // (2 * t["cols"])
+                    e["x_offset"] = xs
+                    entries.append(e)
+                ys += t["rows"]
+            xs += cols
+            plans.append(xksv_gpu.Plan(entries))
+    x = torch.randn(xs, generator=torch.Generator(device=dev).manual_seed(3), device=dev).to(torch.bfloat16).float()
+    y = torch.empty(ys, device=dev)
+    h = stream.cuda_stream
+
+    def forward():
+        for pl in plans:
+            pl.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 1, h)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            forward()
+    stream.synchronize()
+    bad = sum(pl.status(h) for pl in plans)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        forward()
+    launches = sum(pl.launches() for pl in plans)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+        t = time_steps(graph.replay, args.gemv_steps, stream)
+    ms = t / args.gemv_steps * 1e3
+    bad += sum(pl.status(h) for pl in plans)
+    # correctness spot check of one layer's down_proj against an FP32 matmul of
+    # the decoded weights (decode plan of the same slabs)
+    t0 = name_to["model.layers.0.mlp.down_proj.weight"]
+    dplan = xksv_gpu.Plan(slabs[t0["first"]:t0["first"] + t0["n"]])
+    wdec = torch.empty(t0["rows"] * t0["cols"] * 2 + t0["dst"], dtype=torch.uint8, device=dev)
+    dplan.decode(d_payload.data_ptr(), wdec.data_ptr(), h)
+    bad += dplan.status(h)
+    W = wdec[t0["dst"]:].view(torch.bfloat16).view(t0["rows"], t0["cols"]).float()
+    # down_proj is the 4th group of layer 0: its x and y offsets
+    xo = cfg["hidden"] + cfg["q_heads"] * cfg["head_dim"] + cfg["hidden"]
+    yo = (cfg["q_heads"] + 2 * cfg["kv_heads"]) * cfg["head_dim"] + cfg["hidden"] + 2 * cfg["ffn"]
+    ref = W @ x[xo:xo + t0["cols"]]
+    got = y[yo:yo + t0["rows"]]
+    rel = float((got - ref).norm() / ref.norm())
+    for pl in plans:
+        pl.close()
+    dplan.close()
+    del graph
+    return dict(metric="fused-GEMV tok/s Llama-8B b=1", value=round(1e3 / ms, 2), unit="tok/s",
+                ms_per_token=round(ms, 4), codec="dfloat11", compressed_bytes=comp_bytes,
+                hbm_gbs=round(comp_bytes / (ms / 1e3) / 1e9, 1), launches_per_token=launches,
+                rel_l2_layer0_down=rel, status_errors=bad,
+                note="per token: 128 dependent plan launches (qkv, o, gate+up, down per layer) in one CUDA graph; lm_head excluded as in runtime.py:258")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--warmup-cpu", type=int, default=0)
+    ap.add_argument("--gemv-steps", type=int, default=20)
+    ap.add_argument("--no-gemv", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import xksv_gpu
+
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(dev))
+    xksv_gpu.load()
+    threads = host_threads(world)
+    tensors = llama_tensors(**CONFIG2)
+    payload, slabs, out_bytes, _ = build_archive(tensors, 2, 0.02, 1, dev, threads)
+    comp_bytes = payload.nbytes
+    n_par = sum(1 for s in slabs if s["codec"] == 2)
+    n_raw = sum(1 for s in slabs if s["codec"] == 0)
+    par_comp = sum(s["src_size"] for s in slabs if s["codec"] == 2)
+    par_out = sum(s["rows"] * s["cols"] * 2 for s in slabs if s["codec"] == 2)
+
+    d_payload = torch.from_numpy(payload).to(dev)
+    d_out = torch.empty(out_bytes, dtype=torch.uint8, device=dev)
+    plan = xksv_gpu.Plan(slabs)
+    par_plan = xksv_gpu.Plan([s for s in slabs if s["codec"] == 2])
+    stream = torch.cuda.Stream(device=dev)
+    h = stream.cuda_stream
+
+    def step():
+        plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+
+    # correctness of the decoded checkpoint: every slab's bytes against the
+    # BF16 source regenerated with the same seed
+    with torch.cuda.stream(stream):
+        step()
+    assert plan.status(h) == 0, "decode reported a slab error"
+    gen = torch.Generator(device=dev).manual_seed(1)
+    checked = 0
+    for name, rows, cols, kind in tensors:
+        ref = (torch.ones(rows, cols, dtype=torch.bfloat16, device=dev) if kind == "norm" else
+               (torch.randn(rows, cols, generator=gen, device=dev) * 0.02).to(torch.bfloat16))
+        seg = d_out[checked:checked + rows * cols * 2]
+        assert torch.equal(seg, ref.view(torch.uint8).reshape(-1)), f"decode mismatch in {name}"
+        checked += rows * cols * 2
+    assert checked == out_bytes
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t = time_steps(step, args.steps, stream)
+    torch.cuda.synchronize()
+    assert plan.status(h) == 0
+    launches = plan.launches() * args.steps
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+        dist.barrier()
+    value = world * out_bytes * args.steps / t / 1e9
+
+    # dominant kernel alone (the parallel-codec decode), for the roofline
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            par_plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+    tk = time_steps(lambda: par_plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h), args.steps, stream)
+    assert par_plan.status(h) == 0
+    kdur = tk / args.steps
+    peak, peak_src = measured_peak()
+    achieved = (par_comp + par_out) / kdur / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic_parallel_decode.json"
+    if tf.exists():
+        try:
+            d = json.loads(tf.read_text())
+            traffic = int(d["dram_bytes_per_byte_algorithmic"] * (par_comp + par_out))
+        except Exception:
+            traffic = None
+
+    # end to end through the public API: pinned host payload -> device, decode,
+    # status word back
+    h_payload = torch.from_numpy(payload).pin_memory()
+
+    def e2e_step():
+        d_payload.copy_(h_payload, non_blocking=True)
+        plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+        if plan.status(h):
+            raise RuntimeError("decode error")
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+        te = time_steps(e2e_step, max(3, args.steps // 4), stream)
+    e2e_steps = max(3, args.steps // 4)
+    if world > 1:
+        tt = torch.tensor([te], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        te = float(tt.item())
+    e2e_val = world * out_bytes * e2e_steps / te / 1e9
+
+    gemv = None
+    if not args.no_gemv and rank == 0 and world == 1:
+        del d_out
+        torch.cuda.empty_cache()
+        try:
+            gemv = fused_gemv(args, dev, stream, threads)
+        except Exception as ex:  # reported, never silently replaced
+            gemv = dict(error=f"{type(ex).__name__}: {ex}")
+
+    cpu = None
+    if rank == 0 and world == 1:
+        v, kind, cores, sample = cpu_reference_decode(payload, slabs, args.cpu_seconds, host_threads(1))
+        cpu = dict(value=round(v, 3), unit="GB/s", cores=cores, kind=kind, sample=sample)
+
+    clocks = clk.summary()
+    if world > 1:
+        allc = [None] * world
+        dist.all_gather_object(allc, clocks)
+        sm = [c["sm_mhz"] for c in allc if c["sm_mhz"]]
+        clocks = dict(sm_mhz=statistics.median(sm) if sm else None,
+                      sm_max_mhz=max((c["sm_max_mhz"] or 0) for c in allc) or None,
+                      reasons=sorted(set(r for c in allc for r in c["reasons"])),
+                      samples=sum(c["samples"] for c in allc))
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=round(value, 2), unit="GB/s", n_gpus=world, steps=args.steps,
+            warmup=args.warmup, ms_per_step=round(t / args.steps * 1e3, 4), higher_is_better=True,
+            scaling="weak", vs_baseline=None, dtype="bf16",
+            data="synthetic: seeded BF16 N(0,0.02) Llama-1.1B-shaped weights, norms 1.0 (no checkpoint download)",
+            config=dict(workload="configs[1]: Llama-1.1B-shaped checkpoint (h2048, 22L, 32/4 heads, FFN 5632, vocab 32000, untied), dfloat11-parallel, whole-checkpoint decode per GPU",
+                        codec="bf16-huffman-parallel32", slabs=len(slabs), parallel_slabs=n_par,
+                        raw_slabs=n_raw, compressed_bytes=comp_bytes, out_bytes=out_bytes,
+                        l2="inputs (%.2f GB) larger than L2 (126 MB); no flush" % ((comp_bytes + out_bytes) / 1e9),
+                        parallelism=f"slab partition, {world} independent GPU(s), no collective"),
+            roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s",
+                          frac=round(achieved / peak, 4), traffic=traffic,
+                          kernel="parallel_slab_kernel<0> (decode)", peak_source=peak_src,
+                          algorithmic_bytes_per_launch=par_comp + par_out,
+                          launch_ms=round(kdur * 1e3, 4)),
+            cpu_baseline=cpu,
+            e2e=dict(value=round(e2e_val, 2), unit="GB/s", h2d_bytes_per_step=comp_bytes,
+                     d2h_bytes_per_step=4, steps=e2e_steps,
+                     path="pinned host payload -> cudaMemcpyAsync -> xksv_plan_decode -> xksv_plan_status"),
+            clocks=clocks, gpu_launches=launches, fused_gemv=gemv)
+        print(json.dumps(line), flush=True)
+    plan.close()
+    par_plan.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

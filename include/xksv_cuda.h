@@ -104,6 +104,28 @@ int xksv_plan_status(const xksv_plan* plan, void* stream);
  * enqueued (for accounting in benchmarks). */
 int xksv_plan_launches(const xksv_plan* plan);
 
+
+/* ---------------- Part 3: archive-side encoder (host CPU) --------------- */
+/* The compile step that produces slabs for the decoder; byte-identical to the
+ * reference's xksv_pack (codec XKSV_CODEC_TILE16, src/c_api.cpp:18-28) and
+ * xksv_pack_parallel (XKSV_CODEC_PARALLEL32, src/c_api.cpp:44-65): same
+ * argument checks, 0 on success and 1 on failure (the reference returns -1),
+ * output malloc'd and released with xksv_host_free. */
+int xksv_host_pack(const void* data, size_t n, size_t rows, size_t cols, int codec, void** out,
+                   size_t* out_size);
+void xksv_host_free(void* p);
+
+/* Splits a row-major BF16 [rows, cols] tensor into the compiler's slabs
+ * (whole rows, at most 16 rows and 1 MiB each: src/compile.cpp:449-479),
+ * encodes them on `threads` host threads (0 = all cores), keeps an encoding
+ * only when smaller than the raw bytes (src/compile.cpp:268-275), and returns
+ * the concatenated payload plus one xksv_slab per slab (dst_offset =
+ * dst_base + the slab's byte offset in the tensor).  Both outputs are
+ * malloc'd; release them with xksv_host_free. */
+int xksv_host_pack_tensor(const void* data, size_t nbytes, size_t rows, size_t cols, int codec,
+                          int threads, uint64_t dst_base, void** payload, size_t* payload_size,
+                          xksv_slab** table, size_t* nslabs);
+
 #ifdef __cplusplus
 }
 #endif

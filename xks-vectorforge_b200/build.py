@@ -14,7 +14,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libxksv_cuda.so"
-SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu"]
+SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu", "pack_host.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -28,7 +28,7 @@ def build(verbose=False, force=False):
     deps = srcs + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "xksv_cuda.h"]
     if LIB.exists() and not force and all(LIB.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return LIB
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-pthread",
            "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp", *map(str, srcs)]
     if verbose:
         cmd[1:1] = ["-Xptxas", "-v"]

@@ -12,7 +12,7 @@
 #include <mutex>
 #include <vector>
 
-#include "../../include/xksv_cuda.h"
+#include "xksv_cuda.h"
 #include "kernels.h"
 
 namespace xksv {

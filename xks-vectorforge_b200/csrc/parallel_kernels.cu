@@ -4,21 +4,23 @@
 // per-substream tree walk, packed->(row, col) mapping :23-24), header checks
 // cuda/parallel.cu:33-53, CPU semantics src/c_api.cpp:66-85.
 //
-// B200 design: one warp per slab and one lane per substream (the format's
-// up-to-32 independently coded substreams are exactly a warp's worth of
-// independent work), many slabs in flight per SM.  Each lane
-//   * builds its own canonical decode table in shared memory: a 2^PK-entry
-//     first-level table for codes of length <= PK plus a compact table for
-//     longer codes (lengths PK+1..PK+PNL, at most PLONG symbols);
-//   * streams its exponent bits through 16-byte loads into a 64-bit window,
-//     its sign/mantissa bytes through aligned 8-byte loads;
-//   * writes 8 decoded BF16 words (one 16-byte store, half a tile row) at a
-//     time, un-tiled on the fly, for the common slab shape (16 rows, cols a
-//     multiple of 16, 16-byte aligned output).  Other shapes take an
-//     element-wise store path.
-// A substream whose codebook does not fit the compact table (lengths > PK+PNL
-// or more than PLONG long codes, e.g. near-uniform exponents) is decoded
-// afterwards by lane 0 with a bit-serial canonical decoder.
+// B200 design: one warp per slab, one lane per substream (the format's up to
+// 32 independently coded substreams are a warp's worth of independent work);
+// many slabs in flight per SM.  Each lane
+//   * builds its own canonical decode table: a 2^PK-entry first-level table
+//     for codes of length <= PK and a compact table for lengths PK+1..PK+PNL
+//     (at most PLONG symbols).  Tables are stored transposed ([entry][lane])
+//     so a warp's 32 lookups never conflict on shared-memory banks;
+//   * streams its exponent bits through a 64-bit register window fed by
+//     16-byte loads issued one chunk ahead, refilled once per 4 codes without
+//     a data-dependent branch (codes of length <= PK need <= 28 bits);
+//   * streams its sign/mantissa bytes through 8-byte loads two words ahead;
+//   * writes 8 BF16 words (half a tile row) per 16-byte store, un-tiled on the
+//     fly, for 16-row slabs with cols % 16 == 0 and 16-byte aligned output;
+//     other shapes use an element-wise store path.
+// A substream whose codebook does not fit the compact table (a length above
+// PK+PNL or more than PLONG long codes, e.g. near-uniform exponents) is decoded
+// afterwards by lane 0 with the bit-serial canonical decoder.
 #include "kernels.h"
 #include "xksv_device.cuh"
 
@@ -31,54 +33,48 @@ constexpr int PLONG = 32;  // long symbols held per lane
 constexpr int PWARPS = 4;  // slabs (warps) per CTA
 constexpr int PMAXB = 8;   // GEMM columns per pass
 
-struct __align__(16) LaneTab {
-  uint16_t lut[1 << PK];  // exponent << 7 | length; 0 = no code of length <= PK
-  uint16_t cnt[PNL];      // number of codes of length PK+1+j
-  uint8_t lpos[PNL];      // fill cursor per long length (build time only)
-  uint8_t lsym[PLONG];    // long-code symbols in canonical (length, symbol) order
+// One warp's tables, lane-minor so that lane l always touches bank l/2.
+struct WarpTabs {
+  uint16_t lut[1 << PK][32];  // exponent << 7 | length; 0 = no code of length <= PK
+  uint16_t cnt[PNL][32];      // number of codes of length PK+1+j
+  uint8_t lpos[PNL][32];      // fill cursor per long length (build only)
+  uint8_t lsym[PLONG][32];    // long-code symbols, canonical (length, symbol) order
+  float y[16 * PMAXB];        // GEMM accumulators for the slab's rows
 };
-static_assert(sizeof(LaneTab) % 16 == 0, "LaneTab alignment");
+constexpr size_t kSmemBytes = PWARPS * sizeof(WarpTabs);
 
-struct WarpShared {
-  float y[16 * PMAXB];  // GEMM accumulators for the slab's rows
-};
-
-constexpr size_t kWarpTabBytes = sizeof(LaneTab) * 32;
-constexpr size_t kSmemBytes = PWARPS * (kWarpTabBytes + sizeof(WarpShared));
-
-// Generic (bit-serial) tables overlay a warp's 32 LaneTabs once the fast lanes
-// are done.
+// Bit-serial tables for a substream the compact tables cannot hold; they
+// overlay the warp's first-level tables once the fast lanes are done.
 struct GenericTab {
   uint16_t cnt[256];
   uint16_t off[257];
   uint8_t sorted[256];
 };
-static_assert(sizeof(GenericTab) <= kWarpTabBytes, "generic table fits");
+static_assert(sizeof(GenericTab) <= sizeof(WarpTabs::lut), "generic table fits");
 
 struct Seg {
   const uint8_t* lens;
   const uint8_t* sm;
   const uint8_t* bits;
-  uint64_t count;
+  uint32_t count;
+  uint32_t start;  // packed index of the substream's first element
   uint64_t nbits;
   uint64_t ebytes;
-  uint64_t start;  // packed index of the substream's first element
 };
 
 __device__ __forceinline__ uint32_t byte_of(const uint4& v, int b) {
-  uint32_t w = b < 4 ? v.x : b < 8 ? v.y : b < 12 ? v.z : v.w;
+  const uint32_t w = b < 4 ? v.x : b < 8 ? v.y : b < 12 ? v.z : v.w;
   return (w >> (8 * (b & 3))) & 255u;
 }
 
-// 16 bytes from any address, as little-endian words (two aligned loads and a
-// byte funnel).
+// 16 bytes from any address (two aligned loads and a byte funnel).
 __device__ __forceinline__ uint4 ld16_any(const uint8_t* p) {
-  uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
   const uint4* q = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
-  int off = int(a & 15);
-  uint4 lo = ldg16(q);
+  const int off = int(a & 15);
+  const uint4 lo = ldg16(q);
   if (off == 0) return lo;
-  uint4 hi = ldg16(q + 1);
+  const uint4 hi = ldg16(q + 1);
   uint32_t w0 = lo.x, w1 = lo.y, w2 = lo.z, w3 = lo.w, w4 = hi.x, w5 = hi.y, w6 = hi.z, w7 = hi.w;
   if (off & 8) {
     w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
@@ -86,47 +82,57 @@ __device__ __forceinline__ uint4 ld16_any(const uint8_t* p) {
   if (off & 4) {
     w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
   }
-  int bs = (off & 3) * 8;
+  const int bs = (off & 3) * 8;
   return make_uint4(__funnelshift_r(w0, w1, bs), __funnelshift_r(w1, w2, bs),
                     __funnelshift_r(w2, w3, bs), __funnelshift_r(w3, w4, bs));
 }
 
-// Builds the lane's fast tables.  Returns 0 when built, 1 when the codebook
-// needs the generic decoder, -1 when the lengths are oversubscribed.
-__device__ int build_lane_tables(const uint8_t* lens, LaneTab& T, uint32_t& F, int& maxlen) {
-  uint64_t c_lo = 0, c_hi = 0;  // 16-bit counters: lengths 1-4 | 5-8
+// Builds the lane's tables.  Returns 0 when built, 1 when the codebook needs
+// the generic decoder, -1 when the lengths are oversubscribed (the canonical
+// assignment of src/codec.cpp:11-29 fails exactly then).
+__device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uint32_t& F,
+                                 int& maxlen) {
+  uint64_t c_lo = 0, c_hi = 0;  // 16-bit counters: lengths 1-4 | 5-PK
   uint32_t nlong = 0;
   bool generic = false;
   maxlen = 0;
-  reinterpret_cast<uint4*>(T.cnt)[0] = make_uint4(0, 0, 0, 0);
-  reinterpret_cast<uint4*>(T.cnt)[1] = make_uint4(0, 0, 0, 0);
-  for (int c16 = 0; c16 < 16; ++c16) {
-    uint4 v = ld16_any(lens + 16 * c16);
-    if ((v.x | v.y | v.z | v.w) == 0) continue;
 #pragma unroll
-    for (int b = 0; b < 16; ++b) {
-      uint32_t l = byte_of(v, b);
-      if (!l) continue;
-      maxlen = max(maxlen, int(l));
-      if (l <= 4)
-        c_lo += 1ull << (16 * (l - 1));
-      else if (l <= PK)
-        c_hi += 1ull << (16 * (l - 5));
-      else if (l <= PK + PNL) {
-        T.cnt[l - PK - 1] += 1;
-        ++nlong;
-      } else
-        generic = true;
+  for (int j = 0; j < PNL; ++j) W.cnt[j][lane] = 0;
+  uint32_t nz = 0;  // chunks holding a non-zero length
+  for (int g = 0; g < 16; g += 4) {
+    uint4 vv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) vv[k] = ld16_any(lens + 16 * (g + k));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 v = vv[k];
+      if ((v.x | v.y | v.z | v.w) == 0) continue;
+      nz |= 1u << (g + k);
+#pragma unroll
+      for (int b = 0; b < 16; ++b) {
+        const uint32_t l = byte_of(v, b);
+        if (!l) continue;
+        maxlen = max(maxlen, int(l));
+        if (l <= 4)
+          c_lo += 1ull << (16 * (l - 1));
+        else if (l <= PK)
+          c_hi += 1ull << (16 * (l - 5));
+        else if (l <= PK + PNL) {
+          W.cnt[l - PK - 1][lane] += 1;
+          ++nlong;
+        } else
+          generic = true;
+      }
     }
   }
   if (generic || nlong > PLONG) return 1;
-  // first-level start index per short length; Kraft check
+  // first-level start row per short length; Kraft check
   uint64_t s_lo = 0, s_hi = 0;
   uint32_t L = 0;
 #pragma unroll
   for (int l = 1; l <= PK; ++l) {
-    uint32_t c = l <= 4 ? uint32_t(c_lo >> (16 * (l - 1))) & 0xFFFFu
-                        : uint32_t(c_hi >> (16 * (l - 5))) & 0xFFFFu;
+    const uint32_t c = l <= 4 ? uint32_t(c_lo >> (16 * (l - 1))) & 0xFFFFu
+                              : uint32_t(c_hi >> (16 * (l - 5))) & 0xFFFFu;
     if (l <= 4)
       s_lo |= uint64_t(L) << (16 * (l - 1));
     else
@@ -137,22 +143,23 @@ __device__ int build_lane_tables(const uint8_t* lens, LaneTab& T, uint32_t& F, i
   uint64_t used = L;
   uint32_t pos = 0;
   for (int l = PK + 1; l <= maxlen; ++l) {
-    uint32_t c = T.cnt[l - PK - 1];
+    const uint32_t c = W.cnt[l - PK - 1][lane];
     used = (used << 1) + c;
-    T.lpos[l - PK - 1] = uint8_t(pos);
+    W.lpos[l - PK - 1][lane] = uint8_t(pos);
     pos += c;
   }
   if (maxlen > PK && used > (1ull << maxlen)) return -1;
   F = L << 1;
-  // fill
-  for (int c16 = 0; c16 < 16; ++c16) {
-    uint4 v = ld16_any(lens + 16 * c16);
-    if ((v.x | v.y | v.z | v.w) == 0) continue;
+  // fill, re-reading only the non-zero chunks
+  while (nz) {
+    const int c16 = __ffs(nz) - 1;
+    nz &= nz - 1;
+    const uint4 v = ld16_any(lens + 16 * c16);
 #pragma unroll
     for (int b = 0; b < 16; ++b) {
-      uint32_t l = byte_of(v, b);
+      const uint32_t l = byte_of(v, b);
       if (!l) continue;
-      uint32_t s = uint32_t(c16 * 16 + b);
+      const uint32_t s = uint32_t(c16 * 16 + b);
       if (l <= PK) {
         uint32_t st;
         if (l <= 4) {
@@ -162,152 +169,162 @@ __device__ int build_lane_tables(const uint8_t* lens, LaneTab& T, uint32_t& F, i
           st = uint32_t(s_hi >> (16 * (l - 5))) & 0xFFFFu;
           s_hi += uint64_t(1u << (PK - l)) << (16 * (l - 5));
         }
-        uint32_t e = (s << 7) | l, run = 1u << (PK - l);
-        uint32_t e2 = e | (e << 16);
-        if (run == 1)
-          T.lut[st] = uint16_t(e);
-        else if (run == 2)
-          *reinterpret_cast<uint32_t*>(&T.lut[st]) = e2;
-        else if (run == 4)
-          *reinterpret_cast<uint2*>(&T.lut[st]) = make_uint2(e2, e2);
-        else
-          for (uint32_t k = 0; k < run; k += 8)
-            *reinterpret_cast<uint4*>(&T.lut[st + k]) = make_uint4(e2, e2, e2, e2);
+        const uint16_t e = uint16_t((s << 7) | l);
+        const uint32_t run = 1u << (PK - l);
+        for (uint32_t k = 0; k < run; ++k) W.lut[st + k][lane] = e;
       } else {
-        T.lsym[T.lpos[l - PK - 1]++] = uint8_t(s);
+        const int j = int(l) - PK - 1;
+        W.lsym[W.lpos[j][lane]][lane] = uint8_t(s);
+        W.lpos[j][lane] += 1;
       }
     }
   }
-  // entries past the short codes: prefixes of long codes or unused space
-  uint32_t z = L;
-  for (; z < (1u << PK) && (z & 7); ++z) T.lut[z] = 0;
-  for (; z < (1u << PK); z += 8) *reinterpret_cast<uint4*>(&T.lut[z]) = make_uint4(0, 0, 0, 0);
+  // rows past the short codes: prefixes of long codes or unused code space
+  for (uint32_t z = L; z < (1u << PK); ++z) W.lut[z][lane] = 0;
   return 0;
 }
 
-// Next table entry (exponent << 7 | length) of the lane's stream.
-__device__ __forceinline__ uint32_t next_entry(BitReader& br, const LaneTab& T, uint32_t F,
-                                               int maxlen, uint64_t& used, bool& bad) {
-  uint32_t w = br.peek32();
-  uint32_t e = T.lut[w >> (32 - PK)];
-  uint32_t len = e & 31u;
-  if (len == 0) {
-    uint32_t cf = F, idx = 0;
-    for (int l = PK + 1; l <= maxlen; ++l) {
-      uint32_t v = w >> (32 - l);
-      uint32_t c = T.cnt[l - PK - 1];
-      if (v - cf < c) {
-        e = (uint32_t(T.lsym[idx + v - cf]) << 7) | uint32_t(l);
-        break;
-      }
-      idx += c;
-      cf = (cf + c) << 1;
-    }
-    len = e & 31u;
-    if (len == 0) bad = true;
+// Entry for a code longer than PK bits: exponent << 7 | length, or 0.
+__device__ __noinline__ uint32_t long_entry(uint32_t w, const WarpTabs& W, int lane, uint32_t F,
+                                            int maxlen) {
+  uint32_t cf = F, idx = 0;
+  for (int l = PK + 1; l <= maxlen; ++l) {
+    const uint32_t v = w >> (32 - l);
+    const uint32_t c = W.cnt[l - PK - 1][lane];
+    if (v - cf < c) return (uint32_t(W.lsym[idx + v - cf][lane]) << 7) | uint32_t(l);
+    idx += c;
+    cf = (cf + c) << 1;
   }
-  br.skip(int(len));
-  br.refill();
-  used += len;
+  return 0;
+}
+
+// Next entry (exponent << 7 | length) of the lane's stream.  Needs >= PK valid
+// bits in the window; a long code refills around itself.
+__device__ __forceinline__ uint32_t dec(BitReader& br, const WarpTabs& W, int lane, uint32_t F,
+                                       int maxlen, bool& bad) {
+  uint32_t e = W.lut[br.peek32() >> (32 - PK)][lane];
+  if ((e & 31u) == 0) {
+    br.refill();
+    e = long_entry(br.peek32(), W, lane, F, maxlen);
+    bad |= (e & 31u) == 0;
+    br.skip(int(e & 31u));
+    br.refill();
+  } else {
+    br.skip(int(e & 31u));
+  }
   return e;
 }
 
-// Output of one decoded element (packed index p).
-struct DecodeOut {
-  uint16_t* out;  // slab output (row-major)
-  uint64_t rows, cols;
-  __device__ __forceinline__ void one(uint64_t p, uint32_t word) const {
-    out[untile_index(p, rows, cols)] = uint16_t(word);
-  }
+struct Out {
+  uint16_t* out;   // decode: slab output
+  const float* x;  // GEMM: X at this slab's column 0 (row stride ld)
+  float* ysm;      // GEMM: [16][PMAXB] warp accumulators
+  uint32_t rows, cols, ld, nb;
+  bool xvec;       // GEMM: nb == 1, ld == 1, 16-byte aligned x
 };
 
-struct GemmOut {
-  const float* x;  // X at this slab's column 0, row stride ld
-  float* ysm;      // [16][PMAXB] warp accumulators
-  uint64_t rows, cols;
-  uint32_t ld, nb;
-  __device__ __forceinline__ void one(uint64_t p, uint32_t word) const {
-    uint64_t o = untile_index(p, rows, cols);
-    uint64_t r = o / cols, c = o - r * cols;
-    float w = __uint_as_float(word << 16);
-    for (uint32_t b = 0; b < nb; ++b) atomicAdd(&ysm[r * PMAXB + b], w * __ldg(&x[c * ld + b]));
-  }
-};
-
-// Decodes one substream with the lane tables; `nice` = 16-row slab, cols %
-// 16 == 0, 16-byte aligned output (decode) / contiguous 16-byte aligned x
-// with nb == 1 (GEMV).
 template <int MODE>
-__device__ void decode_segment(const Seg& s, const LaneTab& T, uint32_t F, int maxlen, bool nice,
-                               const DecodeOut& dout, const GemmOut& gout, bool& bad) {
+__device__ __forceinline__ void emit_one(const Out& o, uint32_t p, uint32_t word) {
+  const uint64_t idx = untile_index(p, o.rows, o.cols);
+  if (MODE == 0) {
+    o.out[idx] = uint16_t(word);
+  } else {
+    const uint32_t r = uint32_t(idx / o.cols), c = uint32_t(idx - uint64_t(r) * o.cols);
+    const float w = __uint_as_float(word << 16);
+    for (uint32_t b = 0; b < o.nb; ++b)
+      atomicAdd(&o.ysm[r * PMAXB + b], w * __ldg(&o.x[uint64_t(c) * o.ld + b]));
+  }
+}
+
+// Decodes one substream.  `nice`: 16-row slab, cols % 16 == 0 and (decode)
+// 16-byte aligned output.
+template <int MODE>
+__device__ void decode_segment(const Seg& s, const WarpTabs& W, int lane, uint32_t F, int maxlen,
+                               bool nice, const Out& o, bool& bad) {
   BitReader br;
-  br.init(s.bits, s.ebytes, 0);
-  uint64_t used = 0, i = 0, p = s.start;
+  br.init(s.bits, s.ebytes);
+  uint32_t i = 0, p = s.start;
   if (nice) {
     for (; i < s.count && (p & 7); ++i, ++p) {
-      uint32_t e = next_entry(br, T, F, maxlen, used, bad);
-      uint32_t w = merge1(e, __ldg(s.sm + i));
-      if (MODE == 0) dout.one(p, w); else gout.one(p, w);
+      br.refill();
+      const uint32_t e = dec(br, W, lane, F, maxlen, bad);
+      emit_one<MODE>(o, p, merge1(e, __ldg(s.sm + i)));
     }
-    const uintptr_t a = reinterpret_cast<uintptr_t>(s.sm + i);
-    const uint64_t* sw = reinterpret_cast<const uint64_t*>(a & ~uintptr_t(7));
-    const int sh = int(a & 7) * 8;
-    uint64_t s_lo = (i + 8 <= s.count) ? __ldg(sw) : 0ull;
-    for (; i + 8 <= s.count && !bad; i += 8, p += 8) {
-      uint64_t s_hi = sh ? __ldg(sw + 1) : 0ull;
-      uint64_t s8 = sh ? (s_lo >> sh) | (s_hi << (64 - sh)) : s_lo;
-      ++sw;
-      s_lo = sh ? s_hi : ((i + 16 <= s.count) ? __ldg(sw) : 0ull);
+    ByteReader16 smr;
+    smr.init(s.sm + i, s.sm + s.count);
+    uint4 s16 = make_uint4(0, 0, 0, 0);
+    const uint32_t i0 = i;
+    for (; i + 8 <= s.count; i += 8, p += 8) {
+      const bool second = ((i - i0) & 8) != 0;
+      if (!second) s16 = smr.take();
+      const uint64_t s8 = second ? (uint64_t(s16.w) << 32 | s16.z) : (uint64_t(s16.y) << 32 | s16.x);
       uint32_t e[8];
+      br.refill_uniform();
 #pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = next_entry(br, T, F, maxlen, used, bad);
+      for (int k = 0; k < 4; ++k) e[k] = dec(br, W, lane, F, maxlen, bad);
+      br.refill_uniform();
+#pragma unroll
+      for (int k = 4; k < 8; ++k) e[k] = dec(br, W, lane, F, maxlen, bad);
       const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
-      uint64_t t = p >> 8, r = (p >> 4) & 15, c = t * 16 + (p & 15);
+      const uint32_t r = (p >> 4) & 15, c = (p >> 8) * 16 + (p & 15);
       if (MODE == 0) {
-        uint4 o;
-        o.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
-        o.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
-        o.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
-        o.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
-        *reinterpret_cast<uint4*>(dout.out + r * dout.cols + c) = o;
+        uint4 v;
+        v.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
+        v.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
+        v.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
+        v.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
+        *reinterpret_cast<uint4*>(o.out + size_t(r) * o.cols + c) = v;
       } else {
-        const float4* xv = reinterpret_cast<const float4*>(gout.x + c);
-        float4 x0 = __ldg(xv), x1 = __ldg(xv + 1);
-        float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        float acc = 0.f;
+        float wf[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          uint32_t sb = (k < 4 ? slo : shi) >> (8 * (k & 3));
-          uint32_t w = merge1(e[k], sb & 255u);
-          acc = fmaf(__uint_as_float(w << 16), xs[k], acc);
+          const uint32_t sb = (k < 4 ? slo : shi) >> (8 * (k & 3));
+          wf[k] = __uint_as_float(merge1(e[k], sb & 255u) << 16);
         }
-        atomicAdd(&gout.ysm[r * PMAXB], acc);
+        if (o.xvec) {
+          const float4* xv = reinterpret_cast<const float4*>(o.x + c);
+          const float4 x0 = __ldg(xv), x1 = __ldg(xv + 1);
+          float acc = wf[0] * x0.x;
+          acc = fmaf(wf[1], x0.y, acc);
+          acc = fmaf(wf[2], x0.z, acc);
+          acc = fmaf(wf[3], x0.w, acc);
+          acc = fmaf(wf[4], x1.x, acc);
+          acc = fmaf(wf[5], x1.y, acc);
+          acc = fmaf(wf[6], x1.z, acc);
+          acc = fmaf(wf[7], x1.w, acc);
+          atomicAdd(&o.ysm[r * PMAXB], acc);
+        } else {
+          for (uint32_t b = 0; b < o.nb; ++b) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc = fmaf(wf[k], __ldg(&o.x[uint64_t(c + k) * o.ld + b]), acc);
+            atomicAdd(&o.ysm[r * PMAXB + b], acc);
+          }
+        }
       }
     }
   }
-  for (; i < s.count && !bad; ++i, ++p) {
-    uint32_t e = next_entry(br, T, F, maxlen, used, bad);
-    uint32_t w = merge1(e, __ldg(s.sm + i));
-    if (MODE == 0) dout.one(p, w); else gout.one(p, w);
+  for (; i < s.count; ++i, ++p) {
+    br.refill();
+    const uint32_t e = dec(br, W, lane, F, maxlen, bad);
+    emit_one<MODE>(o, p, merge1(e, __ldg(s.sm + i)));
   }
-  if (used != s.nbits) bad = true;
+  if (br.consumed() != s.nbits) bad = true;
 }
 
 // Lane 0 decodes a substream whose codebook needs the generic decoder.
 template <int MODE>
-__device__ bool decode_segment_generic(const Seg& s, GenericTab& G, const DecodeOut& dout,
-                                       const GemmOut& gout) {
+__device__ bool decode_segment_generic(const Seg& s, GenericTab& G, const Out& o) {
   for (int l = 0; l < 256; ++l) G.cnt[l] = 0;
   int maxlen = 0;
   for (int sym = 0; sym < 256; ++sym) {
-    int l = __ldg(s.lens + sym);
+    const int l = __ldg(s.lens + sym);
     if (l) {
       G.cnt[l] += 1;
       maxlen = max(maxlen, l);
     }
   }
-  // Kraft check: open prefixes per level, clamped once they exceed 256
-  int64_t avail = 1;
+  int64_t avail = 1;  // Kraft check: open prefixes per level, clamped past 256
   for (int l = 1; l <= maxlen; ++l) {
     avail = 2 * avail - G.cnt[l];
     if (avail < 0) return false;
@@ -316,32 +333,29 @@ __device__ bool decode_segment_generic(const Seg& s, GenericTab& G, const Decode
   G.off[0] = 0;
   for (int l = 1; l <= 256; ++l) G.off[l] = uint16_t(G.off[l - 1] + G.cnt[l - 1]);
   for (int sym = 0; sym < 256; ++sym) {
-    int l = __ldg(s.lens + sym);
+    const int l = __ldg(s.lens + sym);
     if (l) G.sorted[G.off[l]++] = uint8_t(sym);
   }
   uint64_t pos = 0;
-  const uint8_t* bits = s.bits;
-  const uint64_t nbits = s.nbits;
-  for (uint64_t i = 0; i < s.count; ++i) {
+  for (uint32_t i = 0; i < s.count; ++i) {
     int len = 0;
     auto bit_at = [&](int k) -> uint32_t {
-      uint64_t q = pos + uint64_t(k);
-      return q < nbits ? (__ldg(bits + (q >> 3)) >> (7 - (q & 7))) & 1u : 0u;
+      const uint64_t q = pos + uint64_t(k);
+      return q < s.nbits ? (__ldg(s.bits + (q >> 3)) >> (7 - (q & 7))) & 1u : 0u;
     };
-    int sym = generic_decode(bit_at, G.cnt, G.sorted, maxlen, &len);
+    const int sym = generic_decode(bit_at, G.cnt, G.sorted, maxlen, &len);
     if (sym < 0) return false;
     pos += uint64_t(len);
-    if (pos > nbits) return false;
-    uint32_t w = merge1(uint32_t(sym) << 7, __ldg(s.sm + i));
-    if (MODE == 0) dout.one(s.start + i, w); else gout.one(s.start + i, w);
+    if (pos > s.nbits) return false;
+    emit_one<MODE>(o, s.start + i, merge1(uint32_t(sym) << 7, __ldg(s.sm + i)));
   }
-  return pos == nbits;
+  return pos == s.nbits;
 }
 
 __device__ __forceinline__ uint64_t warp_incl_scan(uint64_t v, int lane) {
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
-    uint64_t t = __shfl_up_sync(0xffffffffu, v, d);
+    const uint64_t t = __shfl_up_sync(0xffffffffu, v, d);
     if (lane >= d) v += t;
   }
   return v;
@@ -355,8 +369,7 @@ __global__ void __launch_bounds__(PWARPS * 32)
                          uint32_t nb, int* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  LaneTab* tabs = reinterpret_cast<LaneTab*>(smem + warp * kWarpTabBytes);
-  WarpShared* ws = reinterpret_cast<WarpShared*>(smem + PWARPS * kWarpTabBytes) + warp;
+  WarpTabs& W = reinterpret_cast<WarpTabs*>(smem)[warp];
 
   for (uint32_t si = blockIdx.x * PWARPS + warp; si < nslabs; si += gridDim.x * PWARPS) {
     const Slab sd = slabs[si];
@@ -379,77 +392,80 @@ __global__ void __launch_bounds__(PWARPS * 32)
       if (lane == 0) atomicOr(status, kStatusHeader);
       continue;
     }
+    if (rows * cols >= (1ull << 31)) {  // this implementation indexes elements in 32 bits
+      if (lane == 0) atomicOr(status, kStatusInternal);
+      continue;
+    }
     // ---- substream table (cuda/parallel.cu:39-51) ----
-    const uint64_t total = rows * cols;
+    const uint32_t total = uint32_t(rows * cols);
     const bool active = uint64_t(lane) < chunks;
-    uint64_t len = active ? ld_le64(p + 32 + 8 * lane) : 0;
+    const uint64_t len = active ? ld_le64(p + 32 + 8 * lane) : 0;
     bool lok = !active || (len >= kHdr && len <= n);
-    uint64_t incl = warp_incl_scan(lok ? len : 0, lane);
-    uint64_t base = 32 + 8 * chunks + incl - len;
+    const uint64_t incl = warp_incl_scan(lok ? len : 0, lane);
+    const uint64_t base = 32 + 8 * chunks + incl - len;
     Seg s{};
     if (active && lok) {
       lok = base + len <= n;
       if (lok) {
         const uint8_t* q = p + base;
-        s.count = ld_le64(q);
+        const uint64_t count = ld_le64(q);
         s.nbits = ld_le64(q + 8);
-        s.start = total * uint64_t(lane) / chunks;
-        uint64_t expect = total * uint64_t(lane + 1) / chunks - s.start;
+        s.start = uint32_t(uint64_t(total) * uint64_t(lane) / chunks);
+        const uint64_t expect = uint64_t(total) * uint64_t(lane + 1) / chunks - s.start;
         s.ebytes = s.nbits / 8 + (s.nbits % 8 != 0);
-        lok = s.count == expect && s.count <= len - kHdr && s.ebytes == len - kHdr - s.count;
+        lok = count == expect && count <= len - kHdr && s.ebytes == len - kHdr - count;
+        s.count = uint32_t(count);
         s.lens = q + 16;
         s.sm = q + kHdr;
-        s.bits = q + kHdr + s.count;
+        s.bits = q + kHdr + count;
       }
     }
-    uint64_t end_all = __shfl_sync(0xffffffffu, base + len, int(chunks - 1));
-    bool all_ok = __all_sync(0xffffffffu, lok) && end_all == n;
-    if (!all_ok) {
+    const uint64_t end_all = __shfl_sync(0xffffffffu, base + len, int(chunks - 1));
+    if (!(__all_sync(0xffffffffu, lok) && end_all == n)) {
       if (lane == 0) atomicOr(status, kStatusHeader);
       continue;
     }
     // ---- per-lane tables ----
-    LaneTab& T = tabs[lane];
     uint32_t F = 0;
     int maxlen = 0;
-    int tb = active ? build_lane_tables(s.lens, T, F, maxlen) : 0;
+    const int tb = active ? build_lane_tables(s.lens, W, lane, F, maxlen) : 0;
     if (__any_sync(0xffffffffu, tb < 0)) {
       if (lane == 0) atomicOr(status, kStatusCodebook);
       continue;
     }
-    uint16_t* o16 = reinterpret_cast<uint16_t*>(out + sd.dst);
-    DecodeOut dout{o16, rows, cols};
-    GemmOut gout{x + sd.xoff * ld, ws->y, rows, cols, ld, nb};
+    Out o;
+    o.out = reinterpret_cast<uint16_t*>(out + sd.dst);
+    o.x = MODE == 1 ? x + sd.xoff * ld : nullptr;
+    o.ysm = W.y;
+    o.rows = uint32_t(rows);
+    o.cols = uint32_t(cols);
+    o.ld = ld;
+    o.nb = nb;
+    o.xvec = nb == 1 && ld == 1 && (reinterpret_cast<uintptr_t>(o.x) & 15) == 0;
     if (MODE == 1) {
-      for (int k = lane; k < 16 * PMAXB; k += 32) ws->y[k] = 0.f;
+      for (int k = lane; k < 16 * PMAXB; k += 32) W.y[k] = 0.f;
       __syncwarp();
     }
-    bool nice;
-    if (MODE == 0)
-      nice = rows == 16 && (cols & 15) == 0 && ((reinterpret_cast<uintptr_t>(o16)) & 15) == 0;
-    else
-      nice = rows == 16 && (cols & 15) == 0 && nb == 1 && ld == 1 &&
-             ((reinterpret_cast<uintptr_t>(gout.x)) & 15) == 0;
+    const bool nice = rows == 16 && (cols & 15) == 0 &&
+                      (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
     bool bad = false;
-    if (active && tb == 0) decode_segment<MODE>(s, T, F, maxlen, nice, dout, gout, bad);
+    if (active && tb == 0) decode_segment<MODE>(s, W, lane, F, maxlen, nice, o, bad);
     // ---- substreams that need the generic decoder ----
     uint32_t gmask = __ballot_sync(0xffffffffu, active && tb == 1);
     __syncwarp();
     while (gmask) {
-      int g = __ffs(gmask) - 1;
+      const int g = __ffs(gmask) - 1;
       gmask &= gmask - 1;
       Seg sg;
       sg.lens = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(s.lens), g));
       sg.sm = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(s.sm), g));
       sg.bits = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(s.bits), g));
       sg.count = __shfl_sync(0xffffffffu, s.count, g);
+      sg.start = __shfl_sync(0xffffffffu, s.start, g);
       sg.nbits = __shfl_sync(0xffffffffu, s.nbits, g);
       sg.ebytes = __shfl_sync(0xffffffffu, s.ebytes, g);
-      sg.start = __shfl_sync(0xffffffffu, s.start, g);
-      if (lane == 0) {
-        bool gok = decode_segment_generic<MODE>(sg, *reinterpret_cast<GenericTab*>(tabs), dout, gout);
-        if (!gok) bad = true;
-      }
+      if (lane == 0 && !decode_segment_generic<MODE>(sg, *reinterpret_cast<GenericTab*>(&W.lut[0][0]), o))
+        bad = true;
       __syncwarp();
     }
     if (__any_sync(0xffffffffu, bad)) {
@@ -458,13 +474,23 @@ __global__ void __launch_bounds__(PWARPS * 32)
     }
     if (MODE == 1) {
       __syncwarp();
-      for (uint32_t k = lane; k < rows * nb; k += 32) {
-        uint32_t r = k / nb, b = k - r * nb;
-        y[(sd.dst + r) * ld + b] = ws->y[r * PMAXB + b];
+      for (uint32_t k = lane; k < uint32_t(rows) * nb; k += 32) {
+        const uint32_t r = k / nb, b = k - r * nb;
+        y[(sd.dst + r) * ld + b] = W.y[r * PMAXB + b];
       }
       __syncwarp();
     }
   }
+}
+
+void set_attr_once() {
+  static int done_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 31 && ((done_mask >> dev) & 1)) return;
+  cudaFuncSetAttribute(parallel_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+  cudaFuncSetAttribute(parallel_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+  if (dev < 31) done_mask |= 1 << dev;
 }
 
 }  // namespace
@@ -474,13 +500,8 @@ size_t parallel_smem_bytes() { return kSmemBytes; }
 cudaError_t launch_parallel_decode(const Slab* slabs, uint32_t n, const uint8_t* payload,
                                    uint8_t* out, int* status, int grid, cudaStream_t st) {
   if (!n) return cudaSuccess;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(parallel_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    cudaFuncSetAttribute(parallel_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    attr = true;
-  }
-  int need = int((n + PWARPS - 1) / PWARPS);
+  set_attr_once();
+  const int need = int((n + PWARPS - 1) / PWARPS);
   parallel_slab_kernel<0><<<grid < need ? grid : need, PWARPS * 32, kSmemBytes, st>>>(
       slabs, n, payload, out, nullptr, nullptr, 1, 1, status);
   return cudaGetLastError();
@@ -490,13 +511,8 @@ cudaError_t launch_parallel_gemm(const Slab* slabs, uint32_t n, const uint8_t* p
                                  const float* x, float* y, uint32_t ld, uint32_t b0, uint32_t nb,
                                  int* status, int grid, cudaStream_t st) {
   if (!n) return cudaSuccess;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(parallel_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    cudaFuncSetAttribute(parallel_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    attr = true;
-  }
-  int need = int((n + PWARPS - 1) / PWARPS);
+  set_attr_once();
+  const int need = int((n + PWARPS - 1) / PWARPS);
   parallel_slab_kernel<1><<<grid < need ? grid : need, PWARPS * 32, kSmemBytes, st>>>(
       slabs, n, payload, nullptr, x + b0, y + b0, ld, nb, status);
   return cudaGetLastError();

@@ -7,37 +7,37 @@
 // B200 design: a slab has ONE Huffman bit stream and no substream offsets, so
 // one CTA decodes it cooperatively by self-synchronising speculative decoding
 // (after Weissenberger & Schmidt, "Massively Parallel Huffman Decoding on
-// GPUs", ICPP 2018).  The stream is processed in rounds of ST*S bits held in
-// shared memory:
+// GPUs", ICPP 2018).  The stream is cut into rounds of ST*S bits (S chosen per
+// slab so rounds are balanced), each held in shared memory:
 //   1. every thread decodes its own S-bit range from the range's first bit
-//      (thread 0 from the exact round start), marking each code start in a
-//      bitmap and counting codes;
+//      (thread 0 from the exact round start) and records where its first REC
+//      codes start;
 //   2. thread t re-decodes from the true end of thread t-1's last code until it
-//      lands on a position it marked itself: from there its first pass was on
-//      the true code sequence, so its count is corrected by the marks it
-//      skipped (a popcount); repeated until no end position changes (each
-//      repetition makes at least one more thread exact, so the loop is
-//      bounded; Huffman codes resynchronise within a few codes in practice);
-//   3. a block scan of the corrected counts gives each thread's output index,
-//      and the threads decode their exact ranges again into a shared staging
-//      buffer of exponent bytes;
-//   4. the staged exponents are merged with the sign/mantissa bytes and
-//      written un-tiled with 16-byte stores (or fed to the GEMV/GEMM).
-// Decode tables: a 2^SK-entry table for codes of length <= SK, canonical
-// limits for lengths up to 32, and a bit-serial decoder beyond that (the
-// format allows lengths up to 255).
+//      lands on one of its recorded code starts: from there its first pass was
+//      on the true code sequence, so its count needs only the codes it skipped
+//      removed.  Repeated until no end position changes: each repetition makes
+//      at least one more thread exact (bounded by ST); in practice Huffman
+//      codes resynchronise within a few codes and one repetition suffices;
+//   3. a block scan of the corrected counts gives each thread its output
+//      index; each thread decodes its exact range again, merges exponents with
+//      the sign/mantissa bytes and writes 8 BF16 words (half a tile row) per
+//      16-byte store, un-tiled on the fly (or feeds the GEMV/GEMM).
+// Bits reach the threads through a 64-bit register window refilled from the
+// shared copy of the round (one shared load per three codes).  Decode tables:
+// a 2^SK-entry table for codes of length <= SK, canonical limits up to 32 bits
+// and a bit-serial decoder beyond that (the format allows lengths up to 255).
 #include "kernels.h"
 #include "xksv_device.cuh"
 
 namespace xksv {
 namespace {
 
-constexpr int SK = 11;         // first-level table bits
+constexpr int SK = 11;         // first-level table bits (3 codes fit one refill)
 constexpr int ST = 256;        // threads per CTA
-constexpr int SCAP = 16384;    // staged symbols per round (=> S = 64 * min length)
-constexpr int SMAXS = 256;     // max bits per thread per round
+constexpr int SMAXS = 1024;    // max bits per thread per round
 constexpr int PADW = 12;       // window words past the round end (255-bit code + read-ahead)
 constexpr int WINW = ST * SMAXS / 32 + PADW;
+constexpr int REC = 16;        // code starts recorded per thread in pass 1
 constexpr int SMAXB = 8;       // GEMM columns per pass
 constexpr uint32_t kDead = 0xFFFFFFFFu;
 
@@ -48,66 +48,62 @@ struct SerialShared {
   alignas(16) uint16_t cnt[256];  // codes per length
   uint16_t offs[257];    // index in sorted[] of the first code of length l
   uint8_t sorted[256];   // symbols in canonical (length, symbol) order
-  uint32_t win[WINW];    // the round's bits, big-endian words
-  uint32_t marks[ST * SMAXS / 32];
+  alignas(16) uint32_t win[WINW];  // the round's bits, big-endian words
+  union {
+    uint16_t rec[REC][ST];         // first code starts, relative to the range start
+    uint8_t hist[ST / 32][256];    // rank scratch while building tables
+  };
   uint32_t endpos[ST];   // relative end of each thread's last code (or kDead)
   uint32_t warpsum[ST / 32];
   float y[16 * SMAXB];
   int maxlen, minlen, flag;
-  uint32_t total;
-  alignas(16) uint8_t stage[SCAP + 16];
-  uint8_t hist[ST / 32][256];  // rank scratch at table build
 };
 
 __device__ __forceinline__ uint32_t win32(const SerialShared& S, uint32_t pos) {
-  uint32_t i = pos >> 5;
+  const uint32_t i = pos >> 5;
   return __funnelshift_l(S.win[i + 1], S.win[i], pos & 31);
 }
 
-// Codes longer than SK bits.  Returns (symbol << 7 | 0) with *len set, or -1.
-__device__ int slow_decode(const SerialShared& S, uint32_t w, uint32_t pos, int* len) {
-  int top = S.maxlen < 32 ? S.maxlen : 32;
+// Codes longer than SK bits at relative bit `pos` (w = the 32 bits there).
+// Returns the symbol with *len set, or -1.
+__device__ __noinline__ int slow_decode(const SerialShared& S, uint32_t w, uint32_t pos, int* len) {
+  const int top = S.maxlen < 32 ? S.maxlen : 32;
   for (int l = SK + 1; l <= top; ++l) {
     if (uint64_t(w) < S.lim[l]) {
-      uint64_t v = uint64_t(w) >> (32 - l);
+      const uint64_t v = uint64_t(w) >> (32 - l);
       *len = l;
       return S.sorted[S.offs[l] + uint32_t(v - S.firstc[l])];
     }
   }
   if (S.maxlen <= 32) return -1;
   auto bit_at = [&](int k) -> uint32_t {
-    uint32_t q = pos + uint32_t(k);
+    const uint32_t q = pos + uint32_t(k);
     return (S.win[q >> 5] >> (31 - (q & 31))) & 1u;
   };
   return generic_decode(bit_at, S.cnt, S.sorted, S.maxlen, len);
 }
 
-// Decodes the code at relative bit `pos`; returns symbol and length, or -1.
-__device__ __forceinline__ int decode_at(const SerialShared& S, uint32_t pos, int* len) {
-  uint32_t w = win32(S, pos);
-  uint32_t e = S.lut[w >> (32 - SK)];
-  if (e & 31u) {
-    *len = int(e & 31u);
-    return int(e >> 7);
+// Decodes the code at `pos` (the reader positioned there, >= SK valid bits).
+// Returns exponent << 7 in bits 7-14; advances pos and the reader.
+__device__ __forceinline__ uint32_t sdec(const SerialShared& S, SmemBitReader& br, uint32_t& pos,
+                                         bool& dead) {
+  const uint32_t e = S.lut[br.peek32() >> (32 - SK)];
+  const uint32_t len = e & 31u;
+  if (len == 0) {
+    int l = 1;
+    int sym = slow_decode(S, win32(S, pos), pos, &l);
+    if (sym < 0) {
+      dead = true;
+      sym = 0;
+      l = 1;
+    }
+    pos += uint32_t(l);
+    br.init(S.win, pos);
+    return uint32_t(sym) << 7;
   }
-  return slow_decode(S, w, pos, len);
-}
-
-__device__ __forceinline__ bool marked(const SerialShared& S, uint32_t pos) {
-  return (S.marks[pos >> 5] >> (pos & 31)) & 1u;
-}
-
-// Marks in [from, to) (both inside one thread's range).
-__device__ __forceinline__ uint32_t count_marks(const SerialShared& S, uint32_t from, uint32_t to) {
-  uint32_t n = 0;
-  uint32_t w0 = from >> 5, w1 = to >> 5;
-  for (uint32_t w = w0; w <= w1 && w < ST * SMAXS / 32; ++w) {
-    uint32_t m = S.marks[w];
-    if (w == w0) m &= ~0u << (from & 31);
-    if (w == w1) m &= (to & 31) ? (~0u >> (32 - (to & 31))) : 0u;
-    n += __popc(m);
-  }
-  return n;
+  br.skip(int(len));
+  pos += len;
+  return e;
 }
 
 // Builds canonical tables for the slab's code lengths.  Returns false for an
@@ -140,7 +136,7 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
   uint32_t v = c;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
-    uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
+    const uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
     if (lane >= d) v += u;
   }
   if (lane == 31) S.warpsum[warp] = v;
@@ -150,7 +146,7 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
   S.offs[t] = uint16_t(pre + v - c);
   if (t == ST - 1) S.offs[256] = uint16_t(pre + v);
   if (t == 0) {
-    int64_t avail = 1;
+    int64_t avail = 1;  // Kraft check: open prefixes per level, clamped past 256
     bool ok = true;
     for (int k = 1; k <= S.maxlen; ++k) {
       avail = 2 * avail - S.cnt[k];
@@ -159,7 +155,7 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
     }
     uint64_t code = 0;
     for (int k = 1; k <= 32; ++k) {
-      uint64_t ck = S.cnt[k];
+      const uint64_t ck = S.cnt[k];
       S.firstc[k] = code;
       S.lim[k] = (code + ck) << (32 - k);
       code = (code + ck) << 1;
@@ -180,12 +176,12 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
   constexpr int PER = (1 << SK) / ST;
   int len = S.minlen;
   for (int k = 0; k < PER; ++k) {
-    uint32_t e = uint32_t(t * PER + k);
-    uint64_t W = uint64_t(e) << (32 - SK);
+    const uint32_t e = uint32_t(t * PER + k);
+    const uint64_t W = uint64_t(e) << (32 - SK);
     while (len <= SK && W >= S.lim[len]) ++len;
     uint16_t val = 0;
     if (len <= SK) {
-      uint32_t code = e >> (SK - len);
+      const uint32_t code = e >> (SK - len);
       val = uint16_t((uint32_t(S.sorted[S.offs[len] + code - uint32_t(S.firstc[len])]) << 7) |
                      uint32_t(len));
     }
@@ -203,6 +199,34 @@ struct SerialArgs {
   uint32_t ld, nb;
   int* status;
 };
+
+struct SOut {
+  uint16_t* out;
+  const float* x;
+  float* ysm;
+  float* yg;
+  uint64_t rows, cols;
+  uint32_t ld, nb;
+  bool nice;
+};
+
+template <int MODE>
+__device__ __forceinline__ void semit_one(const SOut& o, uint32_t p, uint32_t word) {
+  const uint64_t idx = untile_index(p, o.rows, o.cols);
+  if (MODE == 0) {
+    o.out[idx] = uint16_t(word);
+  } else {
+    const uint64_t r = idx / o.cols, c = idx - r * o.cols;
+    const float wf = __uint_as_float(word << 16);
+    for (uint32_t b = 0; b < o.nb; ++b) {
+      const float pv = wf * __ldg(&o.x[c * o.ld + b]);
+      if (o.nice)
+        atomicAdd(&o.ysm[r * SMAXB + b], pv);
+      else
+        atomicAdd(&o.yg[r * o.ld + b], pv);
+    }
+  }
+}
 
 template <int MODE>
 __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict__ slabs,
@@ -222,10 +246,14 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
       count = ld_le64(p);
       nbits = ld_le64(p + 8);
       ok = count == rows * cols && count <= size - kHdr &&
-           nbits / 8 + (nbits % 8 != 0) == size - kHdr - count && count < (1ull << 40);
+           nbits / 8 + (nbits % 8 != 0) == size - kHdr - count;
     }
     if (!ok) {
       if (t == 0) atomicOr(a.status, kStatusHeader);
+      continue;
+    }
+    if (count >= (1ull << 31) || nbits >= (1ull << 32)) {  // 32-bit element / bit indexing
+      if (t == 0) atomicOr(a.status, kStatusInternal);
       continue;
     }
     if (!build_tables(S, p + 16)) {
@@ -236,116 +264,119 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
     const uint8_t* sm = p + kHdr;
     const uint8_t* bits = p + kHdr + count;
     const uint8_t* end = p + size;
-    uint16_t* o16 = reinterpret_cast<uint16_t*>(a.out + sd.dst);
-    const float* xs = MODE == 1 ? a.x + sd.xoff * a.ld : nullptr;
-    bool nice;
-    if (MODE == 0)
-      nice = rows == 16 && (cols & 15) == 0 && (reinterpret_cast<uintptr_t>(o16) & 15) == 0;
-    else
-      nice = rows == 16 && (cols & 15) == 0;
+    SOut o;
+    o.out = reinterpret_cast<uint16_t*>(a.out + sd.dst);
+    o.x = MODE == 1 ? a.x + sd.xoff * a.ld : nullptr;
+    o.ysm = S.y;
+    o.yg = MODE == 1 ? a.y + sd.dst * a.ld : nullptr;
+    o.rows = rows;
+    o.cols = cols;
+    o.ld = a.ld;
+    o.nb = a.nb;
+    o.nice = rows == 16 && (cols & 15) == 0 &&
+             (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
     if (MODE == 1) {
       for (int k = t; k < 16 * SMAXB; k += ST) S.y[k] = 0.f;
-      if (!nice)
+      if (!o.nice)
         for (uint64_t k = t; k < rows * a.nb; k += ST) {
-          uint64_t r = k / a.nb, b = k - r * a.nb;
-          a.y[(sd.dst + r) * a.ld + b] = 0.f;
+          const uint64_t r = k / a.nb, b = k - r * a.nb;
+          o.yg[r * a.ld + b] = 0.f;
         }
       __syncthreads();
     }
-    // bits per thread per round: at most SCAP codes start in a round
-    const uint32_t S_bits = uint32_t(min(SMAXS, 32 * max(1, (SCAP / ST) * S.minlen / 32)));
+    // balanced rounds of ST * S bits, S a multiple of 32 in [64, SMAXS]
+    const uint32_t nb32 = uint32_t(nbits);
+    const uint32_t nrounds = uint32_t((uint64_t(nb32) + ST * SMAXS - 1) / (ST * SMAXS));
+    const uint32_t per_round = nrounds ? uint32_t((uint64_t(nb32) + nrounds - 1) / nrounds) : 0;
+    const uint32_t S_bits = max(64u, ((per_round + ST - 1) / ST + 31) & ~31u);
     const uint32_t round_bits = ST * S_bits;
-    uint64_t R0 = 0, p0 = 0, base = 0;
+    uint32_t R0 = 0, p0 = 0, base = 0;
     int err = 0;
-    while (R0 < nbits) {
-      // ---- 1. window ----
+    const uint32_t cnt32 = uint32_t(count);
+    while (R0 < nb32) {
+      // ---- 1. the round's bits into shared memory (zero past the slab) ----
       const uint32_t nw = round_bits / 32 + PADW;
       for (uint32_t j = t; j < nw; j += ST) {
-        const uint8_t* q = bits + (R0 >> 3) + 4 * uint64_t(j);
+        const uint8_t* q = bits + (R0 >> 3) + 4 * j;
         uint32_t v = 0;
         if (q < end) {
-          uintptr_t qa = reinterpret_cast<uintptr_t>(q);
+          const uintptr_t qa = reinterpret_cast<uintptr_t>(q);
           const uint32_t* qw = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
-          int sh = int(qa & 3) * 8;
-          uint32_t lo = __ldg(qw);
-          uint32_t hi = (sh && reinterpret_cast<const uint8_t*>(qw + 1) < end) ? __ldg(qw + 1) : 0u;
+          const int sh = int(qa & 3) * 8;
+          const uint32_t lo = __ldg(qw);
+          const uint32_t hi =
+              (sh && reinterpret_cast<const uint8_t*>(qw + 1) < end) ? __ldg(qw + 1) : 0u;
           v = bswap32(sh ? __funnelshift_r(lo, hi, sh) : lo);
         }
         S.win[j] = v;
       }
-      const uint32_t lim_rel = uint32_t(nbits - R0 < round_bits ? nbits - R0 : round_bits);
+      const uint32_t lim_rel = min(nb32 - R0, round_bits);
       const uint32_t my_lo = uint32_t(t) * S_bits;
       const uint32_t my_hi = min(my_lo + S_bits, lim_rel);
-      for (uint32_t w = my_lo / 32; w < (my_lo + S_bits) / 32; ++w) S.marks[w] = 0;
+      const uint32_t p0rel = p0 - R0;
       __syncthreads();
       // ---- 2. speculative pass ----
-      const uint32_t p0rel = uint32_t(p0 - R0);
-      uint32_t st0 = t == 0 ? p0rel : my_lo;
+      const uint32_t st0 = t == 0 ? p0rel : my_lo;
       uint32_t e1 = st0, n1 = 0;
       bool d1 = false;
-      {
-        uint32_t pos = st0, mw = pos >> 5, m = 0;
-        while (pos < my_hi) {
-          int len;
-          int sym = decode_at(S, pos, &len);
-          if (sym < 0) {
-            d1 = true;
-            break;
+      if (st0 < my_hi) {
+        SmemBitReader br;
+        br.init(S.win, st0);
+        uint32_t pos = st0;
+        bool go = true;
+        while (go) {
+          br.refill_uniform();
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            if (go) {
+              if (n1 < REC) S.rec[n1][t] = uint16_t(pos - my_lo);
+              sdec(S, br, pos, d1);
+              ++n1;
+              go = !d1 && pos < my_hi;
+            }
           }
-          if ((pos >> 5) != mw) {
-            S.marks[mw] = m;
-            mw = pos >> 5;
-            m = 0;
-          }
-          m |= 1u << (pos & 31);
-          ++n1;
-          pos += uint32_t(len);
         }
-        if (pos > st0 || d1) S.marks[mw] |= m;
         e1 = pos;
       }
-      __syncthreads();
       // ---- 3. resynchronisation ----
       uint32_t myE = d1 ? kDead : e1, myN = n1, last_start = st0;
       bool myD = d1;
       S.endpos[t] = myE;
       for (int iter = 0; iter <= ST; ++iter) {
         __syncthreads();
-        uint32_t A = t == 0 ? p0rel : S.endpos[t - 1];
-        bool redo = t > 0 && A != last_start;
+        const uint32_t A = t == 0 ? p0rel : S.endpos[t - 1];
+        const bool redo = t > 0 && A != last_start;
         __syncthreads();
         if (redo) {
           last_start = A;
-          if (A == kDead) {
-            myD = true;
-            myE = kDead;
-            myN = 0;
-          } else if (A >= my_hi) {
-            myD = false;
+          if (A != kDead && A >= my_hi) {
+            myD = false;  // no code of the true sequence starts in this range
             myE = A;
             myN = 0;
-          } else if (A < my_lo) {
-            myD = true;
+          } else if (A == kDead || A < my_lo) {
+            myD = true;   // predecessor hit an invalid code
             myE = kDead;
             myN = 0;
           } else {
-            uint32_t pos = A, k = 0;
+            SmemBitReader br;
+            br.init(S.win, A);
+            uint32_t pos = A, k = 0, j = 0;
+            const uint32_t m = min(n1, uint32_t(REC));
             bool synced = false, dead = false;
             while (pos < my_hi) {
-              if (marked(S, pos)) {
+              const uint32_t rel = pos - my_lo;
+              while (j < m && S.rec[j][t] < rel) ++j;
+              if (j < m && S.rec[j][t] == rel) {
                 synced = true;
                 break;
               }
-              int len;
-              if (decode_at(S, pos, &len) < 0) {
-                dead = true;
-                break;
-              }
-              pos += uint32_t(len);
+              br.refill_uniform();
+              sdec(S, br, pos, dead);
+              if (dead) break;
               ++k;
             }
             if (synced) {
-              myN = k + n1 - count_marks(S, my_lo, pos);
+              myN = k + n1 - j;
               myE = d1 ? kDead : e1;
               myD = d1;
             } else {
@@ -362,87 +393,85 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
       uint32_t v = myN;
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
-        uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
+        const uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
         if (lane >= d) v += u;
       }
       if (lane == 31) S.warpsum[warp] = v;
       const int any_dead = __syncthreads_or(myD);
       uint32_t wpre = 0, tot = 0;
       for (int w = 0; w < ST / 32; ++w) {
-        uint32_t ws = S.warpsum[w];
+        const uint32_t ws = S.warpsum[w];
         if (w < warp) wpre += ws;
         tot += ws;
       }
       const uint32_t my_off = wpre + v - myN;
       const uint32_t last_end = S.endpos[ST - 1];
-      if (any_dead || base + tot > count) {
+      if (any_dead || uint64_t(base) + tot > count) {
         err = kStatusStream;
         break;
       }
-      // ---- 5. exact decode into the staging buffer ----
-      const uint32_t a0 = uint32_t(base & 7);
-      {
+      // ---- 5. exact decode straight to the output ----
+      if (myN) {
         uint32_t pos = t == 0 ? p0rel : S.endpos[t - 1];
-        uint8_t* dst = S.stage + a0 + my_off;
-        for (uint32_t k = 0; k < myN; ++k) {
-          int len;
-          int sym = decode_at(S, pos, &len);
-          dst[k] = uint8_t(sym);
-          pos += uint32_t(len);
-        }
-      }
-      __syncthreads();
-      // ---- 6. write out ----
-      const uint64_t g0 = base & ~7ull;
-      const uint64_t fin = base + tot;
-      const uint32_t ngroups = uint32_t((fin - g0 + 7) >> 3);
-      for (uint32_t g = t; g < ngroups; g += ST) {
-        const uint64_t q = g0 + 8ull * g;
-        const bool full = q >= base && q + 8 <= fin;
-        if (nice && full) {
-          uint64_t e8 = *reinterpret_cast<const uint64_t*>(S.stage + (q - g0));
-          uint64_t s8 = ld8_any(sm + q, end);
-          const uint32_t elo = uint32_t(e8), ehi = uint32_t(e8 >> 32);
-          const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
-          const uint64_t tt = q >> 8, r = (q >> 4) & 15, c = tt * 16 + (q & 15);
-          uint4 o;
-          o.x = (__byte_perm(elo, 0, 0x4140) << 7) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
-          o.y = (__byte_perm(elo, 0, 0x4342) << 7) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
-          o.z = (__byte_perm(ehi, 0, 0x4140) << 7) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
-          o.w = (__byte_perm(ehi, 0, 0x4342) << 7) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
-          if (MODE == 0) {
-            *reinterpret_cast<uint4*>(o16 + r * cols + c) = o;
-          } else {
-            uint32_t wv[4] = {o.x, o.y, o.z, o.w};
-            for (uint32_t b = 0; b < a.nb; ++b) {
-              float acc = 0.f;
+        SmemBitReader br;
+        br.init(S.win, pos);
+        bool dead = false;
+        uint32_t g = base + my_off;
+        const uint32_t gend = g + myN;
+        if (o.nice) {
+          for (; g < gend && (g & 7); ++g) {
+            br.refill_uniform();
+            const uint32_t e = sdec(S, br, pos, dead);
+            semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
+          }
+          if (g + 8 <= gend) {
+            ByteReader8 smr;
+            smr.init(sm + g, sm + cnt32);
+            for (; g + 8 <= gend; g += 8) {
+              const uint64_t s8 = smr.take();
+              uint32_t e[8];
+              br.refill_uniform();
+              e[0] = sdec(S, br, pos, dead);
+              e[1] = sdec(S, br, pos, dead);
+              e[2] = sdec(S, br, pos, dead);
+              br.refill_uniform();
+              e[3] = sdec(S, br, pos, dead);
+              e[4] = sdec(S, br, pos, dead);
+              e[5] = sdec(S, br, pos, dead);
+              br.refill_uniform();
+              e[6] = sdec(S, br, pos, dead);
+              e[7] = sdec(S, br, pos, dead);
+              const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
+              const uint32_t r = (g >> 4) & 15, c = (g >> 8) * 16 + (g & 15);
+              if (MODE == 0) {
+                uint4 w;
+                w.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
+                w.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
+                w.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
+                w.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
+                *reinterpret_cast<uint4*>(o.out + size_t(r) * cols + c) = w;
+              } else {
+                float wf[8];
 #pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                uint32_t word = (wv[k >> 1] >> (16 * (k & 1))) & 0xFFFFu;
-                acc = fmaf(__uint_as_float(word << 16), __ldg(&xs[(c + k) * a.ld + b]), acc);
-              }
-              atomicAdd(&S.y[r * SMAXB + b], acc);
-            }
-          }
-        } else {
-          const uint64_t lo = q > base ? q : base, hi = q + 8 < fin ? q + 8 : fin;
-          for (uint64_t e = lo; e < hi; ++e) {
-            uint32_t word = merge1(uint32_t(S.stage[e - g0]) << 7, __ldg(sm + e));
-            uint64_t o = untile_index(e, rows, cols);
-            if (MODE == 0) {
-              o16[o] = uint16_t(word);
-            } else {
-              uint64_t r = o / cols, c = o - r * cols;
-              float wf = __uint_as_float(word << 16);
-              for (uint32_t b = 0; b < a.nb; ++b) {
-                float pv = wf * __ldg(&xs[c * a.ld + b]);
-                if (nice)
-                  atomicAdd(&S.y[r * SMAXB + b], pv);
-                else
-                  atomicAdd(&a.y[(sd.dst + r) * a.ld + b], pv);
+                for (int q = 0; q < 8; ++q) {
+                  const uint32_t sb = (q < 4 ? slo : shi) >> (8 * (q & 3));
+                  wf[q] = __uint_as_float(merge1(e[q], sb & 255u) << 16);
+                }
+                for (uint32_t b = 0; b < o.nb; ++b) {
+                  float acc = 0.f;
+#pragma unroll
+                  for (int q = 0; q < 8; ++q)
+                    acc = fmaf(wf[q], __ldg(&o.x[uint64_t(c + q) * o.ld + b]), acc);
+                  atomicAdd(&S.y[r * SMAXB + b], acc);
+                }
               }
             }
           }
+        }
+        for (; g < gend; ++g) {
+          br.refill_uniform();
+          const uint32_t e = sdec(S, br, pos, dead);
+          semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
         }
       }
       base += tot;
@@ -450,12 +479,12 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
       R0 += round_bits;
       __syncthreads();
     }
-    if (!err && (base != count || p0 != nbits)) err = kStatusStream;
+    if (!err && (base != cnt32 || p0 != nb32)) err = kStatusStream;
     if (err) {
       if (t == 0) atomicOr(a.status, err);
-    } else if (MODE == 1 && nice) {
+    } else if (MODE == 1 && o.nice) {
       for (uint32_t k = t; k < 16 * a.nb; k += ST) {
-        uint32_t r = k / a.nb, b = k - r * a.nb;
+        const uint32_t r = k / a.nb, b = k - r * a.nb;
         a.y[(sd.dst + r) * a.ld + b] = S.y[r * SMAXB + b];
       }
     }
@@ -463,26 +492,26 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
   }
 }
 
-}  // namespace
-
-size_t serial_smem_bytes() { return sizeof(SerialShared); }
-
-static void serial_set_attr() {
+void serial_set_attr() {
   static int done_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && (done_mask >> dev) & 1) return;
+  if (dev < 31 && ((done_mask >> dev) & 1)) return;
   cudaFuncSetAttribute(serial_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   if (dev < 31) done_mask |= 1 << dev;
 }
+
+}  // namespace
+
+size_t serial_smem_bytes() { return sizeof(SerialShared); }
 
 cudaError_t launch_serial_decode(const Slab* slabs, uint32_t n, const uint8_t* payload,
                                  uint8_t* out, int* status, int grid, cudaStream_t st) {
   if (!n) return cudaSuccess;
   serial_set_attr();
   SerialArgs a{payload, out, nullptr, nullptr, 1, 1, status};
-  int g = grid < int(n) ? grid : int(n);
+  const int g = grid < int(n) ? grid : int(n);
   serial_slab_kernel<0><<<g, ST, sizeof(SerialShared), st>>>(slabs, n, a);
   return cudaGetLastError();
 }
@@ -493,7 +522,7 @@ cudaError_t launch_serial_gemm(const Slab* slabs, uint32_t n, const uint8_t* pay
   if (!n) return cudaSuccess;
   serial_set_attr();
   SerialArgs a{payload, nullptr, x + b0, y + b0, ld, nb, status};
-  int g = grid < int(n) ? grid : int(n);
+  const int g = grid < int(n) ? grid : int(n);
   serial_slab_kernel<1><<<g, ST, sizeof(SerialShared), st>>>(slabs, n, a);
   return cudaGetLastError();
 }

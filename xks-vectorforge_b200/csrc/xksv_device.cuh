@@ -46,58 +46,192 @@ __device__ __forceinline__ uint64_t ld8_any(const uint8_t* p, const uint8_t* end
 }
 
 // ------------------------------------------------------- bit reader -------
-// MSB-first bit stream read through aligned 16-byte chunks.  `buf` holds the
-// next bits left-aligned; `nb` is how many are valid (>= 32 after refill()).
-// Reads past `end` (the stream's last byte + 1) return zero bits, so a
-// corrupt stream can be decoded to its (wrong) end without leaving the buffer.
+// MSB-first bit stream in global memory, read through aligned 16-byte chunks
+// with one chunk always in flight ahead of the one being consumed.  Fetches
+// are unconditional (the address is clamped to the stream's last chunk), so a
+// fetch never stalls on a select of its own result; bits past the stream end
+// are whatever the last chunk holds, which only a corrupt stream can reach and
+// which the caller's final bit count rejects.  `buf` holds the next bits
+// left-aligned, `nb` how many are valid.
 struct BitReader {
-  const uint4* next;   // next aligned chunk to load
+  const uint4* next;   // next aligned chunk to fetch
   const uint4* last;   // last chunk holding stream bytes
-  uint4 cur;           // current chunk (byte-swapped to big-endian words)
-  int cw;              // words of `cur` not yet moved into buf
+  uint4 nxt;           // fetched, not yet consumed
+  uint4 cur;           // current chunk, big-endian words, consumed from .x
+  int cw;              // words left in cur
+  uint32_t taken;      // words moved into buf so far
+  uint32_t skip0;      // bits of the first words that precede the stream start
   uint64_t buf;
   int nb;
 
-  __device__ __forceinline__ void load_chunk() {
-    uint4 c = make_uint4(0, 0, 0, 0);
-    if (next <= last) c = ldg16(next);
+  __device__ __forceinline__ uint4 fetch() {
+    const uint4* q = next <= last ? next : last;
     ++next;
+    return ldg16(q);
+  }
+  __device__ __forceinline__ void load_chunk() {
+    const uint4 c = nxt;
+    nxt = fetch();
     cur = make_uint4(bswap32(c.x), bswap32(c.y), bswap32(c.z), bswap32(c.w));
     cw = 4;
   }
+  // Takes the next word; `cur` always holds at least one word afterwards.
   __device__ __forceinline__ uint32_t take_word() {
-    if (cw == 0) load_chunk();
-    uint32_t w = cur.x;
+    const uint32_t w = cur.x;
     cur.x = cur.y;
     cur.y = cur.z;
     cur.z = cur.w;
     --cw;
+    ++taken;
+    if (cw == 0) load_chunk();
     return w;
   }
-  // Positions the reader at bit `bit` of the stream starting at `base`.
-  __device__ __forceinline__ void init(const uint8_t* base, uint64_t nbytes, uint64_t bit) {
-    uintptr_t a = reinterpret_cast<uintptr_t>(base);
-    const uint8_t* first = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(15));
-    uint64_t skip = uint64_t(a & 15) * 8 + bit;  // bits from `first`
-    next = reinterpret_cast<const uint4*>(first) + (skip >> 7);
+  __device__ __forceinline__ void init(const uint8_t* base, uint64_t nbytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(base);
+    const uint4* first = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
+    next = first;
     last = reinterpret_cast<const uint4*>((a + (nbytes ? nbytes - 1 : 0)) & ~uintptr_t(15));
-    if (nbytes == 0) last = reinterpret_cast<const uint4*>(first) - 1;
+    const int skipb = int(a & 15) * 8;
+    taken = 0;
+    skip0 = uint32_t(skipb);
+    nxt = fetch();
     load_chunk();
-    int sw = int((skip >> 5) & 3);
-    for (int i = 0; i < sw; ++i) take_word();
+    for (int i = 0; i < (skipb >> 5); ++i) take_word();
     buf = uint64_t(take_word()) << 32;
     buf |= take_word();
-    int sb = int(skip & 31);
+    const int sb = skipb & 31;
     buf <<= sb;
     nb = 64 - sb;
-    refill();
   }
+  // Ensures nb > 32 (a branch: use where lanes rarely get here together).
   __device__ __forceinline__ void refill() {
     if (nb <= 32) {
-      uint64_t w = take_word();
-      buf |= w << (32 - nb);
+      buf |= uint64_t(take_word()) << (32 - nb);
       nb += 32;
     }
+  }
+  // Same effect without a data-dependent branch around the word move; the
+  // chunk load below it is the only per-lane branch, one in four refills.
+  __device__ __forceinline__ void refill_uniform() {
+    const bool need = nb <= 32;
+    const uint32_t w = cur.x;
+    const uint64_t add = uint64_t(w) << (need ? 32 - nb : 0);
+    buf |= need ? add : 0ull;
+    nb += need ? 32 : 0;
+    cur.x = need ? cur.y : cur.x;
+    cur.y = need ? cur.z : cur.y;
+    cur.z = need ? cur.w : cur.z;
+    cw -= need ? 1 : 0;
+    taken += need ? 1u : 0u;
+    if (cw == 0) load_chunk();
+  }
+  __device__ __forceinline__ uint32_t peek32() const { return uint32_t(buf >> 32); }
+  __device__ __forceinline__ void skip(int n) {
+    buf <<= n;
+    nb -= n;
+  }
+  // Bits consumed from the stream start.
+  __device__ __forceinline__ uint64_t consumed() const {
+    return uint64_t(taken) * 32 - uint64_t(nb) - skip0;
+  }
+};
+
+// Sequential 8-byte groups of a byte stream starting at any address, fetched
+// two aligned words ahead of use; fetch addresses are clamped to `lastw` (the
+// aligned word holding the stream's final byte).
+struct ByteReader8 {
+  const uint64_t* next;
+  const uint64_t* lastw;
+  uint64_t w0, w1, w2;
+  int sh;
+  __device__ __forceinline__ uint64_t fetch() {
+    const uint64_t* q = next <= lastw ? next : lastw;
+    ++next;
+    return __ldg(q);
+  }
+  __device__ __forceinline__ void init(const uint8_t* p, const uint8_t* end) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    next = reinterpret_cast<const uint64_t*>(a & ~uintptr_t(7));
+    lastw = reinterpret_cast<const uint64_t*>((reinterpret_cast<uintptr_t>(end) - 1) & ~uintptr_t(7));
+    sh = int(a & 7) * 8;
+    w0 = fetch();
+    w1 = fetch();
+    w2 = fetch();
+  }
+  // The next 8 bytes, little-endian.
+  __device__ __forceinline__ uint64_t take() {
+    const uint64_t v = sh ? (w0 >> sh) | (w1 << (64 - sh)) : w0;
+    w0 = w1;
+    w1 = w2;
+    w2 = fetch();
+    return v;
+  }
+};
+
+// Sequential 16-byte groups of a byte stream starting at any address.  Raw
+// aligned chunks sit in a 3-deep register ring (two loads in flight); the
+// funnel that realigns them runs only when a group is consumed, so no load is
+// waited on early.  Fetch addresses are clamped to the chunk holding the
+// stream's final byte.
+struct ByteReader16 {
+  const uint4* next;
+  const uint4* lastc;
+  uint4 r0, r1, r2;
+  int q, bs;  // word and bit offset of the stream start inside a chunk
+  __device__ __forceinline__ uint4 fetch() {
+    const uint4* p = next <= lastc ? next : lastc;
+    ++next;
+    return ldg16(p);
+  }
+  __device__ __forceinline__ void init(const uint8_t* p, const uint8_t* end) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    next = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
+    lastc = reinterpret_cast<const uint4*>((reinterpret_cast<uintptr_t>(end) - 1) & ~uintptr_t(15));
+    q = int((a >> 2) & 3);
+    bs = int(a & 3) * 8;
+    r0 = fetch();
+    r1 = fetch();
+    r2 = fetch();
+  }
+  // The next 16 bytes, little-endian words.
+  __device__ __forceinline__ uint4 take() {
+    uint32_t w0 = r0.x, w1 = r0.y, w2 = r0.z, w3 = r0.w, w4 = r1.x, w5 = r1.y, w6 = r1.z, w7 = r1.w;
+    if (q & 2) {
+      w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
+    }
+    if (q & 1) {
+      w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
+    }
+    const uint4 v = make_uint4(__funnelshift_r(w0, w1, bs), __funnelshift_r(w1, w2, bs),
+                               __funnelshift_r(w2, w3, bs), __funnelshift_r(w3, w4, bs));
+    r0 = r1;
+    r1 = r2;
+    r2 = fetch();
+    return v;
+  }
+};
+
+// MSB-first bit stream held in shared memory as big-endian 32-bit words,
+// read through a 64-bit register window (one shared load per refill).
+struct SmemBitReader {
+  const uint32_t* win;
+  uint32_t wi;  // next word to append
+  uint64_t buf;
+  int nb;
+  __device__ __forceinline__ void init(const uint32_t* w, uint32_t pos) {
+    win = w;
+    wi = pos >> 5;
+    const int sb = int(pos & 31);
+    buf = ((uint64_t(win[wi]) << 32) | win[wi + 1]) << sb;
+    nb = 64 - sb;
+    wi += 2;
+  }
+  __device__ __forceinline__ void refill_uniform() {
+    const bool need = nb <= 32;
+    const uint32_t w = win[wi];
+    buf |= need ? uint64_t(w) << (need ? 32 - nb : 0) : 0ull;
+    nb += need ? 32 : 0;
+    wi += need ? 1u : 0u;
   }
   __device__ __forceinline__ uint32_t peek32() const { return uint32_t(buf >> 32); }
   __device__ __forceinline__ void skip(int n) {

@@ -44,6 +44,15 @@ _SIGS = {
                         ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
+    "xksv_host_pack": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                        ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                        ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "xksv_host_free": ([ctypes.c_void_p], None),
+    "xksv_host_pack_tensor": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                               ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                               ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t),
+                               ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)],
+                              ctypes.c_int),
 }
 
 EXPORTS = tuple(_SIGS)
@@ -83,6 +92,42 @@ def slab_table(entries):
         else:
             arr[i] = Slab(*e)
     return arr, len(entries)
+
+
+def host_pack(raw, rows, cols, codec, lib=None):
+    """Encodes one slab on the host (xksv_host_pack); returns bytes."""
+    lib = lib or load()
+    buf = ctypes.create_string_buffer(bytes(raw), max(1, len(raw)))
+    out, size = ctypes.c_void_p(), ctypes.c_size_t()
+    if lib.xksv_host_pack(buf, len(raw), rows, cols, codec, ctypes.byref(out), ctypes.byref(size)):
+        raise ValueError("xksv_host_pack failed")
+    try:
+        return ctypes.string_at(out, size.value)
+    finally:
+        lib.xksv_host_free(out)
+
+
+def host_pack_tensor(ptr, nbytes, rows, cols, codec, threads=0, dst_base=0, lib=None):
+    """Encodes a row-major BF16 tensor at host address `ptr` into compiler
+    slabs.  Returns (payload bytes as a numpy uint8 array, list of slab dicts)."""
+    import numpy as np
+    lib = lib or load()
+    pay, psize = ctypes.c_void_p(), ctypes.c_size_t()
+    tab, ns = ctypes.c_void_p(), ctypes.c_size_t()
+    if lib.xksv_host_pack_tensor(ptr, nbytes, rows, cols, codec, threads, dst_base,
+                                 ctypes.byref(pay), ctypes.byref(psize), ctypes.byref(tab),
+                                 ctypes.byref(ns)):
+        raise ValueError("xksv_host_pack_tensor failed")
+    try:
+        payload = np.ctypeslib.as_array((ctypes.c_uint8 * max(1, psize.value)).from_address(pay.value))[:psize.value].copy()
+        arr = (Slab * max(1, ns.value)).from_address(tab.value)
+        slabs = [dict(src_offset=s.src_offset, src_size=s.src_size, rows=s.rows, cols=s.cols,
+                      dst_offset=s.dst_offset, x_offset=s.x_offset, codec=s.codec)
+                 for s in arr[:ns.value]]
+    finally:
+        lib.xksv_host_free(pay)
+        lib.xksv_host_free(tab)
+    return payload, slabs
 
 
 class Plan:
