@@ -6,19 +6,22 @@
 //
 // B200 design: one warp per slab, one lane per substream (the format's up to
 // 32 independently coded substreams are a warp's worth of independent work);
-// many slabs in flight per SM.  Each lane
-//   * builds its own canonical decode table: a 2^PK-entry first-level table
-//     for codes of length <= PK and a compact table for lengths PK+1..PK+PNL
-//     (at most PLONG symbols).  Tables are stored transposed ([entry][lane])
-//     so a warp's 32 lookups never conflict on shared-memory banks;
-//   * streams its exponent bits through a 64-bit register window fed by
-//     16-byte loads issued one chunk ahead, refilled once per 4 codes without
-//     a data-dependent branch (codes of length <= PK need <= 28 bits);
-//   * streams its sign/mantissa bytes through 8-byte loads two words ahead;
-//   * writes 8 BF16 words (half a tile row) per 16-byte store, un-tiled on the
-//     fly, for 16-row slabs with cols % 16 == 0 and 16-byte aligned output;
-//     other shapes use an element-wise store path.
-// A substream whose codebook does not fit the compact table (a length above
+// many slabs in flight per SM.  Every per-lane event in the inner loop runs at
+// a cadence shared by all lanes, so the warp never serialises on one lane:
+//   * each lane builds its own canonical tables: a 2^PK-entry first level for
+//     codes of length <= PK, a second level for lengths PK+1..PK+K2 under the
+//     first NE escape prefixes, and a compact list for lengths up to PK+PNL.
+//     Tables are lane-minor ([entry][lane]) so lookups never share a bank
+//     beyond lane pairs;
+//   * a lane's exponent bits are staged in a 4-slot shared ring by 16-byte
+//     cp.async copies issued once per 16 codes, and read through a 64-bit
+//     register window refilled from the ring once per 4 codes without a
+//     data-dependent branch;
+//   * sign/mantissa bytes arrive 16 at a time through a 3-deep register ring;
+//   * 16 decoded BF16 words (one tile row) leave as two 16-byte stores,
+//     un-tiled on the fly, for 16-row slabs with cols % 16 == 0 and 16-byte
+//     aligned output; other shapes use an element-wise store path.
+// A substream whose codebook the compact tables cannot hold (a length above
 // PK+PNL or more than PLONG long codes, e.g. near-uniform exponents) is decoded
 // afterwards by lane 0 with the bit-serial canonical decoder.
 #include "kernels.h"
@@ -28,18 +31,25 @@ namespace xksv {
 namespace {
 
 constexpr int PK = 7;      // first-level table bits
+constexpr int K2 = 5;      // second level covers lengths PK+1 .. PK+K2
+constexpr int NE = 2;      // escape prefixes with a second-level table
 constexpr int PNL = 16;    // long lengths held per lane: PK+1 .. PK+PNL
 constexpr int PLONG = 32;  // long symbols held per lane
-constexpr int PWARPS = 4;  // slabs (warps) per CTA
+constexpr int RING = 4;    // 16-byte bit-stream slots per lane
+constexpr int SMR = 4;     // 16-byte sign/mantissa slots per lane
+constexpr int PWARPS = 2;  // slabs (warps) per CTA: small CTAs free their tables sooner
 constexpr int PMAXB = 8;   // GEMM columns per pass
 
 // One warp's tables, lane-minor so that lane l always touches bank l/2.
 struct WarpTabs {
-  uint16_t lut[1 << PK][32];  // exponent << 7 | length; 0 = no code of length <= PK
-  uint16_t cnt[PNL][32];      // number of codes of length PK+1+j
-  uint8_t lpos[PNL][32];      // fill cursor per long length (build only)
-  uint8_t lsym[PLONG][32];    // long-code symbols, canonical (length, symbol) order
-  float y[16 * PMAXB];        // GEMM accumulators for the slab's rows
+  uint16_t lut[1 << PK][32];      // exponent << 7 | length; 0 = no code of length <= PK
+  uint16_t lut2[NE > 0 ? NE << K2 : 1][32];  // second level: 12-bit prefix - (L << K2)
+  uint16_t cnt[PNL][32];          // number of codes of length PK+1+j
+  uint8_t lpos[PNL][32];          // fill cursor per long length (build only)
+  uint8_t lsym[PLONG][32];        // long-code symbols, canonical (length, symbol) order
+  uint4 ring[RING][32];           // staged exponent-bit chunks (little-endian bytes)
+  uint4 smring[SMR][32];          // staged sign/mantissa chunks
+  float y[16 * PMAXB];            // GEMM accumulators for the slab's rows
 };
 constexpr size_t kSmemBytes = PWARPS * sizeof(WarpTabs);
 
@@ -91,7 +101,7 @@ __device__ __forceinline__ uint4 ld16_any(const uint8_t* p) {
 // the generic decoder, -1 when the lengths are oversubscribed (the canonical
 // assignment of src/codec.cpp:11-29 fails exactly then).
 __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uint32_t& F,
-                                 int& maxlen) {
+                                 int& maxlen, uint32_t& Lout) {
   uint64_t c_lo = 0, c_hi = 0;  // 16-bit counters: lengths 1-4 | 5-PK
   uint32_t nlong = 0;
   bool generic = false;
@@ -181,6 +191,30 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
   }
   // rows past the short codes: prefixes of long codes or unused code space
   for (uint32_t z = L; z < (1u << PK); ++z) W.lut[z][lane] = 0;
+  // second level: codes of length PK+1..PK+K2 whose (PK+K2)-bit prefixes fall
+  // in the first NE escape prefixes
+  for (int z = 0; z < (NE << K2); ++z) W.lut2[z][lane] = 0;
+  if (NE == 0) {
+    Lout = L;
+    return 0;
+  }
+  uint32_t cf = F, idx = 0;
+  const uint32_t base = L << K2;
+  for (int l = PK + 1; l <= maxlen && l <= PK + K2; ++l) {
+    const uint32_t c = W.cnt[l - PK - 1][lane];
+    for (uint32_t k = 0; k < c; ++k) {
+      const uint32_t code = cf + k;
+      const uint32_t run = 1u << (PK + K2 - l);
+      const uint32_t st = (code << (PK + K2 - l)) - base;
+      if (st + run <= uint32_t(NE << K2)) {
+        const uint16_t e = uint16_t((uint32_t(W.lsym[idx + k][lane]) << 7) | uint32_t(l));
+        for (uint32_t q = 0; q < run; ++q) W.lut2[st + q][lane] = e;
+      }
+    }
+    idx += c;
+    cf = (cf + c) << 1;
+  }
+  Lout = L;
   return 0;
 }
 
@@ -198,19 +232,160 @@ __device__ __noinline__ uint32_t long_entry(uint32_t w, const WarpTabs& W, int l
   return 0;
 }
 
-// Next entry (exponent << 7 | length) of the lane's stream.  Needs >= PK valid
-// bits in the window; a long code refills around itself.
-__device__ __forceinline__ uint32_t dec(BitReader& br, const WarpTabs& W, int lane, uint32_t F,
-                                       int maxlen, bool& bad) {
-  uint32_t e = W.lut[br.peek32() >> (32 - PK)][lane];
+// A lane's exponent bits: 16-byte chunks staged by cp.async into the lane's
+// RING slots (fw = words fetched, rw = words consumed), read through a 64-bit
+// window hi:lo holding nb valid bits (MSB first).
+struct LaneBits {
+  const uint4* src;   // next chunk to fetch
+  const uint4* last;  // last chunk holding stream bytes (fetches are clamped to it)
+  uint32_t fw, rw, rw0, skipb;
+  uint32_t hi, lo;
+  int nb;
+
+  __device__ __forceinline__ void fetch(WarpTabs& W, int lane) {
+    const uint4* q = src <= last ? src : last;
+    cp_async16(&W.ring[(fw >> 2) & (RING - 1)][lane], q);
+    ++src;
+    fw += 4;
+  }
+  __device__ __forceinline__ uint32_t word(const WarpTabs& W, int lane, uint32_t k) const {
+    return bswap32(reinterpret_cast<const uint32_t*>(&W.ring[(k >> 2) & (RING - 1)][lane])[k & 3]);
+  }
+  __device__ __forceinline__ void init(WarpTabs& W, int lane, const uint8_t* base, uint64_t nbytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(base);
+    src = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
+    last = reinterpret_cast<const uint4*>((a + (nbytes ? nbytes - 1 : 0)) & ~uintptr_t(15));
+    fw = 0;
+    for (int k = 0; k < RING; ++k) fetch(W, lane);
+    cp_async_commit();
+    cp_async_wait_all();
+    rw0 = rw = uint32_t(a & 15) >> 2;
+    skipb = uint32_t(a & 3) * 8;
+    hi = word(W, lane, rw);
+    lo = word(W, lane, rw + 1);
+    rw += 2;
+    hi = __funnelshift_l(lo, hi, skipb);
+    lo <<= skipb;
+    nb = 64 - int(skipb);
+  }
+  // Once per 16 codes (every lane at the same point): keep >= 8 unread words
+  // staged, and make sure every staged word this stretch may read has landed.
+  __device__ __forceinline__ void maintain(WarpTabs& W, int lane) {
+    int nf = 0;
+    while (fw - rw <= uint32_t(4 * RING - 4)) {
+      fetch(W, lane);
+      ++nf;
+    }
+    cp_async_commit();
+    if (nf <= 1 && fw - rw >= uint32_t(4 * RING - 4))
+      cp_async_wait_1();
+    else
+      cp_async_wait_all();
+  }
+  // Adds one word when nb <= 32, without a data-dependent branch.
+  __device__ __forceinline__ void refill_uniform(const WarpTabs& W, int lane) {
+    const bool need = nb <= 32;
+    const uint32_t t = need ? word(W, lane, rw) : 0u;
+    hi |= __funnelshift_rc(t, 0u, uint32_t(need ? nb : 0));
+    lo |= t << (need ? 32 - nb : 0);
+    nb += need ? 32 : 0;
+    rw += need ? 1u : 0u;
+  }
+  // Same, for the rare long-code path: tops the ring up first if needed.
+  __device__ __forceinline__ void refill_guarded(WarpTabs& W, int lane) {
+    if (nb <= 32) {
+      if (rw + 1 >= fw) {
+        fetch(W, lane);
+        cp_async_commit();
+      }
+      if (rw + 4 >= fw) cp_async_wait_all();
+      const uint32_t t = word(W, lane, rw);
+      hi |= __funnelshift_rc(t, 0u, uint32_t(nb));
+      lo |= t << (32 - nb);
+      nb += 32;
+      ++rw;
+    }
+  }
+  __device__ __forceinline__ void skip(uint32_t n) {
+    hi = __funnelshift_l(lo, hi, n);
+    lo <<= n;
+    nb -= int(n);
+  }
+  __device__ __forceinline__ uint64_t consumed() const {
+    return uint64_t(rw - rw0) * 32 - uint64_t(nb) - skipb;
+  }
+};
+
+// A lane's sign/mantissa bytes for 16-code groups: aligned 16-byte chunks
+// staged by cp.async two groups ahead, realigned when a group is consumed.
+struct LaneSm {
+  const uint4* src;
+  const uint4* last;
+  uint32_t g;   // chunk index of the next group's first byte
+  int q, bs;    // word / bit offset of the stream start inside a chunk
+  __device__ __forceinline__ void fetch(WarpTabs& W, int lane, uint32_t k) {
+    const uint4* p = src + k <= last ? src + k : last;
+    cp_async16(&W.smring[k & (SMR - 1)][lane], p);
+  }
+  __device__ __forceinline__ void init(WarpTabs& W, int lane, const uint8_t* p, const uint8_t* end) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    src = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
+    last = reinterpret_cast<const uint4*>((reinterpret_cast<uintptr_t>(end) - 1) & ~uintptr_t(15));
+    q = int((a >> 2) & 3);
+    bs = int(a & 3) * 8;
+    g = 0;
+    fetch(W, lane, 0);
+    fetch(W, lane, 1);
+    fetch(W, lane, 2);
+  }
+  // Called in step with LaneBits::maintain (same commit group): stages the
+  // chunk three ahead of the group about to be consumed.
+  __device__ __forceinline__ void stage(WarpTabs& W, int lane) { fetch(W, lane, g + 3); }
+  __device__ __forceinline__ uint4 take(const WarpTabs& W, int lane) {
+    const uint4 r0 = W.smring[g & (SMR - 1)][lane];
+    const uint4 r1 = W.smring[(g + 1) & (SMR - 1)][lane];
+    ++g;
+    uint32_t w0 = r0.x, w1 = r0.y, w2 = r0.z, w3 = r0.w, w4 = r1.x, w5 = r1.y, w6 = r1.z, w7 = r1.w;
+    if (q & 2) {
+      w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
+    }
+    if (q & 1) {
+      w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
+    }
+    return make_uint4(__funnelshift_r(w0, w1, bs), __funnelshift_r(w1, w2, bs),
+                      __funnelshift_r(w2, w3, bs), __funnelshift_r(w3, w4, bs));
+  }
+};
+
+struct LaneCode {
+  uint32_t F;  // first code of length PK+1
+  uint32_t L;  // first escape prefix (PK-bit units)
+  int maxlen;
+};
+
+// Next entry (exponent << 7 | length) of the lane's stream.  Needs >= PK+K2
+// valid bits in the window when the first level misses; the long-code path
+// refills around itself and restores >= 8 staged words.
+__device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
+                                       bool& bad) {
+  uint32_t e = W.lut[b.hi >> (32 - PK)][lane];
   if ((e & 31u) == 0) {
-    br.refill();
-    e = long_entry(br.peek32(), W, lane, F, maxlen);
-    bad |= (e & 31u) == 0;
-    br.skip(int(e & 31u));
-    br.refill();
+    const uint32_t i2 = (b.hi >> (32 - PK - K2)) - (lc.L << K2);
+    e = (NE > 0 && i2 < uint32_t(NE << K2)) ? W.lut2[i2][lane] : 0u;
+    if ((e & 31u) == 0) {
+      b.refill_guarded(W, lane);
+      e = long_entry(b.hi, W, lane, lc.F, lc.maxlen);
+      bad |= (e & 31u) == 0;
+    }
+    b.skip(e & 31u);
+    b.refill_guarded(W, lane);
+    if (b.fw - b.rw < 8) {
+      b.fetch(W, lane);
+      cp_async_commit();
+      cp_async_wait_all();
+    }
   } else {
-    br.skip(int(e & 31u));
+    b.skip(e & 31u);
   }
   return e;
 }
@@ -237,79 +412,82 @@ __device__ __forceinline__ void emit_one(const Out& o, uint32_t p, uint32_t word
 }
 
 // Decodes one substream.  `nice`: 16-row slab, cols % 16 == 0 and (decode)
-// 16-byte aligned output.
+// 16-byte aligned output; whole tile rows then leave as two 16-byte stores.
 template <int MODE>
-__device__ void decode_segment(const Seg& s, const WarpTabs& W, int lane, uint32_t F, int maxlen,
+__device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCode& lc,
                                bool nice, const Out& o, bool& bad) {
-  BitReader br;
-  br.init(s.bits, s.ebytes);
+  const bool rows16 = nice && (s.start & 15) == 0;
+  LaneSm smr;
+  if (rows16) smr.init(W, lane, s.sm, s.sm + s.count);
+  LaneBits b;
+  b.init(W, lane, s.bits, s.ebytes);  // its commit/wait also covers the first sm chunks
   uint32_t i = 0, p = s.start;
-  if (nice) {
-    for (; i < s.count && (p & 7); ++i, ++p) {
-      br.refill();
-      const uint32_t e = dec(br, W, lane, F, maxlen, bad);
-      emit_one<MODE>(o, p, merge1(e, __ldg(s.sm + i)));
-    }
-    ByteReader16 smr;
-    smr.init(s.sm + i, s.sm + s.count);
-    uint4 s16 = make_uint4(0, 0, 0, 0);
-    const uint32_t i0 = i;
-    for (; i + 8 <= s.count; i += 8, p += 8) {
-      const bool second = ((i - i0) & 8) != 0;
-      if (!second) s16 = smr.take();
-      const uint64_t s8 = second ? (uint64_t(s16.w) << 32 | s16.z) : (uint64_t(s16.y) << 32 | s16.x);
-      uint32_t e[8];
-      br.refill_uniform();
+  while (i < s.count) {
+    if (rows16) smr.stage(W, lane);
+    b.maintain(W, lane);
+    const uint32_t n = min(16u, s.count - i);
+    if (rows16 && n == 16) {
+      const uint4 s16 = smr.take(W, lane);
+      uint32_t e[16];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) e[k] = dec(br, W, lane, F, maxlen, bad);
-      br.refill_uniform();
+      for (int k = 0; k < 4; ++k) {
+        b.refill_uniform(W, lane);
 #pragma unroll
-      for (int k = 4; k < 8; ++k) e[k] = dec(br, W, lane, F, maxlen, bad);
-      const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
-      const uint32_t r = (p >> 4) & 15, c = (p >> 8) * 16 + (p & 15);
+        for (int j = 0; j < 4; ++j) e[4 * k + j] = dec(b, W, lane, lc, bad);
+      }
+      const uint32_t r = (p >> 4) & 15, c = (p >> 8) * 16;
       if (MODE == 0) {
-        uint4 v;
-        v.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
-        v.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
-        v.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
-        v.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
-        *reinterpret_cast<uint4*>(o.out + size_t(r) * o.cols + c) = v;
+        uint4 v0, v1;
+        v0.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.x, 0, 0x1100) & 0x807F807Fu);
+        v0.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.x, 0, 0x3322) & 0x807F807Fu);
+        v0.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.y, 0, 0x1100) & 0x807F807Fu);
+        v0.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.y, 0, 0x3322) & 0x807F807Fu);
+        v1.x = (__byte_perm(e[8], e[9], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.z, 0, 0x1100) & 0x807F807Fu);
+        v1.y = (__byte_perm(e[10], e[11], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.z, 0, 0x3322) & 0x807F807Fu);
+        v1.z = (__byte_perm(e[12], e[13], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.w, 0, 0x1100) & 0x807F807Fu);
+        v1.w = (__byte_perm(e[14], e[15], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.w, 0, 0x3322) & 0x807F807Fu);
+        uint4* dst = reinterpret_cast<uint4*>(o.out + size_t(r) * o.cols + c);
+        dst[0] = v0;
+        dst[1] = v1;
       } else {
-        float wf[8];
+        float wf[16];
+        const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t sb = (k < 4 ? slo : shi) >> (8 * (k & 3));
-          wf[k] = __uint_as_float(merge1(e[k], sb & 255u) << 16);
-        }
+        for (int k = 0; k < 16; ++k)
+          wf[k] = __uint_as_float(merge1(e[k], (sw[k >> 2] >> (8 * (k & 3))) & 255u) << 16);
         if (o.xvec) {
           const float4* xv = reinterpret_cast<const float4*>(o.x + c);
-          const float4 x0 = __ldg(xv), x1 = __ldg(xv + 1);
-          float acc = wf[0] * x0.x;
-          acc = fmaf(wf[1], x0.y, acc);
-          acc = fmaf(wf[2], x0.z, acc);
-          acc = fmaf(wf[3], x0.w, acc);
-          acc = fmaf(wf[4], x1.x, acc);
-          acc = fmaf(wf[5], x1.y, acc);
-          acc = fmaf(wf[6], x1.z, acc);
-          acc = fmaf(wf[7], x1.w, acc);
+          float acc = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 xq = __ldg(xv + q);
+            acc = fmaf(wf[4 * q], xq.x, acc);
+            acc = fmaf(wf[4 * q + 1], xq.y, acc);
+            acc = fmaf(wf[4 * q + 2], xq.z, acc);
+            acc = fmaf(wf[4 * q + 3], xq.w, acc);
+          }
           atomicAdd(&o.ysm[r * PMAXB], acc);
         } else {
-          for (uint32_t b = 0; b < o.nb; ++b) {
+          for (uint32_t bb = 0; bb < o.nb; ++bb) {
             float acc = 0.f;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) acc = fmaf(wf[k], __ldg(&o.x[uint64_t(c + k) * o.ld + b]), acc);
-            atomicAdd(&o.ysm[r * PMAXB + b], acc);
+            for (int k = 0; k < 16; ++k) acc = fmaf(wf[k], __ldg(&o.x[uint64_t(c + k) * o.ld + bb]), acc);
+            atomicAdd(&o.ysm[r * PMAXB + bb], acc);
           }
         }
       }
+    } else {
+      for (uint32_t k = 0; k < n; ++k) {
+        b.refill_uniform(W, lane);
+        const uint32_t e = dec(b, W, lane, lc, bad);
+        emit_one<MODE>(o, p + k, merge1(e, __ldg(s.sm + i + k)));
+      }
     }
+    i += n;
+    p += n;
   }
-  for (; i < s.count; ++i, ++p) {
-    br.refill();
-    const uint32_t e = dec(br, W, lane, F, maxlen, bad);
-    emit_one<MODE>(o, p, merge1(e, __ldg(s.sm + i)));
-  }
-  if (br.consumed() != s.nbits) bad = true;
+  cp_async_wait_all();
+  if (b.consumed() != s.nbits) bad = true;
 }
 
 // Lane 0 decodes a substream whose codebook needs the generic decoder.
@@ -426,9 +604,8 @@ __global__ void __launch_bounds__(PWARPS * 32)
       continue;
     }
     // ---- per-lane tables ----
-    uint32_t F = 0;
-    int maxlen = 0;
-    const int tb = active ? build_lane_tables(s.lens, W, lane, F, maxlen) : 0;
+    LaneCode lc{0, 0, 0};
+    const int tb = active ? build_lane_tables(s.lens, W, lane, lc.F, lc.maxlen, lc.L) : 0;
     if (__any_sync(0xffffffffu, tb < 0)) {
       if (lane == 0) atomicOr(status, kStatusCodebook);
       continue;
@@ -449,7 +626,7 @@ __global__ void __launch_bounds__(PWARPS * 32)
     const bool nice = rows == 16 && (cols & 15) == 0 &&
                       (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
     bool bad = false;
-    if (active && tb == 0) decode_segment<MODE>(s, W, lane, F, maxlen, nice, o, bad);
+    if (active && tb == 0) decode_segment<MODE>(s, W, lane, lc, nice, o, bad);
     // ---- substreams that need the generic decoder ----
     uint32_t gmask = __ballot_sync(0xffffffffu, active && tb == 1);
     __syncwarp();

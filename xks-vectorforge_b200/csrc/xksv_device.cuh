@@ -240,6 +240,17 @@ struct SmemBitReader {
   }
 };
 
+// ------------------------------------------------------------ cp.async -----
+// 16-byte global -> shared copies that bypass registers (and L1: .cg), with
+// per-thread commit groups.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
 // ---------------------------------------------------- BF16 assembly -------
 // Two BF16 words from two exponent bytes (e0 in bits 0-7, e1 in bits 8-15)
 // and two sign/mantissa bytes (same places), packed low word first.
