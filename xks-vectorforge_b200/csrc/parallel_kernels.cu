@@ -233,13 +233,14 @@ __device__ __noinline__ uint32_t long_entry(uint32_t w, const WarpTabs& W, int l
 }
 
 // A lane's exponent bits: 16-byte chunks staged by cp.async into the lane's
-// RING slots (fw = words fetched, rw = words consumed), read through a 64-bit
-// window hi:lo holding nb valid bits (MSB first).
+// RING slots (fw = words fetched, rw = words consumed), read through a 96-bit
+// window w0:w1:w2 holding nb valid bits (MSB first).  One refill per four
+// codes keeps nb >= 65, so four codes of up to PK+K2 bits need no check.
 struct LaneBits {
   const uint4* src;   // next chunk to fetch
   const uint4* last;  // last chunk holding stream bytes (fetches are clamped to it)
   uint32_t fw, rw, rw0, skipb;
-  uint32_t hi, lo;
+  uint32_t w0, w1, w2;
   int nb;
 
   __device__ __forceinline__ void fetch(WarpTabs& W, int lane) {
@@ -261,12 +262,14 @@ struct LaneBits {
     cp_async_wait_all();
     rw0 = rw = uint32_t(a & 15) >> 2;
     skipb = uint32_t(a & 3) * 8;
-    hi = word(W, lane, rw);
-    lo = word(W, lane, rw + 1);
-    rw += 2;
-    hi = __funnelshift_l(lo, hi, skipb);
-    lo <<= skipb;
-    nb = 64 - int(skipb);
+    w0 = word(W, lane, rw);
+    w1 = word(W, lane, rw + 1);
+    w2 = word(W, lane, rw + 2);
+    rw += 3;
+    w0 = __funnelshift_l(w1, w0, skipb);
+    w1 = __funnelshift_l(w2, w1, skipb);
+    w2 = __funnelshift_l(0u, w2, skipb);
+    nb = 96 - int(skipb);
   }
   // Once per 16 codes (every lane at the same point): keep >= 8 unread words
   // staged, and make sure every staged word this stretch may read has landed.
@@ -282,34 +285,26 @@ struct LaneBits {
     else
       cp_async_wait_all();
   }
-  // Adds one word when nb <= 32, without a data-dependent branch.
-  __device__ __forceinline__ void refill_uniform(const WarpTabs& W, int lane) {
-    const bool need = nb <= 32;
+  // Inserts the next word at bit nb when nb <= 64, without a data-dependent
+  // branch (needs nb >= 1).
+  __device__ __forceinline__ void refill(const WarpTabs& W, int lane) {
+    const bool need = nb <= 64;
     const uint32_t t = need ? word(W, lane, rw) : 0u;
-    hi |= __funnelshift_rc(t, 0u, uint32_t(need ? nb : 0));
-    lo |= t << (need ? 32 - nb : 0);
+    const bool low = nb < 32;  // lands in w0:w1, else in w1:w2
+    const uint32_t sh = uint32_t(low ? 32 - nb : 64 - nb);  // 0..32
+    const uint64_t v = uint64_t(t) << sh;
+    const uint32_t a = uint32_t(v >> 32), c = uint32_t(v);
+    w0 |= low ? a : 0u;
+    w1 |= low ? c : a;
+    w2 |= low ? 0u : c;
     nb += need ? 32 : 0;
     rw += need ? 1u : 0u;
   }
-  // Same, for the rare long-code path: tops the ring up first if needed.
-  __device__ __forceinline__ void refill_guarded(WarpTabs& W, int lane) {
-    if (nb <= 32) {
-      if (rw + 1 >= fw) {
-        fetch(W, lane);
-        cp_async_commit();
-      }
-      if (rw + 4 >= fw) cp_async_wait_all();
-      const uint32_t t = word(W, lane, rw);
-      hi |= __funnelshift_rc(t, 0u, uint32_t(nb));
-      lo |= t << (32 - nb);
-      nb += 32;
-      ++rw;
-    }
-  }
-  __device__ __forceinline__ void skip(uint32_t n) {
-    hi = __funnelshift_l(lo, hi, n);
-    lo <<= n;
-    nb -= int(n);
+  __device__ __forceinline__ void skip(uint32_t n) {  // n: low 5 bits used
+    w0 = __funnelshift_l(w1, w0, n);
+    w1 = __funnelshift_l(w2, w1, n);
+    w2 = __funnelshift_l(0u, w2, n);
+    nb -= int(n & 31u);
   }
   __device__ __forceinline__ uint64_t consumed() const {
     return uint64_t(rw - rw0) * 32 - uint64_t(nb) - skipb;
@@ -363,30 +358,37 @@ struct LaneCode {
   int maxlen;
 };
 
-// Next entry (exponent << 7 | length) of the lane's stream.  Needs >= PK+K2
-// valid bits in the window when the first level misses; the long-code path
-// refills around itself and restores >= 8 staged words.
-__device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
-                                       bool& bad) {
-  uint32_t e = W.lut[b.hi >> (32 - PK)][lane];
-  if ((e & 31u) == 0) {
-    const uint32_t i2 = (b.hi >> (32 - PK - K2)) - (lc.L << K2);
-    e = (NE > 0 && i2 < uint32_t(NE << K2)) ? W.lut2[i2][lane] : 0u;
-    if ((e & 31u) == 0) {
-      b.refill_guarded(W, lane);
-      e = long_entry(b.hi, W, lane, lc.F, lc.maxlen);
-      bad |= (e & 31u) == 0;
-    }
-    b.skip(e & 31u);
-    b.refill_guarded(W, lane);
-    if (b.fw - b.rw < 8) {
+// Codes the two table levels do not hold (longer than PK+K2 bits, or beyond
+// the covered escape prefixes): the compact list, then a top-up of the window
+// and the ring so the rest of the group still has its bits.
+__device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lane,
+                                               const LaneCode& lc, bool& bad) {
+  uint32_t e = long_entry(b.w0, W, lane, lc.F, lc.maxlen);
+  if ((e & 31u) == 0) bad = true;
+  b.skip(e);
+  if (b.nb < 65) {
+    if (b.rw + 1 >= b.fw) {
       b.fetch(W, lane);
       cp_async_commit();
-      cp_async_wait_all();
     }
-  } else {
-    b.skip(e & 31u);
+    if (b.rw + 4 >= b.fw) cp_async_wait_all();
+    b.refill(W, lane);
   }
+  return e & ~31u;
+}
+
+// Next entry (exponent << 7 | length) of the lane's stream; both table levels
+// are read for every code (no branch), so a 4-code block is one basic block.
+// Needs >= PK+K2 valid bits (>= 23 for the rare path).
+__device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
+                                       bool& bad) {
+  const uint32_t h = b.w0;
+  const uint32_t e1 = W.lut[h >> (32 - PK)][lane];
+  const uint32_t i2 = (h >> (32 - PK - K2)) - (lc.L << K2);
+  const uint32_t e2 = (NE > 0 && i2 < uint32_t(NE << K2)) ? uint32_t(W.lut2[i2][lane]) : 0u;
+  const uint32_t e = e1 ? e1 : e2;
+  if (e == 0) return rare_entry(b, W, lane, lc, bad);
+  b.skip(e);
   return e;
 }
 
@@ -431,7 +433,8 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
       uint32_t e[16];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        b.refill_uniform(W, lane);
+        b.refill(W, lane);  // nb >= 65: four codes of <= PK+K2 bits
+        if (b.nb < 65) b.refill(W, lane);  // a block consumed more than a word
 #pragma unroll
         for (int j = 0; j < 4; ++j) e[4 * k + j] = dec(b, W, lane, lc, bad);
       }
@@ -478,7 +481,8 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
       }
     } else {
       for (uint32_t k = 0; k < n; ++k) {
-        b.refill_uniform(W, lane);
+        b.refill(W, lane);
+        if (b.nb < 65) b.refill(W, lane);
         const uint32_t e = dec(b, W, lane, lc, bad);
         emit_one<MODE>(o, p + k, merge1(e, __ldg(s.sm + i + k)));
       }
