@@ -362,7 +362,7 @@ struct LaneCode {
 // the covered escape prefixes): the compact list, then a top-up of the window
 // and the ring so the rest of the group still has its bits.
 __device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lane,
-                                               const LaneCode& lc, bool& bad) {
+                                            const LaneCode& lc, bool& bad) {
   uint32_t e = long_entry(b.w0, W, lane, lc.F, lc.maxlen);
   if ((e & 31u) == 0) bad = true;
   b.skip(e);
@@ -374,22 +374,55 @@ __device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lan
     if (b.rw + 4 >= b.fw) cp_async_wait_all();
     b.refill(W, lane);
   }
-  return e & ~31u;
+  return e;
 }
 
-// Next entry (exponent << 7 | length) of the lane's stream; both table levels
-// are read for every code (no branch), so a 4-code block is one basic block.
-// Needs >= PK+K2 valid bits (>= 23 for the rare path).
-__device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
-                                       bool& bad) {
+// Table lookup of the code at the window head: exponent << 7 | length, or 0
+// when neither level holds it.  No branch.
+__device__ __forceinline__ uint32_t lookup(const LaneBits& b, const WarpTabs& W, int lane,
+                                          uint32_t L5) {
   const uint32_t h = b.w0;
   const uint32_t e1 = W.lut[h >> (32 - PK)][lane];
-  const uint32_t i2 = (h >> (32 - PK - K2)) - (lc.L << K2);
+  const uint32_t i2 = (h >> (32 - PK - K2)) - L5;
   const uint32_t e2 = (NE > 0 && i2 < uint32_t(NE << K2)) ? uint32_t(W.lut2[i2][lane]) : 0u;
-  const uint32_t e = e1 ? e1 : e2;
+  return e1 ? e1 : e2;
+}
+
+// One code with the rare path (used to redo a block that met a rare code).
+__device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
+                                       bool& bad) {
+  const uint32_t e = lookup(b, W, lane, lc.L << K2);
   if (e == 0) return rare_entry(b, W, lane, lc, bad);
   b.skip(e);
   return e;
+}
+
+// Four codes from a window holding >= 4*(PK+K2) bits, branch-free; a block
+// that meets a code neither level holds is rewound and redone code by code.
+__device__ __forceinline__ void dec4(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
+                                     bool& bad, uint32_t& e0, uint32_t& e1, uint32_t& e2,
+                                     uint32_t& e3) {
+  const uint32_t s0 = b.w0, s1 = b.w1, s2 = b.w2;
+  const int snb = b.nb;
+  const uint32_t L5 = lc.L << K2;
+  e0 = lookup(b, W, lane, L5);
+  b.skip(e0);
+  e1 = lookup(b, W, lane, L5);
+  b.skip(e1);
+  e2 = lookup(b, W, lane, L5);
+  b.skip(e2);
+  e3 = lookup(b, W, lane, L5);
+  b.skip(e3);
+  if ((e0 == 0) | (e1 == 0) | (e2 == 0) | (e3 == 0)) {
+    b.w0 = s0;
+    b.w1 = s1;
+    b.w2 = s2;
+    b.nb = snb;
+    e0 = dec(b, W, lane, lc, bad);
+    e1 = dec(b, W, lane, lc, bad);
+    e2 = dec(b, W, lane, lc, bad);
+    e3 = dec(b, W, lane, lc, bad);
+  }
 }
 
 struct Out {
@@ -435,8 +468,7 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
       for (int k = 0; k < 4; ++k) {
         b.refill(W, lane);  // nb >= 65: four codes of <= PK+K2 bits
         if (b.nb < 65) b.refill(W, lane);  // a block consumed more than a word
-#pragma unroll
-        for (int j = 0; j < 4; ++j) e[4 * k + j] = dec(b, W, lane, lc, bad);
+        dec4(b, W, lane, lc, bad, e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]);
       }
       const uint32_t r = (p >> 4) & 15, c = (p >> 8) * 16;
       if (MODE == 0) {
