@@ -126,6 +126,25 @@ int xksv_host_pack_tensor(const void* data, size_t nbytes, size_t rows, size_t c
                           int threads, uint64_t dst_base, void** payload, size_t* payload_size,
                           xksv_slab** table, size_t* nslabs);
 
+/* ---------------- Part 4: decode without device allocation -------------- */
+/* No counterpart in the reference.  For callers that cannot let a library
+ * allocate device memory -- a server that has reserved the whole GPU for its
+ * own allocator, or code that cannot afford cudaMalloc's implicit
+ * device-wide synchronisation.  Decodes the n slabs of `slabs` (host array,
+ * same fields as for xksv_plan_create) from d_payload into d_out (both device
+ * buffers owned by the caller) on `stream`, then waits for the stream and
+ * returns 0 on success, 1 on a bad table entry, a launch error or a slab that
+ * fails to decode, and 2 when n exceeds XKSV_NOALLOC_MAX_SLABS.
+ * Besides the caller's buffers it uses only a fixed scratch array compiled
+ * into the library (the slab table and a status word, about 192 KiB on every
+ * GPU that loads the library, kept until the process exits).  The first call
+ * on a device looks that array up (cudaGetSymbolAddress): make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * race, so issue them one at a time. */
+#define XKSV_NOALLOC_MAX_SLABS 4096
+int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload,
+                             void* d_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,7 +14,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libxksv_cuda.so"
-SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu", "pack_host.cpp"]
+SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu", "pack_host.cpp", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

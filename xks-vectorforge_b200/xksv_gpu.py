@@ -53,7 +53,11 @@ _SIGS = {
                                ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t),
                                ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)],
                               ctypes.c_int),
+    "xksv_cuda_decode_noalloc": ([ctypes.POINTER(Slab), ctypes.c_size_t, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
+
+NOALLOC_MAX_SLABS = 4096
 
 EXPORTS = tuple(_SIGS)
 _lib = None
