@@ -291,7 +291,7 @@ struct LaneBits {
     const bool need = nb <= 64;
     const uint32_t t = need ? word(W, lane, rw) : 0u;
     const bool low = nb < 32;  // lands in w0:w1, else in w1:w2
-    const uint32_t sh = uint32_t(low ? 32 - nb : 64 - nb);  // 0..32
+    const uint32_t sh = need ? uint32_t(low ? 32 - nb : 64 - nb) : 0u;  // 0..32
     const uint64_t v = uint64_t(t) << sh;
     const uint32_t a = uint32_t(v >> 32), c = uint32_t(v);
     w0 |= low ? a : 0u;

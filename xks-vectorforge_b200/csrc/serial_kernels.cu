@@ -9,51 +9,58 @@
 // (after Weissenberger & Schmidt, "Massively Parallel Huffman Decoding on
 // GPUs", ICPP 2018).  The stream is cut into rounds of ST*S bits (S chosen per
 // slab so rounds are balanced), each held in shared memory:
-//   1. every thread decodes its own S-bit range from the range's first bit
-//      (thread 0 from the exact round start) and records where its first REC
-//      codes start;
-//   2. thread t re-decodes from the true end of thread t-1's last code until it
-//      lands on one of its recorded code starts: from there its first pass was
-//      on the true code sequence, so its count needs only the codes it skipped
-//      removed.  Repeated until no end position changes: each repetition makes
-//      at least one more thread exact (bounded by ST); in practice Huffman
-//      codes resynchronise within a few codes and one repetition suffices;
-//   3. a block scan of the corrected counts gives each thread its output
-//      index; each thread decodes its exact range again, merges exponents with
-//      the sign/mantissa bytes and writes 8 BF16 words (half a tile row) per
-//      16-byte store, un-tiled on the fly (or feeds the GEMV/GEMM).
-// Bits reach the threads through a 64-bit register window refilled from the
-// shared copy of the round (one shared load per three codes).  Decode tables:
-// a 2^SK-entry table for codes of length <= SK, canonical limits up to 32 bits
-// and a bit-serial decoder beyond that (the format allows lengths up to 255).
+//   1. count pass: every thread walks its own S-bit range from the range's
+//      first bit (thread 0 from the exact round start) with a count table that
+//      consumes every whole code inside the next CK bits at once, and records
+//      where its first REC lookups start and how many codes preceded each;
+//   2. thread t re-decodes code by code from the true end of thread t-1's walk
+//      until it lands on one of its recorded lookup starts: from there its walk
+//      followed the true code sequence, so its count only loses the codes
+//      before that point.  Repeated until no end position changes: each
+//      repetition makes at least one more thread exact (bounded by ST); in
+//      practice codes resynchronise within a few codes and one suffices;
+//   3. a block scan of the counts gives every thread its output index; each
+//      thread decodes its exact range code by code (four codes per branch-free
+//      block), merges exponents with the sign/mantissa bytes and writes 8 BF16
+//      words (half a tile row) per 16-byte store, un-tiled on the fly (or feeds
+//      the GEMV/GEMM).
+// Bits reach the threads through a 96-bit register window over the round's
+// shared copy, refilled once per four codes.  Tables: 2^SK-entry single-code
+// table, 2^CK-entry count table, canonical limits up to 32 bits and a
+// bit-serial decoder beyond (the format allows lengths up to 255).
 #include "kernels.h"
 #include "xksv_device.cuh"
 
 namespace xksv {
 namespace {
 
-constexpr int SK = 11;         // first-level table bits (3 codes fit one refill)
+constexpr int SK = 11;         // single-code table bits
+constexpr int CK = 10;         // count table bits
 constexpr int ST = 256;        // threads per CTA
 constexpr int SMAXS = 1024;    // max bits per thread per round
-constexpr int PADW = 12;       // window words past the round end (255-bit code + read-ahead)
+constexpr int PADW = 16;       // window words past the round end (255-bit code + window)
 constexpr int WINW = ST * SMAXS / 32 + PADW;
-constexpr int REC = 16;        // code starts recorded per thread in pass 1
+constexpr int REC = 16;        // lookup starts recorded per thread in the count pass
 constexpr int SMAXB = 8;       // GEMM columns per pass
 constexpr uint32_t kDead = 0xFFFFFFFFu;
 
 struct SerialShared {
-  uint16_t lut[1 << SK];
-  uint64_t lim[33];      // left-aligned limit of codes with length <= l (l <= 32)
-  uint64_t firstc[33];   // canonical first code of length l (l <= 32)
+  uint16_t lut[1 << SK];  // exponent << 7 | length for codes <= SK bits; 0 = none
+  uint8_t clut[1 << CK];  // n << 4 | total length of the n whole codes in CK bits; 0 = none
+  uint64_t lim[33];       // left-aligned limit of codes with length <= l (l <= 32)
+  uint64_t firstc[33];    // canonical first code of length l (l <= 32)
   alignas(16) uint16_t cnt[256];  // codes per length
-  uint16_t offs[257];    // index in sorted[] of the first code of length l
-  uint8_t sorted[256];   // symbols in canonical (length, symbol) order
+  uint16_t offs[257];     // index in sorted[] of the first code of length l
+  uint8_t sorted[256];    // symbols in canonical (length, symbol) order
   alignas(16) uint32_t win[WINW];  // the round's bits, big-endian words
   union {
-    uint16_t rec[REC][ST];         // first code starts, relative to the range start
-    uint8_t hist[ST / 32][256];    // rank scratch while building tables
+    struct {
+      uint16_t pos[REC][ST];  // lookup start, relative to the thread's range start
+      uint16_t cnt[REC][ST];  // codes counted before that lookup
+    } rec;
+    uint8_t hist[ST / 32][256];  // rank scratch while building tables
   };
-  uint32_t endpos[ST];   // relative end of each thread's last code (or kDead)
+  uint32_t endpos[ST];  // relative end of each thread's walk (or kDead)
   uint32_t warpsum[ST / 32];
   float y[16 * SMAXB];
   int maxlen, minlen, flag;
@@ -64,9 +71,10 @@ __device__ __forceinline__ uint32_t win32(const SerialShared& S, uint32_t pos) {
   return __funnelshift_l(S.win[i + 1], S.win[i], pos & 31);
 }
 
-// Codes longer than SK bits at relative bit `pos` (w = the 32 bits there).
-// Returns the symbol with *len set, or -1.
-__device__ __noinline__ int slow_decode(const SerialShared& S, uint32_t w, uint32_t pos, int* len) {
+// Codes longer than SK bits at relative bit `pos`.  Returns the symbol with
+// *len set, or -1.
+__device__ __noinline__ int slow_decode(const SerialShared& S, uint32_t pos, int* len) {
+  const uint32_t w = win32(S, pos);
   const int top = S.maxlen < 32 ? S.maxlen : 32;
   for (int l = SK + 1; l <= top; ++l) {
     if (uint64_t(w) < S.lim[l]) {
@@ -83,27 +91,49 @@ __device__ __noinline__ int slow_decode(const SerialShared& S, uint32_t w, uint3
   return generic_decode(bit_at, S.cnt, S.sorted, S.maxlen, len);
 }
 
-// Decodes the code at `pos` (the reader positioned there, >= SK valid bits).
-// Returns exponent << 7 in bits 7-14; advances pos and the reader.
-__device__ __forceinline__ uint32_t sdec(const SerialShared& S, SmemBitReader& br, uint32_t& pos,
-                                         bool& dead) {
-  const uint32_t e = S.lut[br.peek32() >> (32 - SK)];
-  const uint32_t len = e & 31u;
-  if (len == 0) {
-    int l = 1;
-    int sym = slow_decode(S, win32(S, pos), pos, &l);
-    if (sym < 0) {
-      dead = true;
-      sym = 0;
-      l = 1;
-    }
-    pos += uint32_t(l);
-    br.init(S.win, pos);
-    return uint32_t(sym) << 7;
+// One code at the window head (>= SK valid bits).  Returns exponent << 7 in
+// bits 7-14; a code longer than SK bits re-positions the window after it.
+__device__ __forceinline__ uint32_t code1(const SerialShared& S, SmemWin96& r, bool& dead) {
+  const uint32_t e = S.lut[r.w0 >> (32 - SK)];
+  if (e) {
+    r.skip(e);
+    return e;
   }
-  br.skip(int(len));
-  pos += len;
-  return e;
+  const uint32_t pos = r.pos();
+  int l = 1;
+  int sym = slow_decode(S, pos, &l);
+  if (sym < 0) {
+    dead = true;
+    sym = 0;
+    l = 1;
+  }
+  r.init(S.win, pos + uint32_t(l));
+  return uint32_t(sym) << 7;
+}
+
+// Four codes from a window holding >= 4*SK bits, branch-free; a block that
+// meets a code longer than SK bits is rewound and redone code by code.
+__device__ __forceinline__ void code4(const SerialShared& S, SmemWin96& r, bool& dead,
+                                      uint32_t& e0, uint32_t& e1, uint32_t& e2, uint32_t& e3) {
+  const SmemWin96 s = r;
+  e0 = S.lut[r.w0 >> (32 - SK)];
+  r.skip(e0);
+  e1 = S.lut[r.w0 >> (32 - SK)];
+  r.skip(e1);
+  e2 = S.lut[r.w0 >> (32 - SK)];
+  r.skip(e2);
+  e3 = S.lut[r.w0 >> (32 - SK)];
+  r.skip(e3);
+  if ((e0 == 0) | (e1 == 0) | (e2 == 0) | (e3 == 0)) {
+    r = s;
+    e0 = code1(S, r, dead);
+    r.refill();
+    e1 = code1(S, r, dead);
+    r.refill();
+    e2 = code1(S, r, dead);
+    r.refill();
+    e3 = code1(S, r, dead);
+  }
 }
 
 // Builds canonical tables for the slab's code lengths.  Returns false for an
@@ -172,7 +202,7 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
     S.sorted[S.offs[l] + r] = uint8_t(t);
   }
   __syncthreads();
-  // first-level table: thread t fills entries [PER*t, PER*t + PER)
+  // single-code table: thread t fills entries [PER*t, PER*t + PER)
   constexpr int PER = (1 << SK) / ST;
   int len = S.minlen;
   for (int k = 0; k < PER; ++k) {
@@ -186,6 +216,21 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
                      uint32_t(len));
     }
     S.lut[e] = val;
+  }
+  __syncthreads();
+  // count table: the whole codes inside each CK-bit window
+  constexpr int CPER = (1 << CK) / ST;
+  for (int k = 0; k < CPER; ++k) {
+    const uint32_t v0 = uint32_t(t * CPER + k);
+    uint32_t used = 0, n = 0;
+    for (;;) {
+      const uint32_t idx = ((v0 << used) & ((1u << CK) - 1)) << (SK - CK);
+      const uint32_t ln = S.lut[idx] & 31u;
+      if (ln == 0 || ln > uint32_t(CK) - used) break;
+      used += ln;
+      ++n;
+    }
+    S.clut[v0] = uint8_t(n ? (n << 4) | used : 0);
   }
   __syncthreads();
   return true;
@@ -207,7 +252,7 @@ struct SOut {
   float* yg;
   uint64_t rows, cols;
   uint32_t ld, nb;
-  bool nice;
+  bool nice, xvec;
 };
 
 template <int MODE>
@@ -275,6 +320,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
     o.nb = a.nb;
     o.nice = rows == 16 && (cols & 15) == 0 &&
              (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
+    o.xvec = MODE == 1 && a.nb == 1 && a.ld == 1 && (reinterpret_cast<uintptr_t>(o.x) & 15) == 0;
     if (MODE == 1) {
       for (int k = t; k < 16 * SMAXB; k += ST) S.y[k] = 0.f;
       if (!o.nice)
@@ -315,23 +361,36 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
       const uint32_t my_hi = min(my_lo + S_bits, lim_rel);
       const uint32_t p0rel = p0 - R0;
       __syncthreads();
-      // ---- 2. speculative pass ----
+      // ---- 2. count pass ----
       const uint32_t st0 = t == 0 ? p0rel : my_lo;
-      uint32_t e1 = st0, n1 = 0;
+      uint32_t e1 = st0, n1 = 0, nrec = 0;
       bool d1 = false;
       if (st0 < my_hi) {
-        SmemBitReader br;
-        br.init(S.win, st0);
+        SmemWin96 r;
+        r.init(S.win, st0);
         uint32_t pos = st0;
         bool go = true;
         while (go) {
-          br.refill_uniform();
+          r.refill2();  // >= 65 bits: four lookups of <= SK bits
 #pragma unroll
-          for (int k = 0; k < 3; ++k) {
+          for (int k = 0; k < 4; ++k) {
             if (go) {
-              if (n1 < REC) S.rec[n1][t] = uint16_t(pos - my_lo);
-              sdec(S, br, pos, d1);
-              ++n1;
+              if (nrec < REC) {
+                S.rec.pos[nrec][t] = uint16_t(pos - my_lo);
+                S.rec.cnt[nrec][t] = uint16_t(n1);
+                ++nrec;
+              }
+              // near the stream end whole-window lookups could count padding
+              const uint32_t c = pos + CK <= lim_rel ? uint32_t(S.clut[r.w0 >> (32 - CK)]) : 0u;
+              if (c) {
+                n1 += c >> 4;
+                pos += c & 15u;
+                r.skip(c & 15u);
+              } else {
+                code1(S, r, d1);
+                ++n1;
+                pos = r.pos();
+              }
               go = !d1 && pos < my_hi;
             }
           }
@@ -358,25 +417,26 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
             myE = kDead;
             myN = 0;
           } else {
-            SmemBitReader br;
-            br.init(S.win, A);
+            SmemWin96 r;
+            r.init(S.win, A);
             uint32_t pos = A, k = 0, j = 0;
-            const uint32_t m = min(n1, uint32_t(REC));
+            const uint32_t m = nrec;
             bool synced = false, dead = false;
             while (pos < my_hi) {
               const uint32_t rel = pos - my_lo;
-              while (j < m && S.rec[j][t] < rel) ++j;
-              if (j < m && S.rec[j][t] == rel) {
+              while (j < m && S.rec.pos[j][t] < rel) ++j;
+              if (j < m && S.rec.pos[j][t] == rel) {
                 synced = true;
                 break;
               }
-              br.refill_uniform();
-              sdec(S, br, pos, dead);
+              r.refill();
+              code1(S, r, dead);
               if (dead) break;
+              pos = r.pos();
               ++k;
             }
             if (synced) {
-              myN = k + n1 - j;
+              myN = k + n1 - S.rec.cnt[j][t];
               myE = d1 ? kDead : e1;
               myD = d1;
             } else {
@@ -412,16 +472,15 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
       }
       // ---- 5. exact decode straight to the output ----
       if (myN) {
-        uint32_t pos = t == 0 ? p0rel : S.endpos[t - 1];
-        SmemBitReader br;
-        br.init(S.win, pos);
+        SmemWin96 r;
+        r.init(S.win, t == 0 ? p0rel : S.endpos[t - 1]);
         bool dead = false;
         uint32_t g = base + my_off;
         const uint32_t gend = g + myN;
         if (o.nice) {
           for (; g < gend && (g & 7); ++g) {
-            br.refill_uniform();
-            const uint32_t e = sdec(S, br, pos, dead);
+            r.refill();
+            const uint32_t e = code1(S, r, dead);
             semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
           }
           if (g + 8 <= gend) {
@@ -430,26 +489,19 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
             for (; g + 8 <= gend; g += 8) {
               const uint64_t s8 = smr.take();
               uint32_t e[8];
-              br.refill_uniform();
-              e[0] = sdec(S, br, pos, dead);
-              e[1] = sdec(S, br, pos, dead);
-              e[2] = sdec(S, br, pos, dead);
-              br.refill_uniform();
-              e[3] = sdec(S, br, pos, dead);
-              e[4] = sdec(S, br, pos, dead);
-              e[5] = sdec(S, br, pos, dead);
-              br.refill_uniform();
-              e[6] = sdec(S, br, pos, dead);
-              e[7] = sdec(S, br, pos, dead);
+              r.refill2();
+              code4(S, r, dead, e[0], e[1], e[2], e[3]);
+              r.refill2();
+              code4(S, r, dead, e[4], e[5], e[6], e[7]);
               const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
-              const uint32_t r = (g >> 4) & 15, c = (g >> 8) * 16 + (g & 15);
+              const uint32_t rr = (g >> 4) & 15, c = (g >> 8) * 16 + (g & 15);
               if (MODE == 0) {
                 uint4 w;
                 w.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
                 w.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
                 w.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
                 w.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
-                *reinterpret_cast<uint4*>(o.out + size_t(r) * cols + c) = w;
+                *reinterpret_cast<uint4*>(o.out + size_t(rr) * cols + c) = w;
               } else {
                 float wf[8];
 #pragma unroll
@@ -457,20 +509,34 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
                   const uint32_t sb = (q < 4 ? slo : shi) >> (8 * (q & 3));
                   wf[q] = __uint_as_float(merge1(e[q], sb & 255u) << 16);
                 }
-                for (uint32_t b = 0; b < o.nb; ++b) {
-                  float acc = 0.f;
+                if (o.xvec) {
+                  const float4* xv = reinterpret_cast<const float4*>(o.x + c);
+                  const float4 x0 = __ldg(xv), x1 = __ldg(xv + 1);
+                  float acc = wf[0] * x0.x;
+                  acc = fmaf(wf[1], x0.y, acc);
+                  acc = fmaf(wf[2], x0.z, acc);
+                  acc = fmaf(wf[3], x0.w, acc);
+                  acc = fmaf(wf[4], x1.x, acc);
+                  acc = fmaf(wf[5], x1.y, acc);
+                  acc = fmaf(wf[6], x1.z, acc);
+                  acc = fmaf(wf[7], x1.w, acc);
+                  atomicAdd(&S.y[rr * SMAXB], acc);
+                } else {
+                  for (uint32_t b = 0; b < o.nb; ++b) {
+                    float acc = 0.f;
 #pragma unroll
-                  for (int q = 0; q < 8; ++q)
-                    acc = fmaf(wf[q], __ldg(&o.x[uint64_t(c + q) * o.ld + b]), acc);
-                  atomicAdd(&S.y[r * SMAXB + b], acc);
+                    for (int q = 0; q < 8; ++q)
+                      acc = fmaf(wf[q], __ldg(&o.x[uint64_t(c + q) * o.ld + b]), acc);
+                    atomicAdd(&S.y[rr * SMAXB + b], acc);
+                  }
                 }
               }
             }
           }
         }
         for (; g < gend; ++g) {
-          br.refill_uniform();
-          const uint32_t e = sdec(S, br, pos, dead);
+          r.refill();
+          const uint32_t e = code1(S, r, dead);
           semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
         }
       }

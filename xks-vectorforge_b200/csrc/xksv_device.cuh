@@ -251,6 +251,52 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
+// 96-bit MSB-first bit window w0:w1:w2 (nb valid bits) over a stream held in
+// shared memory as big-endian words; wi is the next word to append, so the
+// window head sits at bit 32*wi - nb.  One refill() keeps nb >= 65 when nb was
+// >= 33, enough for several table-sized codes without further checks.
+struct SmemWin96 {
+  const uint32_t* win;
+  uint32_t wi, w0, w1, w2;
+  int nb;
+  __device__ __forceinline__ void init(const uint32_t* w, uint32_t pos) {
+    win = w;
+    const uint32_t k = pos >> 5, sb = pos & 31;
+    const uint32_t a = win[k], b = win[k + 1], c = win[k + 2];
+    w0 = __funnelshift_l(b, a, sb);
+    w1 = __funnelshift_l(c, b, sb);
+    w2 = __funnelshift_l(0u, c, sb);
+    nb = 96 - int(sb);
+    wi = k + 3;
+  }
+  // Appends the next word when nb <= 64, without a data-dependent branch.
+  __device__ __forceinline__ void refill() {
+    const bool need = nb <= 64;
+    const uint32_t t = need ? win[wi] : 0u;
+    const bool low = nb < 32;
+    const uint32_t sh = need ? uint32_t(low ? 32 - nb : 64 - nb) : 0u;
+    const uint64_t v = uint64_t(t) << sh;
+    const uint32_t a = uint32_t(v >> 32), c = uint32_t(v);
+    w0 |= low ? a : 0u;
+    w1 |= low ? c : a;
+    w2 |= low ? 0u : c;
+    nb += need ? 32 : 0;
+    wi += need ? 1u : 0u;
+  }
+  // nb >= 65 afterwards from any nb >= 1.
+  __device__ __forceinline__ void refill2() {
+    refill();
+    if (nb < 65) refill();
+  }
+  __device__ __forceinline__ void skip(uint32_t n) {  // uses the low 5 bits of n
+    w0 = __funnelshift_l(w1, w0, n);
+    w1 = __funnelshift_l(w2, w1, n);
+    w2 = __funnelshift_l(0u, w2, n);
+    nb -= int(n & 31u);
+  }
+  __device__ __forceinline__ uint32_t pos() const { return 32 * wi - uint32_t(nb); }
+};
+
 // ---------------------------------------------------- BF16 assembly -------
 // Two BF16 words from two exponent bytes (e0 in bits 0-7, e1 in bits 8-15)
 // and two sign/mantissa bytes (same places), packed low word first.
