@@ -304,7 +304,9 @@ def fused_gemv(args, dev, stream, threads):
     with torch.cuda.stream(stream):
         for _ in range(3):
             graph.replay()
+        torch.cuda.nvtx.range_push("timed")
         t = time_steps(graph.replay, args.gemv_steps, stream)
+        torch.cuda.nvtx.range_pop()
     ms = t / args.gemv_steps * 1e3
     bad += sum(pl.status(h) for pl in plans)
     # correctness spot check of one layer's down_proj against an FP32 matmul of
@@ -332,6 +334,56 @@ def fused_gemv(args, dev, stream, threads):
                 note="per token: 128 dependent plan launches (qkv, o, gate+up, down per layer) in one CUDA graph; lm_head excluded as in runtime.py:258")
 
 
+def run_case(args):
+    """Small fixed decode workload for profiling and kernel timing:
+    `--case CODEC:ROWSxCOLS:SLABS` decodes SLABS slabs (64 distinct seeded
+    N(0, 0.02) slabs, repeated) in one plan launch per step, HBM-resident;
+    CODEC is `serial` (bf16-huffman-tile16) or `parallel` (XKSP2).  Prints
+    one JSON line with the per-launch time."""
+    import numpy as np
+    import torch
+    import xksv_gpu
+
+    codec_name, shape, nslabs = args.case.split(":")
+    codec = {"serial": 1, "parallel": 2}[codec_name]
+    rows, cols = map(int, shape.split("x"))
+    nslabs = int(nslabs)
+    dev = "cuda:0"
+    torch.cuda.set_device(0)
+    lib = xksv_gpu.load()
+    gen = torch.Generator(device=dev).manual_seed(5)
+    uniq = []
+    for _ in range(min(64, nslabs)):
+        w = (torch.randn(rows, cols, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        tile = w.view(torch.int16).cpu().numpy().tobytes()
+        uniq.append(xksv_gpu.host_pack(tile, rows, cols, codec, lib))
+    payload, entries, out = bytearray(), [], 0
+    for i in range(nslabs):
+        b = uniq[i % len(uniq)]
+        entries.append(dict(src_offset=len(payload), src_size=len(b), rows=rows, cols=cols,
+                            dst_offset=out, codec=codec))
+        payload += b
+        out += rows * cols * 2
+    d_payload = torch.frombuffer(payload, dtype=torch.uint8).to(dev)
+    d_out = torch.empty(out, dtype=torch.uint8, device=dev)
+    plan = xksv_gpu.Plan(entries)
+    stream = torch.cuda.Stream(device=dev)
+    h = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+        assert plan.status(h) == 0, "decode reported a slab error"
+        torch.cuda.nvtx.range_push("timed")
+        t = time_steps(lambda: plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h), args.steps, stream)
+        torch.cuda.nvtx.range_pop()
+    assert plan.status(h) == 0
+    plan.close()
+    ms = t / args.steps * 1e3
+    print(json.dumps(dict(case=args.case, slabs=nslabs, compressed_bytes=len(payload), out_bytes=out,
+                          ms_per_launch=round(ms, 5), out_gbs=round(out / ms / 1e6, 1),
+                          traffic_gbs=round((out + len(payload)) / ms / 1e6, 1))), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -342,8 +394,13 @@ def main():
     ap.add_argument("--warmup-cpu", type=int, default=0)
     ap.add_argument("--gemv-steps", type=int, default=20)
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--case", default=None,
+                    help="CODEC:ROWSxCOLS:SLABS small decode workload (profiling), e.g. parallel:16x2048:2048")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.case:
+        run_case(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -406,7 +463,9 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         t = time_steps(step, args.steps, stream)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     assert plan.status(h) == 0
     launches = plan.launches() * args.steps
