@@ -287,6 +287,12 @@ def fused_gemv(args, dev, stream, threads):
     x = torch.randn(xs, generator=torch.Generator(device=dev).manual_seed(3), device=dev).to(torch.bfloat16).float()
     y = torch.empty(ys, device=dev)
     h = stream.cuda_stream
+    # one-time tile index of the resident weights (xksv_plan_index)
+    t_idx = time.perf_counter()
+    for pl in plans:
+        if pl.index(d_payload.data_ptr(), h):
+            raise RuntimeError("xksv_plan_index failed")
+    index_s = time.perf_counter() - t_idx
 
     def forward():
         for pl in plans:
@@ -330,6 +336,8 @@ def fused_gemv(args, dev, stream, threads):
     return dict(metric="fused-GEMV tok/s Llama-8B b=1", value=round(1e3 / ms, 2), unit="tok/s",
                 ms_per_token=round(ms, 4), codec="dfloat11", compressed_bytes=comp_bytes,
                 hbm_gbs=round(comp_bytes / (ms / 1e3) / 1e9, 1), launches_per_token=launches,
+                index_build_s=round(index_s, 3),
+                index_bytes=4 * sum(t["n"] * (t["cols"] // 16 + 1) for t in info),
                 rel_l2_layer0_down=rel, status_errors=bad,
                 note="per token: 128 dependent plan launches (qkv, o, gate+up, down per layer) in one CUDA graph; lm_head excluded as in runtime.py:258")
 
@@ -345,7 +353,8 @@ def run_case(args):
     import xksv_gpu
 
     codec_name, shape, nslabs = args.case.split(":")
-    codec = {"serial": 1, "parallel": 2}[codec_name]
+    gemv = codec_name.startswith("gemv-")
+    codec = {"serial": 1, "parallel": 2}[codec_name[5:] if gemv else codec_name]
     rows, cols = map(int, shape.split("x"))
     nslabs = int(nslabs)
     dev = "cuda:0"
@@ -360,28 +369,43 @@ def run_case(args):
     payload, entries, out = bytearray(), [], 0
     for i in range(nslabs):
         b = uniq[i % len(uniq)]
+        # GEMV: slab i computes rows 16i.. of Y from all of X
         entries.append(dict(src_offset=len(payload), src_size=len(b), rows=rows, cols=cols,
-                            dst_offset=out, codec=codec))
+                            dst_offset=i * rows if gemv else out, codec=codec))
         payload += b
         out += rows * cols * 2
     d_payload = torch.frombuffer(payload, dtype=torch.uint8).to(dev)
-    d_out = torch.empty(out, dtype=torch.uint8, device=dev)
     plan = xksv_gpu.Plan(entries)
     stream = torch.cuda.Stream(device=dev)
     h = stream.cuda_stream
+    if gemv:
+        x = torch.randn(cols, device=dev)
+        y = torch.empty(nslabs * rows, device=dev)
+        if plan.index(d_payload.data_ptr(), h):
+            raise RuntimeError("xksv_plan_index failed")
+        fn = lambda: plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 1, h)
+    else:
+        d_out = torch.empty(out, dtype=torch.uint8, device=dev)
+        fn = lambda: plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
-        assert plan.status(h) == 0, "decode reported a slab error"
+            fn()
+        assert plan.status(h) == 0, "slab error"
         torch.cuda.nvtx.range_push("timed")
-        t = time_steps(lambda: plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h), args.steps, stream)
+        t = time_steps(fn, args.steps, stream)
         torch.cuda.nvtx.range_pop()
     assert plan.status(h) == 0
     plan.close()
     ms = t / args.steps * 1e3
-    print(json.dumps(dict(case=args.case, slabs=nslabs, compressed_bytes=len(payload), out_bytes=out,
-                          ms_per_launch=round(ms, 5), out_gbs=round(out / ms / 1e6, 1),
-                          traffic_gbs=round((out + len(payload)) / ms / 1e6, 1))), flush=True)
+    line = dict(case=args.case, slabs=nslabs, compressed_bytes=len(payload), out_bytes=out,
+                ms_per_launch=round(ms, 5))
+    if gemv:
+        idx = nslabs * (cols // 16 + 1) * 4
+        line.update(gweights_per_s=round(out / 2 / ms / 1e6, 1),
+                    traffic_gbs=round((len(payload) + idx) / ms / 1e6, 1), index_bytes=idx)
+    else:
+        line.update(out_gbs=round(out / ms / 1e6, 1), traffic_gbs=round((out + len(payload)) / ms / 1e6, 1))
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -395,7 +419,8 @@ def main():
     ap.add_argument("--gemv-steps", type=int, default=20)
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--case", default=None,
-                    help="CODEC:ROWSxCOLS:SLABS small decode workload (profiling), e.g. parallel:16x2048:2048")
+                    help="CODEC:ROWSxCOLS:SLABS small decode workload (profiling), e.g. parallel:16x2048:2048; "
+                         "gemv-serial:16x4096:1024 runs the indexed batch-1 GEMV instead")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.case:

@@ -104,6 +104,20 @@ int xksv_plan_status(const xksv_plan* plan, void* stream);
  * enqueued (for accounting in benchmarks). */
 int xksv_plan_launches(const xksv_plan* plan);
 
+/* Builds the plan's tile index for resident weights: one decode pass over
+ * the plan's 16-row serial-codec slabs with cols % 16 == 0 records the bit
+ * offset at which every 16x16 tile's codes start (4 bytes per tile, kept on
+ * the device with the plan).  Afterwards xksv_plan_gemm with the same
+ * d_payload pointer decodes those slabs tile-parallel, one thread per tile,
+ * instead of re-synchronising each slab's single bit stream on every call.
+ * The index describes the payload's contents at this call: rebuild it if they
+ * change.  No reference counterpart (the reference decodes every slab from
+ * its first bit, cuda/decode.cu:12-45); it is an acceleration structure on
+ * the side, the slab format is unchanged.  Synchronises `stream`; 0 on
+ * success, 1 on a bad slab or CUDA error (no index is kept then).  Calls on
+ * one plan must not overlap. */
+int xksv_plan_index(xksv_plan* plan, const void* d_payload, void* stream);
+
 
 /* ---------------- Part 3: archive-side encoder (host CPU) --------------- */
 /* The compile step that produces slabs for the decoder; byte-identical to the

@@ -180,7 +180,39 @@ struct xksv_plan {
   int* h_status = nullptr;
   int grid_ser = 148, grid_par = 148, grid_raw = 148;
   int launches = 0;
+  // tile index (xksv_plan_index): the first n_ser_idx serial slabs are
+  // 16-row slabs with cols % 16 == 0
+  uint32_t n_ser_idx = 0;
+  std::vector<xksv::Slab> h_slabs;  // host copy of d_slabs
+  const void* indexed_payload = nullptr;
+  uint32_t* d_tidx = nullptr;
+  uint64_t* d_tbase = nullptr;
+  xksv::GemvItem* d_items = nullptr;
+  uint32_t n_items = 0;
+  float* d_partials = nullptr;
+  uint32_t* d_counters = nullptr;
 };
+
+namespace {
+void free_index(xksv_plan* p) {
+  if (p->d_tidx) cudaFree(p->d_tidx);
+  if (p->d_tbase) cudaFree(p->d_tbase);
+  if (p->d_items) cudaFree(p->d_items);
+  if (p->d_partials) cudaFree(p->d_partials);
+  if (p->d_counters) cudaFree(p->d_counters);
+  p->d_tidx = nullptr;
+  p->d_tbase = nullptr;
+  p->d_items = nullptr;
+  p->d_partials = nullptr;
+  p->d_counters = nullptr;
+  p->n_items = 0;
+  p->indexed_payload = nullptr;
+}
+
+bool tile_indexable(const xksv::Slab& s) {
+  return s.rows == 16 && s.cols % 16 == 0 && s.cols < (1ull << 27);
+}
+}  // namespace
 
 using namespace xksv;
 
@@ -266,8 +298,12 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
         return 1;
     }
   }
+  // indexable serial slabs first (the order of slabs within a codec is free:
+  // every slab carries its own output offset)
+  std::stable_partition(ser.begin(), ser.end(), tile_indexable);
   auto* p = new xksv_plan();
   cudaGetDevice(&p->device);
+  p->n_ser_idx = uint32_t(std::count_if(ser.begin(), ser.end(), tile_indexable));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
   (void)sms;
@@ -292,6 +328,10 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
     ok = cudaMalloc(&p->d_slabs, n * sizeof(Slab)) == cudaSuccess &&
          cudaMemcpy(p->d_slabs, all.data(), n * sizeof(Slab), cudaMemcpyHostToDevice) == cudaSuccess;
   }
+  // the copies above ran on the legacy default stream, which callers' non-blocking
+  // streams do not wait for: finish them before the plan is used anywhere
+  ok = ok && cudaStreamSynchronize(nullptr) == cudaSuccess;
+  p->h_slabs = std::move(all);
   if (!ok) {
     xksv_plan_destroy(p);
     return 1;
@@ -302,6 +342,7 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
 
 void xksv_plan_destroy(xksv_plan* p) {
   if (!p) return;
+  free_index(p);
   if (p->d_slabs) cudaFree(p->d_slabs);
   if (p->d_status) cudaFree(p->d_status);
   if (p->h_status) cudaFreeHost(p->h_status);
@@ -342,11 +383,34 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
   p->launches = 0;
   cudaError_t e = cudaSuccess;
   const uint32_t ld = uint32_t(batch);
+  // indexed serial slabs: tile-parallel kernel, 4 batch columns per pass
+  const bool indexed = p->d_tidx && d_payload == p->indexed_payload;
+  const uint32_t ser0 = indexed ? p->n_ser_idx : 0;
+  if (indexed && p->n_items) {
+    for (size_t b0 = 0; b0 < batch && e == cudaSuccess; b0 += 4) {
+      GemvArgs g{};
+      g.items = p->d_items;
+      g.nitems = p->n_items;
+      g.slabs = p->d_slabs;
+      g.tbase = p->d_tbase;
+      g.tidx = p->d_tidx;
+      g.payload = pay;
+      g.x = d_x + b0;
+      g.y = d_y + b0;
+      g.ld = ld;
+      g.nb = uint32_t(std::min<size_t>(4, batch - b0));
+      g.partials = p->d_partials;
+      g.counters = p->d_counters;
+      g.status = p->d_status;
+      e = launch_serial_tile_gemm(g, st);
+      ++p->launches;
+    }
+  }
   for (size_t b0 = 0; b0 < batch && e == cudaSuccess; b0 += 8) {
     const uint32_t nb = uint32_t(std::min<size_t>(8, batch - b0));
-    if (p->n_ser) {
-      e = launch_serial_gemm(p->d_slabs, p->n_ser, pay, d_x, d_y, ld, uint32_t(b0), nb, p->d_status,
-                             p->grid_ser, st);
+    if (p->n_ser > ser0) {
+      e = launch_serial_gemm(p->d_slabs + ser0, p->n_ser - ser0, pay, d_x, d_y, ld, uint32_t(b0), nb,
+                             p->d_status, p->grid_ser, st);
       ++p->launches;
     }
     if (e == cudaSuccess && p->n_par) {
@@ -377,5 +441,64 @@ int xksv_plan_status(const xksv_plan* pc, void* stream) {
 }
 
 int xksv_plan_launches(const xksv_plan* p) { return p ? p->launches : 0; }
+
+int xksv_plan_index(xksv_plan* p, const void* d_payload, void* stream) {
+  if (!p || !d_payload) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return 1;
+  free_index(p);
+  const uint32_t n = p->n_ser_idx;
+  if (!n) {
+    p->indexed_payload = d_payload;
+    return 0;
+  }
+  const std::vector<Slab>& sl = p->h_slabs;
+  // index layout: per slab (tiles + 1) entries; items: <= 256 tiles each,
+  // tiles spread evenly over the slab's items
+  std::vector<uint64_t> tbase(n);
+  std::vector<GemvItem> items;
+  uint64_t total = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint32_t tiles = uint32_t(sl[i].cols / 16);
+    tbase[i] = total;
+    total += uint64_t(tiles) + 1;
+    const uint32_t ni = (tiles + 255) / 256;
+    const uint32_t per = (tiles + ni - 1) / ni;
+    const uint32_t first = uint32_t(items.size());
+    for (uint32_t k = 0; k < ni; ++k) {
+      const uint32_t t0 = k * per;
+      items.push_back(GemvItem{i, t0, std::min(per, tiles - t0), first, ni, 0, 0, 0});
+    }
+  }
+  if (total > std::numeric_limits<uint32_t>::max() || items.size() > (1u << 31)) return 1;
+  // every copy and fill on the caller's stream, ahead of the index kernel
+  // (a non-blocking stream does not wait for the legacy default stream)
+  bool ok = cudaMalloc(&p->d_tidx, total * sizeof(uint32_t)) == cudaSuccess &&
+            cudaMalloc(&p->d_tbase, n * sizeof(uint64_t)) == cudaSuccess &&
+            cudaMalloc(&p->d_items, items.size() * sizeof(GemvItem)) == cudaSuccess &&
+            cudaMalloc(&p->d_partials, items.size() * 16 * 4 * sizeof(float)) == cudaSuccess &&
+            cudaMalloc(&p->d_counters, n * sizeof(uint32_t)) == cudaSuccess &&
+            cudaMemcpyAsync(p->d_tbase, tbase.data(), n * sizeof(uint64_t), cudaMemcpyHostToDevice, st) == cudaSuccess &&
+            cudaMemcpyAsync(p->d_items, items.data(), items.size() * sizeof(GemvItem), cudaMemcpyHostToDevice, st) == cudaSuccess &&
+            cudaMemsetAsync(p->d_counters, 0, n * sizeof(uint32_t), st) == cudaSuccess &&
+            cudaMemsetAsync(p->d_tidx, 0, total * sizeof(uint32_t), st) == cudaSuccess &&
+            cudaMemsetAsync(p->d_status, 0, sizeof(int), st) == cudaSuccess;
+  if (ok)
+    ok = launch_serial_index(p->d_slabs, n, static_cast<const uint8_t*>(d_payload), p->d_tidx,
+                             p->d_tbase, p->d_status, st) == cudaSuccess;
+  if (ok)
+    ok = cudaMemcpyAsync(p->h_status, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+         cudaStreamSynchronize(st) == cudaSuccess;
+  const bool bad = !ok || *p->h_status != 0;
+  cudaMemsetAsync(p->d_status, 0, sizeof(int), st);
+  cudaStreamSynchronize(st);
+  if (bad) {
+    free_index(p);
+    return 1;
+  }
+  p->n_items = uint32_t(items.size());
+  p->indexed_payload = d_payload;
+  return 0;
+}
 
 }  // extern "C"

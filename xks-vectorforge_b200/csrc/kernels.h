@@ -31,4 +31,26 @@ cudaError_t launch_raw_gemm(const Slab* slabs, uint32_t n, const uint8_t* payloa
                             float* y, uint32_t ld, uint32_t b0, uint32_t nb, int grid,
                             cudaStream_t st);
 
+// Tile index of 16-row serial-codec slabs: tidx[tbase[i] + k] = bit offset of
+// tile k's first code in slab i's stream, tidx[tbase[i] + tiles] = bit count.
+cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* payload,
+                                uint32_t* tidx, const uint64_t* tbase, int* status, cudaStream_t st);
+
+struct GemvArgs {
+  const GemvItem* items;
+  uint32_t nitems;
+  const Slab* slabs;       // slabs the items refer to
+  const uint64_t* tbase;   // per slab: first tile-index entry
+  const uint32_t* tidx;    // tile index
+  const uint8_t* payload;
+  const float* x;          // X at batch column b0 (row stride ld)
+  float* y;                // Y at batch column b0 (row stride ld)
+  uint32_t ld, nb;         // nb <= 4 columns this pass
+  float* partials;         // [item][16][4] row sums of slabs split over several items
+  uint32_t* counters;      // per slab, zero between launches
+  int* status;
+};
+// Indexed fused GEMV/GEMM (nb <= 4) over 16-row serial-codec slabs.
+cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st);
+
 }  // namespace xksv

@@ -66,14 +66,16 @@ struct SerialShared {
   int maxlen, minlen, flag;
 };
 
-__device__ __forceinline__ uint32_t win32(const SerialShared& S, uint32_t pos) {
+template <class SH>
+__device__ __forceinline__ uint32_t win32(const SH& S, uint32_t pos) {
   const uint32_t i = pos >> 5;
   return __funnelshift_l(S.win[i + 1], S.win[i], pos & 31);
 }
 
 // Codes longer than SK bits at relative bit `pos`.  Returns the symbol with
 // *len set, or -1.
-__device__ __noinline__ int slow_decode(const SerialShared& S, uint32_t pos, int* len) {
+template <class SH>
+__device__ __noinline__ int slow_decode(const SH& S, uint32_t pos, int* len) {
   const uint32_t w = win32(S, pos);
   const int top = S.maxlen < 32 ? S.maxlen : 32;
   for (int l = SK + 1; l <= top; ++l) {
@@ -91,9 +93,12 @@ __device__ __noinline__ int slow_decode(const SerialShared& S, uint32_t pos, int
   return generic_decode(bit_at, S.cnt, S.sorted, S.maxlen, len);
 }
 
-// One code at the window head (>= SK valid bits).  Returns exponent << 7 in
-// bits 7-14; a code longer than SK bits re-positions the window after it.
-__device__ __forceinline__ uint32_t code1(const SerialShared& S, SmemWin96& r, bool& dead) {
+// One code at the window head (>= SK valid bits).  Table entries hold the
+// exponent at bit XS and the code length in bits 0-4; the result holds the
+// exponent at bit XS.  A code longer than SK bits re-positions the window
+// after it.
+template <int XS, class SH>
+__device__ __forceinline__ uint32_t code1(const SH& S, SmemWin96& r, bool& dead) {
   const uint32_t e = S.lut[r.w0 >> (32 - SK)];
   if (e) {
     r.skip(e);
@@ -108,13 +113,14 @@ __device__ __forceinline__ uint32_t code1(const SerialShared& S, SmemWin96& r, b
     l = 1;
   }
   r.init(S.win, pos + uint32_t(l));
-  return uint32_t(sym) << 7;
+  return uint32_t(sym) << XS;
 }
 
 // Four codes from a window holding >= 4*SK bits, branch-free; a block that
 // meets a code longer than SK bits is rewound and redone code by code.
-__device__ __forceinline__ void code4(const SerialShared& S, SmemWin96& r, bool& dead,
-                                      uint32_t& e0, uint32_t& e1, uint32_t& e2, uint32_t& e3) {
+template <int XS, class SH>
+__device__ __forceinline__ void code4(const SH& S, SmemWin96& r, bool& dead, uint32_t& e0,
+                                      uint32_t& e1, uint32_t& e2, uint32_t& e3) {
   const SmemWin96 s = r;
   e0 = S.lut[r.w0 >> (32 - SK)];
   r.skip(e0);
@@ -126,19 +132,20 @@ __device__ __forceinline__ void code4(const SerialShared& S, SmemWin96& r, bool&
   r.skip(e3);
   if ((e0 == 0) | (e1 == 0) | (e2 == 0) | (e3 == 0)) {
     r = s;
-    e0 = code1(S, r, dead);
+    e0 = code1<XS>(S, r, dead);
     r.refill();
-    e1 = code1(S, r, dead);
+    e1 = code1<XS>(S, r, dead);
     r.refill();
-    e2 = code1(S, r, dead);
+    e2 = code1<XS>(S, r, dead);
     r.refill();
-    e3 = code1(S, r, dead);
+    e3 = code1<XS>(S, r, dead);
   }
 }
 
 // Builds canonical tables for the slab's code lengths.  Returns false for an
 // oversubscribed codebook.
-__device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
+template <int XS, bool COUNT_TABLE, class SH>
+__device__ bool build_tables(SH& S, const uint8_t* lens) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   S.cnt[t] = 0;
   if (t == 0) {
@@ -209,15 +216,15 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
     const uint32_t e = uint32_t(t * PER + k);
     const uint64_t W = uint64_t(e) << (32 - SK);
     while (len <= SK && W >= S.lim[len]) ++len;
-    uint16_t val = 0;
+    uint32_t val = 0;
     if (len <= SK) {
       const uint32_t code = e >> (SK - len);
-      val = uint16_t((uint32_t(S.sorted[S.offs[len] + code - uint32_t(S.firstc[len])]) << 7) |
-                     uint32_t(len));
+      val = (uint32_t(S.sorted[S.offs[len] + code - uint32_t(S.firstc[len])]) << XS) | uint32_t(len);
     }
-    S.lut[e] = val;
+    S.lut[e] = decltype(+S.lut[0])(val);
   }
   __syncthreads();
+  if constexpr (COUNT_TABLE) {
   // count table: the whole codes inside each CK-bit window
   constexpr int CPER = (1 << CK) / ST;
   for (int k = 0; k < CPER; ++k) {
@@ -232,7 +239,8 @@ __device__ bool build_tables(SerialShared& S, const uint8_t* lens) {
     }
     S.clut[v0] = uint8_t(n ? (n << 4) | used : 0);
   }
-  __syncthreads();
+    __syncthreads();
+  }
   return true;
 }
 
@@ -243,6 +251,8 @@ struct SerialArgs {
   float* y;
   uint32_t ld, nb;
   int* status;
+  uint32_t* tidx;         // MODE 2: tile index (bit offset of each 16x16 tile's first code)
+  const uint64_t* tbase;  // MODE 2: first index entry of each slab
 };
 
 struct SOut {
@@ -301,7 +311,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
       if (t == 0) atomicOr(a.status, kStatusInternal);
       continue;
     }
-    if (!build_tables(S, p + 16)) {
+    if (!build_tables<7, true>(S, p + 16)) {
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       __syncthreads();
       continue;
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
                 pos += c & 15u;
                 r.skip(c & 15u);
               } else {
-                code1(S, r, d1);
+                code1<7>(S, r, d1);
                 ++n1;
                 pos = r.pos();
               }
@@ -430,7 +440,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
                 break;
               }
               r.refill();
-              code1(S, r, dead);
+              code1<7>(S, r, dead);
               if (dead) break;
               pos = r.pos();
               ++k;
@@ -471,7 +481,19 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
         break;
       }
       // ---- 5. exact decode straight to the output ----
-      if (myN) {
+      if (MODE == 2 && myN) {
+        // tile index: the stream offset of every 256th code (a 16x16 tile start)
+        SmemWin96 r;
+        r.init(S.win, t == 0 ? p0rel : S.endpos[t - 1]);
+        bool dead = false;
+        uint32_t* ti = a.tidx + a.tbase[si];
+        const uint32_t gend = base + my_off + myN;
+        for (uint32_t g = base + my_off; g < gend; ++g) {
+          if ((g & 255u) == 0) ti[g >> 8] = R0 + r.pos();
+          r.refill();
+          code1<7>(S, r, dead);
+        }
+      } else if (myN) {
         SmemWin96 r;
         r.init(S.win, t == 0 ? p0rel : S.endpos[t - 1]);
         bool dead = false;
@@ -480,7 +502,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
         if (o.nice) {
           for (; g < gend && (g & 7); ++g) {
             r.refill();
-            const uint32_t e = code1(S, r, dead);
+            const uint32_t e = code1<7>(S, r, dead);
             semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
           }
           if (g + 8 <= gend) {
@@ -490,9 +512,9 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
               const uint64_t s8 = smr.take();
               uint32_t e[8];
               r.refill2();
-              code4(S, r, dead, e[0], e[1], e[2], e[3]);
+              code4<7>(S, r, dead, e[0], e[1], e[2], e[3]);
               r.refill2();
-              code4(S, r, dead, e[4], e[5], e[6], e[7]);
+              code4<7>(S, r, dead, e[4], e[5], e[6], e[7]);
               const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
               const uint32_t rr = (g >> 4) & 15, c = (g >> 8) * 16 + (g & 15);
               if (MODE == 0) {
@@ -536,7 +558,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
         }
         for (; g < gend; ++g) {
           r.refill();
-          const uint32_t e = code1(S, r, dead);
+          const uint32_t e = code1<7>(S, r, dead);
           semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
         }
       }
@@ -548,10 +570,206 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
     if (!err && (base != cnt32 || p0 != nb32)) err = kStatusStream;
     if (err) {
       if (t == 0) atomicOr(a.status, err);
+    } else if (MODE == 2) {
+      if (t == 0) a.tidx[a.tbase[si] + (cnt32 >> 8)] = nb32;  // end sentinel
     } else if (MODE == 1 && o.nice) {
       for (uint32_t k = t; k < 16 * a.nb; k += ST) {
         const uint32_t r = k / a.nb, b = k - r * a.nb;
         a.y[(sd.dst + r) * a.ld + b] = S.y[r * SMAXB + b];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------ indexed tile GEMV ------
+// With a tile index (the bit offset of every 16x16 tile's first code, built
+// once per plan by serial_slab_kernel<2>), every tile of a 16-row slab can be
+// decoded on its own: one thread per tile, no speculative pass.  A CTA takes
+// up to GT consecutive tiles of one slab, stages their bits in shared memory
+// (in several rounds when they do not fit), and each thread walks its tile
+// row by row: 16 codes, 16 FP32 weights assembled from the table entry
+// (exponent at bit 23) and the sign/mantissa bytes, 16 FMAs with x held in
+// registers, then a warp sum per row.  Slabs split over several CTAs combine
+// their row sums in a fixed order in the last CTA to finish (deterministic,
+// and Y is overwritten as cuda/decode.cu:31 requires).
+constexpr int GT = 256;                  // threads (tiles) per GEMV CTA
+constexpr int GPAD = 160;                // zero words past a round: one row of 16 maximal codes + window
+constexpr int GWINW = 6144 + GPAD;       // staged bit words per round
+constexpr uint32_t GCAP = uint32_t(GWINW - GPAD - 1) * 32;  // bits per round
+constexpr int GNB = 4;                   // batch columns per pass
+
+struct GemvShared {
+  uint32_t lut[1 << SK];  // exponent << 23 | length; 0 = none
+  uint64_t lim[33];
+  uint64_t firstc[33];
+  alignas(16) uint16_t cnt[256];
+  uint16_t offs[257];
+  uint8_t sorted[256];
+  alignas(16) uint32_t win[GWINW];
+  uint8_t hist[GT / 32][256];
+  uint32_t warpsum[GT / 32];
+  float red[16][GT / 32][GNB];
+  int maxlen, minlen, flag;
+};
+
+// FP32 weight from a table entry (exponent at bit 23, length in bits 0-4) and
+// the sign/mantissa byte K of sw: byte -> bits 16-23 and 24-31, then one
+// bit-select keeps sign (31) and mantissa (16-22) from it, exponent from e.
+template <int K>
+__device__ __forceinline__ float wfloat(uint32_t e, uint32_t sw) {
+  constexpr uint32_t sel = 0x0044u | (uint32_t(K) << 8) | (uint32_t(K) << 12);
+  const uint32_t s = __byte_perm(sw, 0u, sel);
+  return __uint_as_float((s & 0x807FFFFFu) | (e & 0x7F800000u));
+}
+
+template <int NB>
+__global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  GemvShared& S = *reinterpret_cast<GemvShared*>(smem_raw);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  for (uint32_t ii = blockIdx.x; ii < a.nitems; ii += gridDim.x) {
+    const GemvItem it = a.items[ii];
+    const Slab sd = a.slabs[it.slab];
+    const uint8_t* p = a.payload + sd.src;
+    const uint32_t count = uint32_t(sd.rows * sd.cols);
+    const uint32_t nbits = uint32_t(ld_le64(p + 8));
+    if (!build_tables<23, false>(S, p + 16)) {  // validated when the index was built
+      if (t == 0) atomicOr(a.status, kStatusCodebook);
+      __syncthreads();
+      continue;
+    }
+    for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
+    const uint32_t* ti = a.tidx + a.tbase[it.slab];
+    const uint8_t* sm = p + kHdr;
+    const uint8_t* bits = sm + count;
+    const uint8_t* end = p + sd.size;
+    const bool mine = uint32_t(t) < it.ntiles;
+    const uint32_t tile = it.tile0 + uint32_t(mine ? t : 0);
+    const uint32_t b0 = ti[tile], b1 = ti[tile + 1];
+    // x for this tile's 16 columns
+    const float* xs = a.x + (sd.xoff + uint64_t(tile) * 16) * a.ld;
+    float xr[NB == 1 ? 16 : 1];
+    if (NB == 1) {
+      if (a.ld == 1 && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(xs) + q);
+          xr[4 * q] = v.x;
+          xr[4 * q + 1] = v.y;
+          xr[4 * q + 2] = v.z;
+          xr[4 * q + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) xr[q] = __ldg(xs + q * a.ld);
+      }
+    }
+    const uint8_t* smt = sm + uint64_t(tile) * 256;
+    uint32_t ta = 0;
+    while (ta < it.ntiles) {  // rounds (one, unless the tiles' bits exceed GCAP)
+      const uint32_t base_bit = ti[it.tile0 + ta] & ~31u;
+      const bool fits = mine && uint32_t(t) >= ta && b1 - base_bit <= GCAP;
+      const uint32_t tb = ta + uint32_t(__syncthreads_count(fits));
+      const uint32_t end_bit = ti[it.tile0 + tb];
+      if (tb == ta || end_bit < base_bit || end_bit - base_bit > GCAP) {
+        // an index that does not describe this payload (uniform branch)
+        if (t == 0) atomicOr(a.status, kStatusInternal);
+        break;
+      }
+      const uint32_t nw = (end_bit - base_bit + 31) / 32 + GPAD;
+      for (uint32_t j = t; j < nw; j += GT) {
+        const uint8_t* q = bits + (base_bit >> 3) + 4 * j;
+        uint32_t v = 0;
+        if (q < end) {
+          const uintptr_t qa = reinterpret_cast<uintptr_t>(q);
+          const uint32_t* qw = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
+          const int sh = int(qa & 3) * 8;
+          const uint32_t lo = __ldg(qw);
+          const uint32_t hi =
+              (sh && reinterpret_cast<const uint8_t*>(qw + 1) < end) ? __ldg(qw + 1) : 0u;
+          v = bswap32(sh ? __funnelshift_r(lo, hi, sh) : lo);
+        }
+        S.win[j] = v;
+      }
+      __syncthreads();
+      bool act = mine && uint32_t(t) >= ta && uint32_t(t) < tb && b0 >= base_bit && b1 >= b0;
+      SmemWin96 r;
+      r.init(S.win, act ? b0 - base_bit : 0u);
+      bool dead = false;
+      for (int row = 0; row < 16; ++row) {
+        float acc[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+        // a row starts inside the staged bits: its 16 codes stay inside GPAD
+        if (act && r.pos() > b1 - base_bit) {
+          atomicOr(a.status, kStatusStream);
+          act = false;
+        }
+        if (act) {
+          const uint4 s16 = ld16_any(smt + row * 16);
+          const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t e0, e1, e2, e3;
+            r.refill2();
+            code4<23>(S, r, dead, e0, e1, e2, e3);
+            const float w0 = wfloat<0>(e0, sw[q]), w1 = wfloat<1>(e1, sw[q]);
+            const float w2 = wfloat<2>(e2, sw[q]), w3 = wfloat<3>(e3, sw[q]);
+            if (NB == 1) {
+              acc[0] = fmaf(w0, xr[4 * q], acc[0]);
+              acc[0] = fmaf(w1, xr[4 * q + 1], acc[0]);
+              acc[0] = fmaf(w2, xr[4 * q + 2], acc[0]);
+              acc[0] = fmaf(w3, xr[4 * q + 3], acc[0]);
+            } else {
+              const float* xc = xs + uint64_t(4 * q) * a.ld;
+#pragma unroll
+              for (int b = 0; b < NB; ++b) {
+                if (uint32_t(b) < a.nb) {
+                  acc[b] = fmaf(w0, __ldg(xc + b), acc[b]);
+                  acc[b] = fmaf(w1, __ldg(xc + a.ld + b), acc[b]);
+                  acc[b] = fmaf(w2, __ldg(xc + 2 * a.ld + b), acc[b]);
+                  acc[b] = fmaf(w3, __ldg(xc + 3 * a.ld + b), acc[b]);
+                }
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          float v = acc[b];
+#pragma unroll
+          for (int d = 16; d >= 1; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+          if (lane == 0) S.red[row][warp][b] += v;
+        }
+      }
+      __syncthreads();
+      ta = tb;
+    }
+    (void)nbits;
+    // combine: row r, column b
+    const bool comb = uint32_t(t) < 16u * a.nb;
+    const uint32_t rr = uint32_t(t) / a.nb, bb = uint32_t(t) - rr * a.nb;
+    float v = 0.f;
+    if (comb)
+      for (int w = 0; w < GT / 32; ++w) v += S.red[rr][w][bb];
+    if (it.nitems == 1) {
+      if (comb) a.y[(sd.dst + rr) * a.ld + bb] = v;
+    } else {
+      if (comb) a.partials[uint64_t(ii) * 16 * GNB + rr * GNB + bb] = v;
+      __threadfence();
+      __syncthreads();
+      if (t == 0) S.flag = atomicAdd(&a.counters[it.slab], 1u) == it.nitems - 1;
+      __syncthreads();
+      if (S.flag) {
+        __threadfence();
+        if (comb) {
+          float sum = 0.f;
+          for (uint32_t j = 0; j < it.nitems; ++j)
+            sum += __ldcg(&a.partials[uint64_t(it.first + j) * 16 * GNB + rr * GNB + bb]);
+          a.y[(sd.dst + rr) * a.ld + bb] = sum;
+        }
+        if (t == 0) a.counters[it.slab] = 0;
       }
     }
     __syncthreads();
@@ -565,6 +783,10 @@ void serial_set_attr() {
   if (dev < 31 && ((done_mask >> dev) & 1)) return;
   cudaFuncSetAttribute(serial_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
+  cudaFuncSetAttribute(serial_slab_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   if (dev < 31) done_mask |= 1 << dev;
 }
 
@@ -576,7 +798,7 @@ cudaError_t launch_serial_decode(const Slab* slabs, uint32_t n, const uint8_t* p
                                  uint8_t* out, int* status, int grid, cudaStream_t st) {
   if (!n) return cudaSuccess;
   serial_set_attr();
-  SerialArgs a{payload, out, nullptr, nullptr, 1, 1, status};
+  SerialArgs a{payload, out, nullptr, nullptr, 1, 1, status, nullptr, nullptr};
   const int g = grid < int(n) ? grid : int(n);
   serial_slab_kernel<0><<<g, ST, sizeof(SerialShared), st>>>(slabs, n, a);
   return cudaGetLastError();
@@ -587,9 +809,32 @@ cudaError_t launch_serial_gemm(const Slab* slabs, uint32_t n, const uint8_t* pay
                                int* status, int grid, cudaStream_t st) {
   if (!n) return cudaSuccess;
   serial_set_attr();
-  SerialArgs a{payload, nullptr, x + b0, y + b0, ld, nb, status};
+  SerialArgs a{payload, nullptr, x + b0, y + b0, ld, nb, status, nullptr, nullptr};
   const int g = grid < int(n) ? grid : int(n);
   serial_slab_kernel<1><<<g, ST, sizeof(SerialShared), st>>>(slabs, n, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* payload,
+                                uint32_t* tidx, const uint64_t* tbase, int* status, cudaStream_t st) {
+  if (!n) return cudaSuccess;
+  serial_set_attr();
+  SerialArgs a{payload, nullptr, nullptr, nullptr, 1, 1, status, tidx, tbase};
+  serial_slab_kernel<2><<<n, ST, sizeof(SerialShared), st>>>(slabs, n, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st) {
+  if (!args.nitems) return cudaSuccess;
+  if (args.nb < 1 || args.nb > uint32_t(GNB)) return cudaErrorInvalidValue;
+  serial_set_attr();
+  const uint32_t g = args.nitems;
+  if (args.nb == 1)
+    serial_tile_gemv_kernel<1><<<g, GT, sizeof(GemvShared), st>>>(args);
+  else if (args.nb == 2)
+    serial_tile_gemv_kernel<2><<<g, GT, sizeof(GemvShared), st>>>(args);
+  else
+    serial_tile_gemv_kernel<4><<<g, GT, sizeof(GemvShared), st>>>(args);
   return cudaGetLastError();
 }
 

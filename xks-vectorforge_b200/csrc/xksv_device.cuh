@@ -297,6 +297,26 @@ struct SmemWin96 {
   __device__ __forceinline__ uint32_t pos() const { return 32 * wi - uint32_t(nb); }
 };
 
+// 16 bytes from any address (two aligned loads and a byte funnel).
+__device__ __forceinline__ uint4 ld16_any(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint4* q = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
+  const int off = int(a & 15);
+  const uint4 lo = ldg16(q);
+  if (off == 0) return lo;
+  const uint4 hi = ldg16(q + 1);
+  uint32_t w0 = lo.x, w1 = lo.y, w2 = lo.z, w3 = lo.w, w4 = hi.x, w5 = hi.y, w6 = hi.z, w7 = hi.w;
+  if (off & 8) {
+    w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
+  }
+  if (off & 4) {
+    w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
+  }
+  const int bs = (off & 3) * 8;
+  return make_uint4(__funnelshift_r(w0, w1, bs), __funnelshift_r(w1, w2, bs),
+                    __funnelshift_r(w2, w3, bs), __funnelshift_r(w3, w4, bs));
+}
+
 // ---------------------------------------------------- BF16 assembly -------
 // Two BF16 words from two exponent bytes (e0 in bits 0-7, e1 in bits 8-15)
 // and two sign/mantissa bytes (same places), packed low word first.

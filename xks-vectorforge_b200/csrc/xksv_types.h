@@ -18,6 +18,13 @@ struct Slab {
   uint64_t xoff;  // GEMV/GEMM: element offset of column 0 in X
 };
 
+// Indexed GEMV work item: tiles [tile0, tile0 + ntiles) of slab `slab`
+// (16-row slab, tile k = columns 16k..16k+15); the slab's items are
+// first .. first + nitems - 1.
+struct GemvItem {
+  uint32_t slab, tile0, ntiles, first, nitems, pad0, pad1, pad2;
+};
+
 // Status bits OR-ed into the plan's device status word.
 enum StatusBit : int {
   kStatusHeader = 1,    // malformed header / sizes / shape disagreement

@@ -44,6 +44,7 @@ _SIGS = {
                         ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_host_pack": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                         ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                         ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
@@ -153,6 +154,10 @@ class Plan:
     def gemm(self, d_payload, d_x, d_y, batch, stream=0):
         if self.lib.xksv_plan_gemm(self.handle, d_payload, d_x, d_y, batch, stream):
             raise RuntimeError("xksv_plan_gemm launch failed")
+
+    def index(self, d_payload, stream=0):
+        """Builds the tile index (xksv_plan_index); returns 0, or 1 on a bad slab."""
+        return self.lib.xksv_plan_index(self.handle, d_payload, stream)
 
     def status(self, stream=0):
         """0 when no slab reported an error since the last call, else 1."""
