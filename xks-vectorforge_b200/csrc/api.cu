@@ -461,8 +461,8 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, void* stream) {
   for (uint32_t i = 0; i < n; ++i) {
     const uint32_t tiles = uint32_t(sl[i].cols / 16);
     tbase[i] = total;
-    total += uint64_t(tiles) + 1;
-    const uint32_t ni = (tiles + 255) / 256;
+    total += uint64_t(tiles) + 1;  // every tile's first code + end
+    const uint32_t ni = (tiles + 255) / 256;  // one 256-thread CTA per item
     const uint32_t per = (tiles + ni - 1) / ni;
     const uint32_t first = uint32_t(items.size());
     for (uint32_t k = 0; k < ni; ++k) {

@@ -43,7 +43,7 @@ constexpr int PMAXB = 8;   // GEMM columns per pass
 // One warp's tables, lane-minor so that lane l always touches bank l/2.
 struct WarpTabs {
   uint16_t lut[1 << PK][32];      // exponent << 7 | length; 0 = no code of length <= PK
-  uint16_t lut2[NE > 0 ? NE << K2 : 1][32];  // second level: 12-bit prefix - (L << K2)
+  uint16_t lut2[(NE << K2) + 1][32];  // second level: 12-bit prefix - (L << K2); last row 0
   uint16_t cnt[PNL][32];          // number of codes of length PK+1+j
   uint8_t lpos[PNL][32];          // fill cursor per long length (build only)
   uint8_t lsym[PLONG][32];        // long-code symbols, canonical (length, symbol) order
@@ -173,7 +173,7 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
   for (uint32_t z = L; z < (1u << PK); ++z) W.lut[z][lane] = 0;
   // second level: codes of length PK+1..PK+K2 whose (PK+K2)-bit prefixes fall
   // in the first NE escape prefixes
-  for (int z = 0; z < (NE << K2); ++z) W.lut2[z][lane] = 0;
+  for (int z = 0; z <= (NE << K2); ++z) W.lut2[z][lane] = 0;
   if (NE == 0) {
     Lout = L;
     return 0;
@@ -269,14 +269,14 @@ struct LaneBits {
   // branch (needs nb >= 1).
   __device__ __forceinline__ void refill(const WarpTabs& W, int lane) {
     const bool need = nb <= 64;
-    const uint32_t t = need ? word(W, lane, rw) : 0u;
+    const uint32_t wd = word(W, lane, rw);  // unconditional load of a ring slot, then a select
+    const uint32_t t = need ? wd : 0u;
     const bool low = nb < 32;  // lands in w0:w1, else in w1:w2
-    const uint32_t sh = need ? uint32_t(low ? 32 - nb : 64 - nb) : 0u;  // 0..32
-    const uint64_t v = uint64_t(t) << sh;
-    const uint32_t a = uint32_t(v >> 32), c = uint32_t(v);
-    w0 |= low ? a : 0u;
-    w1 |= low ? c : a;
-    w2 |= low ? 0u : c;
+    const uint32_t k = uint32_t(low ? nb : nb - 32);
+    const uint32_t head = __funnelshift_rc(t, 0u, k), tail = __funnelshift_rc(0u, t, k);
+    w0 |= low ? head : 0u;
+    w1 |= low ? tail : head;
+    w2 |= low ? 0u : tail;
     nb += need ? 32 : 0;
     rw += need ? 1u : 0u;
   }
@@ -285,6 +285,11 @@ struct LaneBits {
     w1 = __funnelshift_l(w2, w1, n);
     w2 = __funnelshift_l(0u, w2, n);
     nb -= int(n & 31u);
+  }
+  __device__ __forceinline__ void shift(uint32_t n) {  // skip without updating nb
+    w0 = __funnelshift_l(w1, w0, n);
+    w1 = __funnelshift_l(w2, w1, n);
+    w2 = __funnelshift_l(0u, w2, n);
   }
   __device__ __forceinline__ uint64_t consumed() const {
     return uint64_t(rw - rw0) * 32 - uint64_t(nb) - skipb;
@@ -341,11 +346,7 @@ struct LaneCode {
 // Codes the two table levels do not hold (longer than PK+K2 bits, or beyond
 // the covered escape prefixes): the compact list, then a top-up of the window
 // and the ring so the rest of the group still has its bits.
-__device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lane,
-                                            const LaneCode& lc, bool& bad) {
-  uint32_t e = long_entry(b.w0, W, lane, lc.F, lc.maxlen);
-  if ((e & 31u) == 0) bad = true;
-  b.skip(e);
+__device__ __forceinline__ void top_up(LaneBits& b, WarpTabs& W, int lane) {
   if (b.nb < 65) {
     if (b.rw + 1 >= b.fw) {
       b.fetch(W, lane);
@@ -354,21 +355,31 @@ __device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lan
     if (b.rw + 4 >= b.fw) cp_async_wait_all();
     b.refill(W, lane);
   }
+}
+
+__device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lane,
+                                            const LaneCode& lc, bool& bad) {
+  top_up(b, W, lane);  // >= 33 bits: a whole long code (<= PK+PNL bits) is in w0
+  uint32_t e = long_entry(b.w0, W, lane, lc.F, lc.maxlen);
+  if ((e & 31u) == 0) bad = true;
+  b.skip(e);
+  top_up(b, W, lane);
   return e;
 }
 
 // Table lookup of the code at the window head: exponent << 7 | length, or 0
-// when neither level holds it.  No branch.
+// when neither level holds it.  No branch: a prefix outside the second level
+// reads its all-zero last row, and a short code (first level) always has a
+// prefix below the escape rows, so at most one level is non-zero.
 __device__ __forceinline__ uint32_t lookup(const LaneBits& b, const WarpTabs& W, int lane,
                                           uint32_t L5) {
   const uint32_t h = b.w0;
   const uint32_t e1 = W.lut[h >> (32 - PK)][lane];
-  const uint32_t i2 = (h >> (32 - PK - K2)) - L5;
-  const uint32_t e2 = (NE > 0 && i2 < uint32_t(NE << K2)) ? uint32_t(W.lut2[i2][lane]) : 0u;
-  return e1 ? e1 : e2;
+  const uint32_t i2 = min((h >> (32 - PK - K2)) - L5, uint32_t(NE << K2));
+  return e1 | uint32_t(W.lut2[i2][lane]);
 }
 
-// One code with the rare path (used to redo a block that met a rare code).
+// One code with the rare path.
 __device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
                                        bool& bad) {
   const uint32_t e = lookup(b, W, lane, lc.L << K2);
@@ -377,30 +388,29 @@ __device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, cons
   return e;
 }
 
-// Four codes from a window holding >= 4*(PK+K2) bits, branch-free; a block
-// that meets a code neither level holds is rewound and redone code by code.
+// Four codes from a window holding >= 4*(PK+K2) bits, without a branch in the
+// common case.  A code neither level holds has entry 0, which skips no bits,
+// so the rest of the block looks up the same code and is 0 too: e3 == 0 tells
+// that the window stopped at such a code, and the block finishes code by code
+// from there.
 __device__ __forceinline__ void dec4(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
                                      bool& bad, uint32_t& e0, uint32_t& e1, uint32_t& e2,
                                      uint32_t& e3) {
-  const uint32_t s0 = b.w0, s1 = b.w1, s2 = b.w2;
-  const int snb = b.nb;
   const uint32_t L5 = lc.L << K2;
   e0 = lookup(b, W, lane, L5);
-  b.skip(e0);
+  b.shift(e0);
   e1 = lookup(b, W, lane, L5);
-  b.skip(e1);
+  b.shift(e1);
   e2 = lookup(b, W, lane, L5);
-  b.skip(e2);
+  b.shift(e2);
   e3 = lookup(b, W, lane, L5);
-  b.skip(e3);
-  if ((e0 == 0) | (e1 == 0) | (e2 == 0) | (e3 == 0)) {
-    b.w0 = s0;
-    b.w1 = s1;
-    b.w2 = s2;
-    b.nb = snb;
-    e0 = dec(b, W, lane, lc, bad);
-    e1 = dec(b, W, lane, lc, bad);
-    e2 = dec(b, W, lane, lc, bad);
+  b.shift(e3);
+  // lengths sit in bits 0-4 above zero bits 5-6, so one sum carries all four
+  b.nb -= int((e0 + e1 + e2 + e3) & 127u);
+  if (e3 == 0) {
+    if (e0 == 0) e0 = dec(b, W, lane, lc, bad);
+    if (e1 == 0) e1 = dec(b, W, lane, lc, bad);
+    if (e2 == 0) e2 = dec(b, W, lane, lc, bad);
     e3 = dec(b, W, lane, lc, bad);
   }
 }
@@ -446,8 +456,8 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
       uint32_t e[16];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        b.refill(W, lane);  // nb >= 65: four codes of <= PK+K2 bits
-        if (b.nb < 65) b.refill(W, lane);  // a block consumed more than a word
+        b.refill(W, lane);
+        if (b.nb < 4 * (PK + K2)) b.refill(W, lane);  // rare: four codes of <= PK+K2 bits
         dec4(b, W, lane, lc, bad, e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]);
       }
       const uint32_t r = (p >> 4) & 15, c = (p >> 8) * 16;

@@ -58,7 +58,7 @@ struct SerialShared {
       uint16_t pos[REC][ST];  // lookup start, relative to the thread's range start
       uint16_t cnt[REC][ST];  // codes counted before that lookup
     } rec;
-    uint8_t hist[ST / 32][256];  // rank scratch while building tables
+    uint8_t hist[8][256];  // rank scratch while building tables
   };
   uint32_t endpos[ST];  // relative end of each thread's walk (or kDead)
   uint32_t warpsum[ST / 32];
@@ -116,61 +116,84 @@ __device__ __forceinline__ uint32_t code1(const SH& S, SmemWin96& r, bool& dead)
   return uint32_t(sym) << XS;
 }
 
-// Four codes from a window holding >= 4*SK bits, branch-free; a block that
-// meets a code longer than SK bits is rewound and redone code by code.
+// Four codes from a window holding >= 4*SK bits, without a branch in the
+// common case.  A code the table does not hold has entry 0, which skips no
+// bits, so every later lookup of the block sees the same code and is 0 too:
+// the window stops at the first such code, and e3 == 0 tells that one did.
+// Those codes are then decoded one by one from where the window stopped.
 template <int XS, class SH>
 __device__ __forceinline__ void code4(const SH& S, SmemWin96& r, bool& dead, uint32_t& e0,
                                       uint32_t& e1, uint32_t& e2, uint32_t& e3) {
-  const SmemWin96 s = r;
   e0 = S.lut[r.w0 >> (32 - SK)];
-  r.skip(e0);
+  r.shift(e0);
   e1 = S.lut[r.w0 >> (32 - SK)];
-  r.skip(e1);
+  r.shift(e1);
   e2 = S.lut[r.w0 >> (32 - SK)];
-  r.skip(e2);
+  r.shift(e2);
   e3 = S.lut[r.w0 >> (32 - SK)];
-  r.skip(e3);
-  if ((e0 == 0) | (e1 == 0) | (e2 == 0) | (e3 == 0)) {
-    r = s;
-    e0 = code1<XS>(S, r, dead);
-    r.refill();
-    e1 = code1<XS>(S, r, dead);
-    r.refill();
-    e2 = code1<XS>(S, r, dead);
-    r.refill();
+  r.shift(e3);
+  // lengths sit in bits 0-4 above zero bits, so one sum carries all four
+  r.nb -= int((e0 + e1 + e2 + e3) & 127u);
+  if (e3 == 0) {
+    if (e0 == 0) {
+      e0 = code1<XS>(S, r, dead);
+      r.refill();
+    }
+    if (e1 == 0) {
+      e1 = code1<XS>(S, r, dead);
+      r.refill();
+    }
+    if (e2 == 0) {
+      e2 = code1<XS>(S, r, dead);
+      r.refill();
+    }
     e3 = code1<XS>(S, r, dead);
   }
 }
 
-// Builds canonical tables for the slab's code lengths.  Returns false for an
-// oversubscribed codebook.
-template <int XS, bool COUNT_TABLE, class SH>
+// Builds canonical tables for the slab's code lengths with NT threads (128 or
+// 256).  Returns false for an oversubscribed codebook.
+template <int XS, bool COUNT_TABLE, int NT = ST, class SH>
 __device__ bool build_tables(SH& S, const uint8_t* lens) {
+  constexpr int NW = NT / 32, R = 256 / NT, E = 256 / NT;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  S.cnt[t] = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j) S.cnt[t * E + j] = 0;
   if (t == 0) {
     S.maxlen = 0;
     S.minlen = 256;
   }
   uint8_t* hist = &S.hist[0][0];
-  for (int k = t; k < (ST / 32) * 256; k += ST) hist[k] = 0;
+  for (int k = t; k < 8 * 256; k += NT) hist[k] = 0;
   __syncthreads();
-  const int l = __ldg(lens + t);
-  // per-length counts (16-bit fields) via 32-bit atomics on the containing word
-  if (l) {
-    uint32_t* w = reinterpret_cast<uint32_t*>(&S.cnt[l & ~1]);
-    atomicAdd(w, (l & 1) ? 0x10000u : 1u);
-    atomicMax(&S.maxlen, l);
-    atomicMin(&S.minlen, l);
+  // symbol chunk c = j * NW + warp holds symbols 32c .. 32c + 31
+  int l[R];
+  uint32_t rank_w[R];
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = j * NW + warp;
+    l[j] = __ldg(lens + 32 * c + lane);
+    // per-length counts (16-bit fields) via 32-bit atomics on the containing word
+    if (l[j]) {
+      uint32_t* w = reinterpret_cast<uint32_t*>(&S.cnt[l[j] & ~1]);
+      atomicAdd(w, (l[j] & 1) ? 0x10000u : 1u);
+      atomicMax(&S.maxlen, l[j]);
+      atomicMin(&S.minlen, l[j]);
+    }
+    // rank of the symbol among earlier symbols of its chunk with the same length
+    const uint32_t same = __match_any_sync(0xffffffffu, l[j]);
+    rank_w[j] = __popc(same & ((1u << lane) - 1));
+    if (l[j] && rank_w[j] == 0) S.hist[c][l[j]] = uint8_t(__popc(same));
   }
-  // rank of symbol t among earlier symbols with the same length
-  const uint32_t same = __match_any_sync(0xffffffffu, l);
-  const uint32_t rank_w = __popc(same & ((1u << lane) - 1));
-  if (l && rank_w == 0) S.hist[warp][l] = uint8_t(__popc(same));
   __syncthreads();
-  // offs[] = exclusive scan of cnt[] (one length per thread)
-  const uint32_t c = S.cnt[t];
-  uint32_t v = c;
+  // offs[] = exclusive scan of cnt[] (E consecutive lengths per thread)
+  uint32_t cl[E], tsum = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    cl[j] = S.cnt[t * E + j];
+    tsum += cl[j];
+  }
+  uint32_t v = tsum;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
     const uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
@@ -180,8 +203,13 @@ __device__ bool build_tables(SH& S, const uint8_t* lens) {
   __syncthreads();
   uint32_t pre = 0;
   for (int w = 0; w < warp; ++w) pre += S.warpsum[w];
-  S.offs[t] = uint16_t(pre + v - c);
-  if (t == ST - 1) S.offs[256] = uint16_t(pre + v);
+  uint32_t run = pre + v - tsum;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    S.offs[t * E + j] = uint16_t(run);
+    run += cl[j];
+  }
+  if (t == NT - 1) S.offs[256] = uint16_t(run);
   if (t == 0) {
     int64_t avail = 1;  // Kraft check: open prefixes per level, clamped past 256
     bool ok = true;
@@ -203,14 +231,18 @@ __device__ bool build_tables(SH& S, const uint8_t* lens) {
   }
   __syncthreads();
   if (S.flag) return false;
-  if (l) {
-    uint32_t r = rank_w;
-    for (int w = 0; w < warp; ++w) r += S.hist[w][l];
-    S.sorted[S.offs[l] + r] = uint8_t(t);
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = j * NW + warp;
+    if (l[j]) {
+      uint32_t r = rank_w[j];
+      for (int w = 0; w < c; ++w) r += S.hist[w][l[j]];
+      S.sorted[S.offs[l[j]] + r] = uint8_t(32 * c + lane);
+    }
   }
   __syncthreads();
   // single-code table: thread t fills entries [PER*t, PER*t + PER)
-  constexpr int PER = (1 << SK) / ST;
+  constexpr int PER = (1 << SK) / NT;
   int len = S.minlen;
   for (int k = 0; k < PER; ++k) {
     const uint32_t e = uint32_t(t * PER + k);
@@ -226,7 +258,7 @@ __device__ bool build_tables(SH& S, const uint8_t* lens) {
   __syncthreads();
   if constexpr (COUNT_TABLE) {
   // count table: the whole codes inside each CK-bit window
-  constexpr int CPER = (1 << CK) / ST;
+  constexpr int CPER = (1 << CK) / NT;
   for (int k = 0; k < CPER; ++k) {
     const uint32_t v0 = uint32_t(t * CPER + k);
     uint32_t used = 0, n = 0;
@@ -381,7 +413,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
         uint32_t pos = st0;
         bool go = true;
         while (go) {
-          r.refill2();  // >= 65 bits: four lookups of <= SK bits
+          r.refill_to<4 * SK>();  // four lookups of <= SK bits
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             if (go) {
@@ -511,9 +543,9 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
             for (; g + 8 <= gend; g += 8) {
               const uint64_t s8 = smr.take();
               uint32_t e[8];
-              r.refill2();
+              r.refill_to<4 * SK>();
               code4<7>(S, r, dead, e[0], e[1], e[2], e[3]);
-              r.refill2();
+              r.refill_to<4 * SK>();
               code4<7>(S, r, dead, e[4], e[5], e[6], e[7]);
               const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
               const uint32_t rr = (g >> 4) & 15, c = (g >> 8) * 16 + (g & 15);
@@ -607,7 +639,7 @@ struct GemvShared {
   uint16_t offs[257];
   uint8_t sorted[256];
   alignas(16) uint32_t win[GWINW];
-  uint8_t hist[GT / 32][256];
+  uint8_t hist[8][256];
   uint32_t warpsum[GT / 32];
   float red[16][GT / 32][GNB];
   int maxlen, minlen, flag;
@@ -623,6 +655,33 @@ __device__ __forceinline__ float wfloat(uint32_t e, uint32_t sw) {
   return __uint_as_float((s & 0x807FFFFFu) | (e & 0x7F800000u));
 }
 
+// acc[b] += w(e_k, byte k of sw) * x[4q + k][b] for the block's four codes;
+// xr holds the tile's 16 x values when NB == 1, else x is read at xc (row
+// stride ld) for the nb active columns.
+template <int NB>
+__device__ __forceinline__ void fma4(float* acc, uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3,
+                                     uint32_t sw, const float* xr4, const float* xc, uint32_t ld,
+                                     uint32_t nb) {
+  const float w0 = wfloat<0>(e0, sw), w1 = wfloat<1>(e1, sw);
+  const float w2 = wfloat<2>(e2, sw), w3 = wfloat<3>(e3, sw);
+  if (NB == 1) {
+    acc[0] = fmaf(w0, xr4[0], acc[0]);
+    acc[0] = fmaf(w1, xr4[1], acc[0]);
+    acc[0] = fmaf(w2, xr4[2], acc[0]);
+    acc[0] = fmaf(w3, xr4[3], acc[0]);
+  } else {
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (uint32_t(b) < nb) {
+        acc[b] = fmaf(w0, __ldg(xc + b), acc[b]);
+        acc[b] = fmaf(w1, __ldg(xc + ld + b), acc[b]);
+        acc[b] = fmaf(w2, __ldg(xc + 2 * ld + b), acc[b]);
+        acc[b] = fmaf(w3, __ldg(xc + 3 * ld + b), acc[b]);
+      }
+    }
+  }
+}
+
 template <int NB>
 __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -634,7 +693,7 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const uint8_t* p = a.payload + sd.src;
     const uint32_t count = uint32_t(sd.rows * sd.cols);
     const uint32_t nbits = uint32_t(ld_le64(p + 8));
-    if (!build_tables<23, false>(S, p + 16)) {  // validated when the index was built
+    if (!build_tables<23, false, GT>(S, p + 16)) {  // validated when the index was built
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       __syncthreads();
       continue;
@@ -665,7 +724,12 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
         for (int q = 0; q < 16; ++q) xr[q] = __ldg(xs + q * a.ld);
       }
     }
-    const uint8_t* smt = sm + uint64_t(tile) * 256;
+    // the tile's 256 sign/mantissa bytes, one 16-byte row per step from
+    // aligned 16-byte loads (the misalignment is the same for the whole slab;
+    // the chunk past the tile is the slab's next bytes, so loads stay inside)
+    const uintptr_t sma = reinterpret_cast<uintptr_t>(sm + uint64_t(tile) * 256);
+    const int soff = int(sma & 15);
+    const uint4* sq = reinterpret_cast<const uint4*>(sma & ~uintptr_t(15));
     uint32_t ta = 0;
     while (ta < it.ntiles) {  // rounds (one, unless the tiles' bits exceed GCAP)
       const uint32_t base_bit = ti[it.tile0 + ta] & ~31u;
@@ -697,7 +761,13 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
       SmemWin96 r;
       r.init(S.win, act ? b0 - base_bit : 0u);
       bool dead = false;
+      // sign/mantissa rows loaded one row ahead of use
+      uint4 nlo = ldg16(sq), nhi = soff ? ldg16(sq + 1) : make_uint4(0, 0, 0, 0);
       for (int row = 0; row < 16; ++row) {
+        const uint4 lo = nlo, hi = nhi;
+        const int nr = row < 15 ? row + 1 : 15;
+        nlo = ldg16(sq + nr);
+        if (soff) nhi = ldg16(sq + nr + 1);
         float acc[NB];
 #pragma unroll
         for (int b = 0; b < NB; ++b) acc[b] = 0.f;
@@ -707,32 +777,14 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
           act = false;
         }
         if (act) {
-          const uint4 s16 = ld16_any(smt + row * 16);
+          const uint4 s16 = realign16(lo, hi, soff);
           const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t e0, e1, e2, e3;
-            r.refill2();
+            r.refill_to<4 * SK>();
             code4<23>(S, r, dead, e0, e1, e2, e3);
-            const float w0 = wfloat<0>(e0, sw[q]), w1 = wfloat<1>(e1, sw[q]);
-            const float w2 = wfloat<2>(e2, sw[q]), w3 = wfloat<3>(e3, sw[q]);
-            if (NB == 1) {
-              acc[0] = fmaf(w0, xr[4 * q], acc[0]);
-              acc[0] = fmaf(w1, xr[4 * q + 1], acc[0]);
-              acc[0] = fmaf(w2, xr[4 * q + 2], acc[0]);
-              acc[0] = fmaf(w3, xr[4 * q + 3], acc[0]);
-            } else {
-              const float* xc = xs + uint64_t(4 * q) * a.ld;
-#pragma unroll
-              for (int b = 0; b < NB; ++b) {
-                if (uint32_t(b) < a.nb) {
-                  acc[b] = fmaf(w0, __ldg(xc + b), acc[b]);
-                  acc[b] = fmaf(w1, __ldg(xc + a.ld + b), acc[b]);
-                  acc[b] = fmaf(w2, __ldg(xc + 2 * a.ld + b), acc[b]);
-                  acc[b] = fmaf(w3, __ldg(xc + 3 * a.ld + b), acc[b]);
-                }
-              }
-            }
+            fma4<NB>(acc, e0, e1, e2, e3, sw[q], xr + 4 * q, xs + uint64_t(4 * q) * a.ld, a.ld, a.nb);
           }
         }
 #pragma unroll

@@ -269,17 +269,20 @@ struct SmemWin96 {
     nb = 96 - int(sb);
     wi = k + 3;
   }
-  // Appends the next word when nb <= 64, without a data-dependent branch.
+  // Appends the next word when nb <= 64, without a branch (the word past the
+  // window is always readable: callers keep padding words after their data).
   __device__ __forceinline__ void refill() {
     const bool need = nb <= 64;
-    const uint32_t t = need ? win[wi] : 0u;
+    const uint32_t word = win[wi];  // unconditional load (in bounds), then a select
+    const uint32_t t = need ? word : 0u;
     const bool low = nb < 32;
-    const uint32_t sh = need ? uint32_t(low ? 32 - nb : 64 - nb) : 0u;
-    const uint64_t v = uint64_t(t) << sh;
-    const uint32_t a = uint32_t(v >> 32), c = uint32_t(v);
-    w0 |= low ? a : 0u;
-    w1 |= low ? c : a;
-    w2 |= low ? 0u : c;
+    // t lands at bit nb: its head ORs into w0 (nb < 32) or w1, its tail into
+    // the next word; clamped funnel shifts keep every nb well defined
+    const uint32_t k = uint32_t(low ? nb : nb - 32);
+    const uint32_t head = __funnelshift_rc(t, 0u, k), tail = __funnelshift_rc(0u, t, k);
+    w0 |= low ? head : 0u;
+    w1 |= low ? tail : head;
+    w2 |= low ? 0u : tail;
     nb += need ? 32 : 0;
     wi += need ? 1u : 0u;
   }
@@ -288,14 +291,42 @@ struct SmemWin96 {
     refill();
     if (nb < 65) refill();
   }
+  // nb >= NEED (<= 64) afterwards from any nb >= 1; the second word is
+  // rarely needed, so the branch is almost always uniform.
+  template <int NEED>
+  __device__ __forceinline__ void refill_to() {
+    refill();
+    if (nb < NEED) refill();
+  }
   __device__ __forceinline__ void skip(uint32_t n) {  // uses the low 5 bits of n
     w0 = __funnelshift_l(w1, w0, n);
     w1 = __funnelshift_l(w2, w1, n);
     w2 = __funnelshift_l(0u, w2, n);
     nb -= int(n & 31u);
   }
+  // Shift only; the caller subtracts the consumed bits from nb later.
+  __device__ __forceinline__ void shift(uint32_t n) {
+    w0 = __funnelshift_l(w1, w0, n);
+    w1 = __funnelshift_l(w2, w1, n);
+    w2 = __funnelshift_l(0u, w2, n);
+  }
   __device__ __forceinline__ uint32_t pos() const { return 32 * wi - uint32_t(nb); }
 };
+
+// The 16 bytes at byte offset off (0..15) of the 32 bytes lo:hi.
+__device__ __forceinline__ uint4 realign16(const uint4& lo, const uint4& hi, int off) {
+  if (off == 0) return lo;
+  uint32_t w0 = lo.x, w1 = lo.y, w2 = lo.z, w3 = lo.w, w4 = hi.x, w5 = hi.y, w6 = hi.z, w7 = hi.w;
+  if (off & 8) {
+    w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
+  }
+  if (off & 4) {
+    w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
+  }
+  const int bs = (off & 3) * 8;
+  return make_uint4(__funnelshift_r(w0, w1, bs), __funnelshift_r(w1, w2, bs),
+                    __funnelshift_r(w2, w3, bs), __funnelshift_r(w3, w4, bs));
+}
 
 // 16 bytes from any address (two aligned loads and a byte funnel).
 __device__ __forceinline__ uint4 ld16_any(const uint8_t* p) {
