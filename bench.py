@@ -68,10 +68,13 @@ def host_threads(world):
     return max(1, n // max(1, world))
 
 
-def build_archive(tensors, codec, sigma, seed, device, threads, only_kinds=("w", "norm")):
+def build_archive(tensors, codec, sigma, seed, device, threads, only_kinds=("w", "norm"),
+                  row_range=None):
     """Generates the seeded BF16 tensors on the GPU, compiles them on the host
     with the library's encoder, returns (payload uint8 numpy, slabs, out_bytes,
-    per-tensor info)."""
+    per-tensor info).  `row_range(rows) -> (r0, r1)` keeps only those rows of
+    every tensor (a tensor-parallel shard; the full tensors are generated so
+    every rank sees the same weights)."""
     import numpy as np
     import torch
     import xksv_gpu
@@ -86,6 +89,10 @@ def build_archive(tensors, codec, sigma, seed, device, threads, only_kinds=("w",
             t = torch.ones(rows, cols, dtype=torch.bfloat16, device=device)
         else:
             t = (torch.randn(rows, cols, generator=gen, device=device) * sigma).to(torch.bfloat16)
+        if row_range is not None:
+            r0, r1 = row_range(rows)
+            t = t[r0:r1].contiguous()
+            rows = r1 - r0
         h = t.view(torch.int16).cpu().numpy()
         pay, sl = xksv_gpu.host_pack_tensor(h.ctypes.data, h.nbytes, rows, cols, codec,
                                             threads=threads, dst_base=dst)
@@ -408,6 +415,81 @@ def run_case(args):
     print(json.dumps(line), flush=True)
 
 
+def tp_gemv(args, dev, stream, threads, rank, world):
+    """Tensor-parallel batch-1 fused GEMV over every linear of the
+    Llama-3-8B-shaped model: each rank encodes and holds only its row shard
+    of every weight (whole 16-row slabs), and per layer runs four fused plan
+    GEMVs (qkv, o, gate+up, down) each followed by one NCCL all-gather of the
+    output shards (xksv_tp_gemm).  Timed on the device, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import xksv_gpu
+
+    cfg = CONFIG3
+    tensors = [t for t in llama_tensors(**cfg) if t[3] == "w" and ("layers." in t[0])]
+    payload, slabs, _, info = build_archive(
+        tensors, 1, 0.02, 2, dev, threads, row_range=lambda rows: xksv_gpu.shard_rows(rows, world, rank))
+    d_payload = torch.from_numpy(payload).to(dev)
+    name_to = {i["name"]: i for i in info}
+    comm = xksv_gpu.TPComm(rank, world)
+    groups, xs = [], 0
+    for L in range(cfg["layers"]):
+        p = f"model.layers.{L}."
+        for members in ([p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight", p + "self_attn.v_proj.weight"],
+                        [p + "self_attn.o_proj.weight"],
+                        [p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"],
+                        [p + "mlp.down_proj.weight"]):
+            cols = name_to[members[0]]["cols"]
+            entries, yl = [], 0
+            for m in members:
+                t = name_to[m]
+                for sl in slabs[t["first"]:t["first"] + t["n"]]:
+                    e = dict(sl)
+                    e["dst_offset"] = yl + (sl["dst_offset"] - t["dst"]) // (2 * t["cols"])
+                    e["x_offset"] = xs
+                    entries.append(e)
+                yl += t["rows"]
+            plan = xksv_gpu.Plan(entries)
+            if plan.index(d_payload.data_ptr(), stream.cuda_stream):
+                raise RuntimeError("xksv_plan_index failed")
+            groups.append(dict(plan=plan, rows=yl, y=torch.empty(yl, device=dev),
+                               yfull=torch.empty(world * yl, device=dev)))
+            xs += cols
+    x = torch.randn(xs, generator=torch.Generator(device=dev).manual_seed(3), device=dev).to(torch.bfloat16).float()
+    h = stream.cuda_stream
+
+    def forward():
+        for g in groups:
+            comm.gemm(g["plan"], d_payload.data_ptr(), x.data_ptr(), g["y"].data_ptr(), g["rows"],
+                      g["yfull"].data_ptr(), 1, h)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            forward()
+    stream.synchronize()
+    bad = sum(g["plan"].status(h) for g in groups)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        t = time_steps(forward, args.gemv_steps, stream)
+    bad += sum(g["plan"].status(h) for g in groups)
+    tt = torch.tensor([t], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t = float(tt.item())
+    # the all-gather placed every rank's shard at its rank's block
+    g0 = groups[-1]
+    own = bool(torch.equal(g0["yfull"][rank * g0["rows"]:(rank + 1) * g0["rows"]], g0["y"]))
+    for g in groups:
+        g["plan"].close()
+    comm.close()
+    ms = t / args.gemv_steps * 1e3
+    return dict(metric="TP fused-GEMV tok/s Llama-8B b=1", value=round(1e3 / ms, 2), unit="tok/s",
+                ms_per_token=round(ms, 4), n_gpus=world, compressed_bytes_per_rank=int(payload.nbytes),
+                launches_per_token=len(groups), all_gathers_per_token=len(groups),
+                status_errors=int(bad), own_shard_gathered=own,
+                note="rows sharded per GPU in whole slabs; xksv_tp_gemm = fused plan GEMV + ncclAllGather")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -540,6 +622,14 @@ def main():
         te = float(tt.item())
     e2e_val = world * out_bytes * e2e_steps / te / 1e9
 
+    tp = None
+    if not args.no_gemv and world > 1:
+        del d_out
+        torch.cuda.empty_cache()
+        try:
+            tp = tp_gemv(args, dev, stream, threads, rank, world)
+        except Exception as ex:  # reported, never silently replaced
+            tp = dict(error=f"{type(ex).__name__}: {ex}")
     gemv = None
     if not args.no_gemv and rank == 0 and world == 1:
         del d_out
@@ -583,7 +673,7 @@ def main():
             e2e=dict(value=round(e2e_val, 2), unit="GB/s", h2d_bytes_per_step=comp_bytes,
                      d2h_bytes_per_step=4, steps=e2e_steps,
                      path="pinned host payload -> cudaMemcpyAsync -> xksv_plan_decode -> xksv_plan_status"),
-            clocks=clocks, gpu_launches=launches, fused_gemv=gemv)
+            clocks=clocks, gpu_launches=launches, fused_gemv=gemv, tp_fused_gemv=tp)
         print(json.dumps(line), flush=True)
     plan.close()
     par_plan.close()

@@ -159,6 +159,31 @@ int xksv_host_pack_tensor(const void* data, size_t nbytes, size_t rows, size_t c
 int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload,
                              void* d_out, void* stream);
 
+/* ---------------- Part 5: tensor-parallel fused GEMV / GEMM ------------- */
+/* One process per GPU; each rank's plan holds the slabs of its own rows
+ * [g*R/G, (g+1)*R/G) of W with dst_offset rebased to the shard's first row.
+ * No reference counterpart (the reference has no multi-GPU path); the NCCL
+ * library is opened at run time (libnccl.so.2, reusing an already loaded
+ * copy), so these return 1 when it is absent. */
+#define XKSV_TP_ID_BYTES 128
+
+/* A fresh NCCL unique id (XKSV_TP_ID_BYTES bytes) for xksv_tp_comm_create:
+ * made by one rank and sent to the others by the caller. 0 or 1. */
+int xksv_tp_unique_id(void* id);
+
+/* Collective over nranks processes: creates this rank's communicator on the
+ * current CUDA device.  0 or 1. */
+int xksv_tp_comm_create(const void* id, int nranks, int rank, void** comm);
+void xksv_tp_comm_destroy(void* comm);
+
+/* Enqueues on `stream`: d_y_shard[rows_shard, batch] = W_shard X (the fused
+ * plan GEMM), then one all-gather of every rank's shard into
+ * d_y_full[nranks * rows_shard, batch] (rank order = row order; all ranks
+ * pass the same rows_shard).  Returns 1 only for launch errors; slab errors
+ * are read with xksv_plan_status. */
+int xksv_tp_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y_shard,
+                 size_t rows_shard, float* d_y_full, size_t batch, void* comm, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

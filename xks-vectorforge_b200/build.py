@@ -14,7 +14,8 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libxksv_cuda.so"
-SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu", "pack_host.cpp", "noalloc.cu"]
+SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu", "pack_host.cpp", "noalloc.cu",
+           "tp.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -29,7 +30,7 @@ def build(verbose=False, force=False):
     if LIB.exists() and not force and all(LIB.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return LIB
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-pthread",
-           "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp", *map(str, srcs)]
+           "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp", *map(str, srcs), "-ldl"]
     if verbose:
         cmd[1:1] = ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -45,6 +45,13 @@ _SIGS = {
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_unique_id": ([ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_comm_create": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                             ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "xksv_tp_comm_destroy": ([ctypes.c_void_p], None),
+    "xksv_tp_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                      ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                      ctypes.c_void_p], ctypes.c_int),
     "xksv_host_pack": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                         ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                         ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
@@ -176,3 +183,87 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------- tensor parallel
+TP_ID_BYTES = 128
+
+
+def shard_rows(rows, world, rank, align=16):
+    """Row range [r0, r1) of `rank` when `rows` rows are split over `world`
+    ranks in whole 16-row slabs (the first ranks take one slab more when the
+    slab count does not divide)."""
+    nslab = (rows + align - 1) // align
+    base, extra = divmod(nslab, world)
+    s0 = rank * base + min(rank, extra)
+    s1 = s0 + base + (1 if rank < extra else 0)
+    return min(rows, s0 * align), min(rows, s1 * align)
+
+
+def shard_entries(entries, world, rank, rows_of):
+    """The slab entries of this rank's rows, for TP GEMV/GEMM.
+
+    `entries` are GEMV slab entries whose dst_offset is the slab's first row
+    in the full Y (a plan may cover several tensors); `rows_of(e)` gives the
+    (first row, row count) of the tensor the slab belongs to.  Each tensor is
+    split separately with shard_rows; returns (local entries with dst_offset
+    rebased to the rank's shard of Y, rows in the shard, and the list of
+    (full_row0, local_row0, nrows) runs that map the shard back)."""
+    out, runs, local = [], [], 0
+    seen = {}
+    for e in entries:
+        t0, trows = rows_of(e)
+        if t0 not in seen:
+            r0, r1 = shard_rows(trows, world, rank)
+            seen[t0] = (r0, r1, local)
+            runs.append((t0 + r0, local, r1 - r0))
+            local += r1 - r0
+        r0, r1, l0 = seen[t0]
+        row = e["dst_offset"] - t0
+        if r0 <= row < r1:
+            d = dict(e)
+            d["dst_offset"] = l0 + row - r0
+            out.append(d)
+    return out, local, runs
+
+
+def gathered_to_full(gathered, world, runs_per_rank, rows_shard):
+    """Row indices: full_row -> row of the all-gathered buffer
+    ([world * rows_shard] rows in rank order), from each rank's runs."""
+    import numpy as np
+    total = sum(n for runs in runs_per_rank for _, _, n in runs)
+    idx = np.empty(total, dtype=np.int64)
+    for g, runs in enumerate(runs_per_rank):
+        for full0, local0, n in runs:
+            idx[full0:full0 + n] = g * rows_shard + local0 + np.arange(n)
+    return idx
+
+
+class TPComm:
+    """NCCL communicator for xksv_tp_gemm over the ranks of a torch.distributed
+    group (which only carries the unique id)."""
+
+    def __init__(self, rank, world, lib=None):
+        import torch.distributed as dist
+        self.lib = lib or load()
+        uid = ctypes.create_string_buffer(TP_ID_BYTES)
+        if rank == 0 and self.lib.xksv_tp_unique_id(uid):
+            raise RuntimeError("xksv_tp_unique_id failed (NCCL not available?)")
+        obj = [bytes(uid.raw) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = ctypes.create_string_buffer(obj[0], TP_ID_BYTES)
+        h = ctypes.c_void_p()
+        if self.lib.xksv_tp_comm_create(uid, world, rank, ctypes.byref(h)):
+            raise RuntimeError("xksv_tp_comm_create failed")
+        self.handle = h
+        self.rank, self.world = rank, world
+
+    def gemm(self, plan, d_payload, d_x, d_y_shard, rows_shard, d_y_full, batch, stream=0):
+        if self.lib.xksv_tp_gemm(plan.handle, d_payload, d_x, d_y_shard, rows_shard, d_y_full,
+                                 batch, self.handle, stream):
+            raise RuntimeError("xksv_tp_gemm failed")
+
+    def close(self):
+        if self.handle:
+            self.lib.xksv_tp_comm_destroy(self.handle)
+            self.handle = None
