@@ -191,6 +191,15 @@ struct xksv_plan {
   uint32_t n_items = 0;
   float* d_partials = nullptr;
   uint32_t* d_counters = nullptr;
+  // tensor-core GEMM path (batch >= 16): the plan's slabs decoded into BF16
+  // row groups of <= 128 rows in a scratch buffer, then tcgen05 GEMM
+  bool tc_ok = false;
+  uint32_t ngroups = 0, tc_ksplit = 1;
+  xksv::TcGroup* d_groups = nullptr;
+  xksv::Slab* d_tc_slabs = nullptr;  // d_slabs with dst = scratch byte offsets
+  uint64_t scratch_bytes = 0, x_cols = 0;
+  uint8_t* d_scratch = nullptr;
+  void* d_xt = nullptr;  // BF16 X^T [256][x_cols]
 };
 
 namespace {
@@ -211,6 +220,48 @@ void free_index(xksv_plan* p) {
 
 bool tile_indexable(const xksv::Slab& s) {
   return s.rows == 16 && s.cols % 16 == 0 && s.cols < (1ull << 27);
+}
+
+// Row groups for the tensor-core GEMM: slabs sharing X columns (x_offset,
+// cols) whose output rows are contiguous, up to 128 rows per group; fills
+// the scratch slab table (same order as `all`).  False when a slab is not
+// 16-byte aligned for cp.async (cols or x_offset not a multiple of 8).
+bool build_tc_groups(const std::vector<xksv::Slab>& all, std::vector<xksv::TcGroup>& groups,
+                     std::vector<xksv::Slab>& tc_slabs, uint64_t& scratch, uint64_t& x_cols) {
+  using xksv::Slab;
+  const size_t n = all.size();
+  if (!n) return false;
+  for (const Slab& s : all)
+    if (s.cols % 8 || s.xoff % 8 || !s.rows || s.rows > 128 || s.cols >= (1u << 31)) return false;
+  std::vector<size_t> idx(n);
+  for (size_t i = 0; i < n; ++i) idx[i] = i;
+  std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) {
+    const Slab &x = all[a], &y = all[b];
+    if (x.xoff != y.xoff) return x.xoff < y.xoff;
+    if (x.cols != y.cols) return x.cols < y.cols;
+    return x.dst < y.dst;
+  });
+  tc_slabs = all;
+  scratch = 0;
+  x_cols = 0;
+  xksv::TcGroup cur{};
+  bool open = false;
+  for (size_t k = 0; k < n; ++k) {
+    const Slab& s = all[idx[k]];
+    x_cols = std::max<uint64_t>(x_cols, s.xoff + s.cols);
+    const bool extend = open && s.xoff == cur.xoff && s.cols == cur.cols &&
+                        s.dst == cur.y_row0 + cur.rows && cur.rows + s.rows <= 128;
+    if (!extend) {
+      if (open) groups.push_back(cur);
+      cur = xksv::TcGroup{scratch, s.dst, s.xoff, 0, uint32_t(s.cols)};
+      open = true;
+    }
+    tc_slabs[idx[k]].dst = cur.a_off + uint64_t(cur.rows) * s.cols * 2;
+    cur.rows += uint32_t(s.rows);
+    scratch += s.rows * s.cols * 2;
+  }
+  groups.push_back(cur);
+  return true;
 }
 }  // namespace
 
@@ -306,7 +357,6 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   p->n_ser_idx = uint32_t(std::count_if(ser.begin(), ser.end(), tile_indexable));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
-  (void)sms;
   // one CTA per slab (per PWARPS slabs for the parallel codec): the block
   // scheduler balances slabs of different cost
   p->grid_ser = 1 << 30;
@@ -328,6 +378,24 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
     ok = cudaMalloc(&p->d_slabs, n * sizeof(Slab)) == cudaSuccess &&
          cudaMemcpy(p->d_slabs, all.data(), n * sizeof(Slab), cudaMemcpyHostToDevice) == cudaSuccess;
   }
+  // tensor-core GEMM groups (raw slabs must hold exactly rows * cols BF16)
+  {
+    std::vector<TcGroup> groups;
+    std::vector<Slab> tc_slabs;
+    if (ok && raw_gemm_ok && build_tc_groups(all, groups, tc_slabs, p->scratch_bytes, p->x_cols)) {
+      p->ngroups = uint32_t(groups.size());
+      uint32_t minch = ~0u;
+      for (const TcGroup& g : groups) minch = std::min<uint32_t>(minch, (g.cols + 63) / 64);
+      const uint32_t want = (2 * uint32_t(sms) + p->ngroups - 1) / p->ngroups;
+      p->tc_ksplit = std::max<uint32_t>(1, std::min<uint32_t>(want, minch));
+      p->tc_ok = cudaMalloc(&p->d_groups, groups.size() * sizeof(TcGroup)) == cudaSuccess &&
+                 cudaMalloc(&p->d_tc_slabs, n * sizeof(Slab)) == cudaSuccess &&
+                 cudaMemcpy(p->d_groups, groups.data(), groups.size() * sizeof(TcGroup),
+                            cudaMemcpyHostToDevice) == cudaSuccess &&
+                 cudaMemcpy(p->d_tc_slabs, tc_slabs.data(), n * sizeof(Slab), cudaMemcpyHostToDevice) ==
+                     cudaSuccess;
+    }
+  }
   // the copies above ran on the legacy default stream, which callers' non-blocking
   // streams do not wait for: finish them before the plan is used anywhere
   ok = ok && cudaStreamSynchronize(nullptr) == cudaSuccess;
@@ -343,6 +411,10 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
 void xksv_plan_destroy(xksv_plan* p) {
   if (!p) return;
   free_index(p);
+  if (p->d_groups) cudaFree(p->d_groups);
+  if (p->d_tc_slabs) cudaFree(p->d_tc_slabs);
+  if (p->d_scratch) cudaFree(p->d_scratch);
+  if (p->d_xt) cudaFree(p->d_xt);
   if (p->d_slabs) cudaFree(p->d_slabs);
   if (p->d_status) cudaFree(p->d_status);
   if (p->h_status) cudaFreeHost(p->h_status);
@@ -383,6 +455,45 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
   p->launches = 0;
   cudaError_t e = cudaSuccess;
   const uint32_t ld = uint32_t(batch);
+  if (batch >= 16 && p->tc_ok) {
+    // decode every slab into its BF16 row group, then the tensor-core GEMM,
+    // up to 256 batch columns per pass over the same decoded scratch
+    if (!p->d_scratch && cudaMalloc(&p->d_scratch, std::max<uint64_t>(16, p->scratch_bytes)) != cudaSuccess)
+      return 1;
+    if (!p->d_xt && cudaMalloc(&p->d_xt, 256 * p->x_cols * 2) != cudaSuccess) return 1;
+    if (p->n_ser) {
+      e = launch_serial_decode(p->d_tc_slabs, p->n_ser, pay, p->d_scratch, p->d_status, p->grid_ser, st);
+      ++p->launches;
+    }
+    if (e == cudaSuccess && p->n_par) {
+      e = launch_parallel_decode(p->d_tc_slabs + p->n_ser, p->n_par, pay, p->d_scratch, p->d_status,
+                                 p->grid_par, st);
+      ++p->launches;
+    }
+    if (e == cudaSuccess && p->n_raw) {
+      e = launch_raw_decode(p->d_tc_slabs + p->n_ser + p->n_par, p->n_raw, pay, p->d_scratch,
+                            p->grid_raw, st);
+      ++p->launches;
+    }
+    for (size_t b0 = 0; b0 < batch && e == cudaSuccess; b0 += 256) {
+      TcGemmArgs g{};
+      g.groups = p->d_groups;
+      g.scratch = p->d_scratch;
+      g.xt = p->d_xt;
+      g.xt_ld = p->x_cols;
+      g.y = d_y + b0;
+      g.ld = ld;
+      g.nb = uint32_t(std::min<size_t>(256, batch - b0));
+      g.npad = (g.nb + 15) / 16 * 16;
+      g.ksplit = p->tc_ksplit;
+      g.tmem_cols = 32;
+      while (g.tmem_cols < g.npad) g.tmem_cols *= 2;
+      g.status = p->d_status;
+      e = launch_tc_gemm(g, p->ngroups, d_x + b0, p->x_cols, st);
+      p->launches += g.ksplit > 1 ? 3 : 2;
+    }
+    return e == cudaSuccess ? 0 : 1;
+  }
   // indexed serial slabs: tile-parallel kernel, 4 batch columns per pass
   const bool indexed = p->d_tidx && d_payload == p->indexed_payload;
   const uint32_t ser0 = indexed ? p->n_ser_idx : 0;

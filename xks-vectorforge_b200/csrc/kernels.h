@@ -53,4 +53,26 @@ struct GemvArgs {
 // Indexed fused GEMV/GEMM (nb <= 4) over 16-row serial-codec slabs.
 cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st);
 
+// Tensor-core GEMM over decoded row groups (batch >= 16 path).
+struct TcGroup {
+  uint64_t a_off;   // byte offset of the group's BF16 rows [rows, cols] in the scratch
+  uint64_t y_row0;  // first output row
+  uint64_t xoff;    // first column of X (element offset into X^T rows)
+  uint32_t rows, cols;
+};
+struct TcGemmArgs {
+  const TcGroup* groups;
+  const uint8_t* scratch;
+  const void* xt;        // BF16 X^T [npad][xt_ld]
+  uint64_t xt_ld;
+  float* y;              // Y at batch column b0 (row stride ld)
+  uint32_t ld, nb, npad, ksplit, tmem_cols;
+  int* status;
+};
+size_t tc_gemm_smem_bytes(uint32_t npad);
+// Converts X (FP32, [x_cols, ld] at column b0) to X^T BF16, zeroes Y rows when
+// K is split, then runs the tensor-core GEMM: ngroups * ksplit CTAs.
+cudaError_t launch_tc_gemm(const TcGemmArgs& args, uint32_t ngroups, const float* x, uint64_t x_cols,
+                           cudaStream_t st);
+
 }  // namespace xksv
