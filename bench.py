@@ -386,11 +386,12 @@ def run_case(args):
     stream = torch.cuda.Stream(device=dev)
     h = stream.cuda_stream
     if gemv:
-        x = torch.randn(cols, device=dev)
-        y = torch.empty(nslabs * rows, device=dev)
+        nb = args.batch
+        x = torch.randn(cols, nb, device=dev)
+        y = torch.empty(nslabs * rows, nb, device=dev)
         if plan.index(d_payload.data_ptr(), h):
             raise RuntimeError("xksv_plan_index failed")
-        fn = lambda: plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 1, h)
+        fn = lambda: plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), nb, h)
     else:
         d_out = torch.empty(out, dtype=torch.uint8, device=dev)
         fn = lambda: plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
@@ -402,13 +403,16 @@ def run_case(args):
         t = time_steps(fn, args.steps, stream)
         torch.cuda.nvtx.range_pop()
     assert plan.status(h) == 0
+    launches = plan.launches()
     plan.close()
     ms = t / args.steps * 1e3
     line = dict(case=args.case, slabs=nslabs, compressed_bytes=len(payload), out_bytes=out,
                 ms_per_launch=round(ms, 5))
     if gemv:
         idx = nslabs * (cols // 16 + 1) * 4
-        line.update(gweights_per_s=round(out / 2 / ms / 1e6, 1),
+        line.update(batch=args.batch, launches=launches,
+                    tflops=round(2 * (out / 2) * args.batch / ms / 1e9, 2),
+                    gweights_per_s=round(out / 2 / ms / 1e6, 1),
                     traffic_gbs=round((len(payload) + idx) / ms / 1e6, 1), index_bytes=idx)
     else:
         line.update(out_gbs=round(out / ms / 1e6, 1), traffic_gbs=round((out + len(payload)) / ms / 1e6, 1))
@@ -500,6 +504,7 @@ def main():
     ap.add_argument("--warmup-cpu", type=int, default=0)
     ap.add_argument("--gemv-steps", type=int, default=20)
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--batch", type=int, default=1, help="batch columns of X in gemv- cases")
     ap.add_argument("--case", default=None,
                     help="CODEC:ROWSxCOLS:SLABS small decode workload (profiling), e.g. parallel:16x2048:2048; "
                          "gemv-serial:16x4096:1024 runs the indexed batch-1 GEMV instead")

@@ -455,7 +455,12 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
   p->launches = 0;
   cudaError_t e = cudaSuccess;
   const uint32_t ld = uint32_t(batch);
-  if (batch >= 16 && p->tc_ok) {
+  // routing (measured on B200, 1024 slabs of 16x4096): up to batch 4 the
+  // CUDA-core kernels with FP32 X (the indexed tile kernel: 116-220 us);
+  // beyond, decode + tensor-core GEMM with X rounded to BF16 (~310 us for
+  // any batch <= 256, against 400-660 us for batch 6-12 on CUDA cores)
+  const bool indexed = p->d_tidx && d_payload == p->indexed_payload;
+  if (p->tc_ok && batch > 4) {
     // decode every slab into its BF16 row group, then the tensor-core GEMM,
     // up to 256 batch columns per pass over the same decoded scratch
     if (!p->d_scratch && cudaMalloc(&p->d_scratch, std::max<uint64_t>(16, p->scratch_bytes)) != cudaSuccess)
@@ -495,7 +500,6 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
     return e == cudaSuccess ? 0 : 1;
   }
   // indexed serial slabs: tile-parallel kernel, 4 batch columns per pass
-  const bool indexed = p->d_tidx && d_payload == p->indexed_payload;
   const uint32_t ser0 = indexed ? p->n_ser_idx : 0;
   if (indexed && p->n_items) {
     for (size_t b0 = 0; b0 < batch && e == cudaSuccess; b0 += 4) {

@@ -656,29 +656,18 @@ __device__ __forceinline__ float wfloat(uint32_t e, uint32_t sw) {
 }
 
 // acc[b] += w(e_k, byte k of sw) * x[4q + k][b] for the block's four codes;
-// xr holds the tile's 16 x values when NB == 1, else x is read at xc (row
-// stride ld) for the nb active columns.
+// xr4 holds the block's x values, column-major in k then b (NB per column).
 template <int NB>
 __device__ __forceinline__ void fma4(float* acc, uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3,
-                                     uint32_t sw, const float* xr4, const float* xc, uint32_t ld,
-                                     uint32_t nb) {
+                                     uint32_t sw, const float* xr4) {
   const float w0 = wfloat<0>(e0, sw), w1 = wfloat<1>(e1, sw);
   const float w2 = wfloat<2>(e2, sw), w3 = wfloat<3>(e3, sw);
-  if (NB == 1) {
-    acc[0] = fmaf(w0, xr4[0], acc[0]);
-    acc[0] = fmaf(w1, xr4[1], acc[0]);
-    acc[0] = fmaf(w2, xr4[2], acc[0]);
-    acc[0] = fmaf(w3, xr4[3], acc[0]);
-  } else {
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      if (uint32_t(b) < nb) {
-        acc[b] = fmaf(w0, __ldg(xc + b), acc[b]);
-        acc[b] = fmaf(w1, __ldg(xc + ld + b), acc[b]);
-        acc[b] = fmaf(w2, __ldg(xc + 2 * ld + b), acc[b]);
-        acc[b] = fmaf(w3, __ldg(xc + 3 * ld + b), acc[b]);
-      }
-    }
+  for (int b = 0; b < NB; ++b) {
+    acc[b] = fmaf(w0, xr4[b], acc[b]);
+    acc[b] = fmaf(w1, xr4[NB + b], acc[b]);
+    acc[b] = fmaf(w2, xr4[2 * NB + b], acc[b]);
+    acc[b] = fmaf(w3, xr4[3 * NB + b], acc[b]);
   }
 }
 
@@ -708,21 +697,24 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const uint32_t b0 = ti[tile], b1 = ti[tile + 1];
     // x for this tile's 16 columns
     const float* xs = a.x + (sd.xoff + uint64_t(tile) * 16) * a.ld;
-    float xr[NB == 1 ? 16 : 1];
-    if (NB == 1) {
-      if (a.ld == 1 && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+    // x[c][b] for the tile's 16 columns and the pass's nb <= NB batch columns
+    // (zero beyond nb), in registers for the whole tile
+    float xr[16 * NB];
+    if (NB == 1 && a.ld == 1 && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(xs) + q);
-          xr[4 * q] = v.x;
-          xr[4 * q + 1] = v.y;
-          xr[4 * q + 2] = v.z;
-          xr[4 * q + 3] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) xr[q] = __ldg(xs + q * a.ld);
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xs) + q);
+        xr[4 * q] = v.x;
+        xr[4 * q + 1] = v.y;
+        xr[4 * q + 2] = v.z;
+        xr[4 * q + 3] = v.w;
       }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          xr[c * NB + b] = uint32_t(b) < a.nb ? __ldg(xs + uint64_t(c) * a.ld + b) : 0.f;
     }
     // the tile's 256 sign/mantissa bytes, one 16-byte row per step from
     // aligned 16-byte loads (the misalignment is the same for the whole slab;
@@ -784,7 +776,7 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
             uint32_t e0, e1, e2, e3;
             r.refill_to<4 * SK>();
             code4<23>(S, r, dead, e0, e1, e2, e3);
-            fma4<NB>(acc, e0, e1, e2, e3, sw[q], xr + 4 * q, xs + uint64_t(4 * q) * a.ld, a.ld, a.nb);
+            fma4<NB>(acc, e0, e1, e2, e3, sw[q], xr + 4 * q * NB);
           }
         }
 #pragma unroll
