@@ -632,7 +632,7 @@ constexpr uint32_t GCAP = uint32_t(GWINW - GPAD - 1) * 32;  // bits per round
 constexpr int GNB = 4;                   // batch columns per pass
 
 struct GemvShared {
-  uint32_t lut[1 << SK];  // exponent << 23 | length; 0 = none
+  uint16_t lut[1 << SK];  // exponent << 7 | length; 0 = none (16-bit: fewer bank conflicts)
   uint64_t lim[33];
   uint64_t firstc[33];
   alignas(16) uint16_t cnt[256];
@@ -645,14 +645,14 @@ struct GemvShared {
   int maxlen, minlen, flag;
 };
 
-// FP32 weight from a table entry (exponent at bit 23, length in bits 0-4) and
+// FP32 weight from a table entry (exponent at bit 7, length in bits 0-4) and
 // the sign/mantissa byte K of sw: byte -> bits 16-23 and 24-31, then one
-// bit-select keeps sign (31) and mantissa (16-22) from it, exponent from e.
+// bit-select keeps sign (31) and mantissa (16-22) from it, exponent from e << 16.
 template <int K>
 __device__ __forceinline__ float wfloat(uint32_t e, uint32_t sw) {
   constexpr uint32_t sel = 0x0044u | (uint32_t(K) << 8) | (uint32_t(K) << 12);
   const uint32_t s = __byte_perm(sw, 0u, sel);
-  return __uint_as_float((s & 0x807FFFFFu) | (e & 0x7F800000u));
+  return __uint_as_float((s & 0x807FFFFFu) | ((e << 16) & 0x7F800000u));
 }
 
 // acc[b] += w(e_k, byte k of sw) * x[4q + k][b] for the block's four codes;
@@ -682,7 +682,7 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const uint8_t* p = a.payload + sd.src;
     const uint32_t count = uint32_t(sd.rows * sd.cols);
     const uint32_t nbits = uint32_t(ld_le64(p + 8));
-    if (!build_tables<23, false, GT>(S, p + 16)) {  // validated when the index was built
+    if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       __syncthreads();
       continue;
@@ -775,7 +775,7 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
           for (int q = 0; q < 4; ++q) {
             uint32_t e0, e1, e2, e3;
             r.refill_to<4 * SK>();
-            code4<23>(S, r, dead, e0, e1, e2, e3);
+            code4<7>(S, r, dead, e0, e1, e2, e3);
             fma4<NB>(acc, e0, e1, e2, e3, sw[q], xr + 4 * q * NB);
           }
         }
