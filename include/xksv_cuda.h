@@ -86,8 +86,9 @@ void xksv_plan_destroy(xksv_plan* plan);
 
 /* Enqueues decode of every slab of the plan from d_payload (device) into
  * d_out (device) on `stream` (a cudaStream_t; NULL = legacy default stream).
- * Returns 1 only for launch errors; stream errors are found by
- * xksv_plan_status(). */
+ * Returns 1 for launch errors and, without launching, when d_out or a coded
+ * slab's dst_offset is odd (BF16 words need 2-byte alignment); stream errors
+ * are found by xksv_plan_status(). */
 int xksv_plan_decode(const xksv_plan* plan, const void* d_payload, void* d_out, void* stream);
 
 /* Enqueues Y[dst_offset + r, b] = sum_c W[r, c] * X[x_offset + c, b] for every
@@ -158,6 +159,24 @@ int xksv_host_pack_tensor(const void* data, size_t nbytes, size_t rows, size_t c
 #define XKSV_NOALLOC_MAX_SLABS 4096
 int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload,
                              void* d_out, void* stream);
+
+/* ---------------- Part 6: SHA-256 of decoded bytes on the GPU ----------- */
+/* The archive index stores the SHA-256 of every block's and tensor's decoded
+ * BF16 bytes (reference src/compile.cpp:255, 483; checked after decoding in
+ * src/verify.cpp:262-273 on the CPU).  These compute FIPS 180-4 SHA-256 on
+ * the device, so decoded weights are verified without copying them back.
+ * No reference counterpart.  Enqueued on `stream`; 0 on success, 1 on bad
+ * arguments or a CUDA error. */
+
+/* n ranges of device memory at d_base: ranges[2i] = byte offset,
+ * ranges[2i + 1] = length (a HOST array); 32-byte digests to d_digests
+ * (device, n * 32 bytes). */
+int xksv_cuda_sha256(const uint64_t* ranges, size_t n, const void* d_base, void* d_digests, void* stream);
+
+/* Digest i (slab order of xksv_plan_create) = SHA-256 of slab i's decoded
+ * bytes in d_out: [dst_offset, dst_offset + rows * cols * 2), or src_size
+ * bytes for a raw slab. */
+int xksv_plan_sha256(const xksv_plan* plan, const void* d_out, void* d_digests, void* stream);
 
 /* ---------------- Part 5: tensor-parallel fused GEMV / GEMM ------------- */
 /* One process per GPU; each rank's plan holds the slabs of its own rows

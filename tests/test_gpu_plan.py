@@ -121,3 +121,32 @@ def test_plan_gemm_multi_tensor(xg, batch):
         xo += C
         yo += R
     plan.close()
+
+
+def test_misaligned_outputs_are_refused(xg):
+    """BF16 outputs need 2-byte and FP32 buffers 4-byte alignment: the calls
+    return 1 without launching anything (a misaligned store would fault)."""
+    import ctypes
+    oracle = Oracle()
+    rng = np.random.default_rng(21)
+    raw = words_for("normal002", 16 * 256, rng).astype("<u2").tobytes()
+    blob = oracle.pack(raw, 16, 256)
+    lib = xg.load()
+    d_out = torch.zeros(16 * 256 * 2 + 16, dtype=torch.uint8, device="cuda")
+    host = ctypes.create_string_buffer(blob, len(blob))
+    assert lib.xksv_cuda_decode(host, len(blob), 16, 256, d_out.data_ptr() + 1) == 1
+    x = torch.zeros(256 + 4, device="cuda")
+    y = torch.zeros(16 + 4, device="cuda")
+    assert lib.xksv_cuda_gemv(host, len(blob), 16, 256, x.data_ptr() + 2, y.data_ptr()) == 1
+    d_payload = torch.frombuffer(bytearray(blob), dtype=torch.uint8).cuda()
+    odd = xg.Plan([dict(src_offset=0, src_size=len(blob), rows=16, cols=256, dst_offset=3, codec=1)])
+    with pytest.raises(RuntimeError):
+        odd.decode(d_payload.data_ptr(), d_out.data_ptr())
+    odd.close()
+    ok = xg.Plan([dict(src_offset=0, src_size=len(blob), rows=16, cols=256, dst_offset=0, codec=1)])
+    with pytest.raises(RuntimeError):
+        ok.decode(d_payload.data_ptr(), d_out.data_ptr() + 1)
+    ok.decode(d_payload.data_ptr(), d_out.data_ptr())
+    assert ok.status() == 0
+    assert d_out[:len(raw)].cpu().numpy().tobytes() == raw
+    ok.close()

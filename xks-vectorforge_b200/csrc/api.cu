@@ -175,6 +175,7 @@ struct xksv_plan {
   xksv::Slab* d_slabs = nullptr;  // [serial | parallel | raw]
   uint32_t n_ser = 0, n_par = 0, n_raw = 0;
   bool raw_gemm_ok = true;
+  bool odd_dst = false;  // a coded slab with an odd byte offset: decode refused
   uint64_t max_batch_rows = 0;
   int* d_status = nullptr;
   int* h_status = nullptr;
@@ -200,6 +201,7 @@ struct xksv_plan {
   uint64_t scratch_bytes = 0, x_cols = 0;
   uint8_t* d_scratch = nullptr;
   void* d_xt = nullptr;  // BF16 X^T [256][x_cols]
+  uint64_t* d_hash_ranges = nullptr;  // per slab in creation order: {dst, decoded bytes}
 };
 
 namespace {
@@ -269,9 +271,14 @@ using namespace xksv;
 
 extern "C" {
 
+// Pointers the kernels store BF16 (2-byte) or FP32 (4-byte) words through.
+static bool misaligned(const void* ptr, uintptr_t align) {
+  return (reinterpret_cast<uintptr_t>(ptr) & (align - 1)) != 0;
+}
+
 int xksv_cuda_decode(const void* input, size_t size, size_t rows, size_t cols, void* output) {
   const uint8_t* p = static_cast<const uint8_t*>(input);
-  if (!p || !output) return 1;
+  if (!p || !output || misaligned(output, 2)) return 1;
   if (!is_device_ptr(input) && !serial_header_ok(p, size, rows, cols, 1)) return 1;
   if (is_device_ptr(input) && (size < kHdr || !rows || !cols || cols > kMax / rows)) return 1;
   return run_single(Kind::Serial, input, size, rows, cols, output, nullptr, 1, false);
@@ -285,7 +292,7 @@ int xksv_cuda_gemv(const void* input, size_t size, size_t rows, size_t cols, con
 int xksv_cuda_gemm(const void* input, size_t size, size_t rows, size_t cols, size_t batch,
                    const float* x, float* output) {
   const uint8_t* p = static_cast<const uint8_t*>(input);
-  if (!x || !p || !output) return 1;
+  if (!x || !p || !output || misaligned(x, 4) || misaligned(output, 4)) return 1;
   if (batch > std::numeric_limits<uint32_t>::max()) return 1;
   if (!is_device_ptr(input) && !serial_header_ok(p, size, rows, cols, batch)) return 1;
   if (is_device_ptr(input) && (size < kHdr || !rows || !cols || !batch || cols > kMax / rows)) return 1;
@@ -294,7 +301,7 @@ int xksv_cuda_gemm(const void* input, size_t size, size_t rows, size_t cols, siz
 
 int xksv_cuda_decode_parallel(const void* input, size_t n, void* output) {
   const uint8_t* p = static_cast<const uint8_t*>(input);
-  if (!p || !output) return 1;
+  if (!p || !output || misaligned(output, 2)) return 1;
   uint64_t rows = 0, cols = 0;
   if (is_device_ptr(input)) {
     uint8_t h[32];
@@ -309,7 +316,7 @@ int xksv_cuda_decode_parallel(const void* input, size_t n, void* output) {
 
 int xksv_cuda_gemv_parallel(const void* input, size_t n, const float* x, float* output) {
   const uint8_t* p = static_cast<const uint8_t*>(input);
-  if (!x || !p || !output) return 1;
+  if (!x || !p || !output || misaligned(x, 4) || misaligned(output, 4)) return 1;
   uint64_t rows = 0, cols = 0;
   if (is_device_ptr(input)) {
     uint8_t h[32];
@@ -326,10 +333,12 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   if (!out || (!slabs && n) || n > std::numeric_limits<uint32_t>::max()) return 1;
   *out = nullptr;
   std::vector<Slab> ser, par, raw;
-  bool raw_gemm_ok = true;
+  bool raw_gemm_ok = true, odd_dst = false;
   for (size_t i = 0; i < n; ++i) {
     const xksv_slab& s = slabs[i];
     if (s.flags || s.src_offset > kMax - s.src_size) return 1;
+    // decode writes BF16 words: an odd byte offset would be a misaligned store
+    if (s.codec != XKSV_CODEC_RAW && (s.dst_offset & 1)) odd_dst = true;
     Slab d{s.src_offset, s.src_size, s.rows, s.cols, s.dst_offset, s.x_offset};
     switch (s.codec) {
       case XKSV_CODEC_TILE16:
@@ -366,6 +375,7 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   p->n_par = uint32_t(par.size());
   p->n_raw = uint32_t(raw.size());
   p->raw_gemm_ok = raw_gemm_ok;
+  p->odd_dst = odd_dst;
   std::vector<Slab> all;
   all.reserve(n);
   all.insert(all.end(), ser.begin(), ser.end());
@@ -377,6 +387,17 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   if (ok && n) {
     ok = cudaMalloc(&p->d_slabs, n * sizeof(Slab)) == cudaSuccess &&
          cudaMemcpy(p->d_slabs, all.data(), n * sizeof(Slab), cudaMemcpyHostToDevice) == cudaSuccess;
+  }
+  // decoded byte ranges in the caller's slab order (xksv_plan_sha256)
+  if (ok && n) {
+    std::vector<uint64_t> hr(2 * n);
+    for (size_t i = 0; i < n; ++i) {
+      hr[2 * i] = slabs[i].dst_offset;
+      hr[2 * i + 1] = slabs[i].codec == XKSV_CODEC_RAW ? slabs[i].src_size : slabs[i].rows * slabs[i].cols * 2;
+    }
+    ok = cudaMalloc(&p->d_hash_ranges, hr.size() * sizeof(uint64_t)) == cudaSuccess &&
+         cudaMemcpy(p->d_hash_ranges, hr.data(), hr.size() * sizeof(uint64_t), cudaMemcpyHostToDevice) ==
+             cudaSuccess;
   }
   // tensor-core GEMM groups (raw slabs must hold exactly rows * cols BF16)
   {
@@ -415,6 +436,7 @@ void xksv_plan_destroy(xksv_plan* p) {
   if (p->d_tc_slabs) cudaFree(p->d_tc_slabs);
   if (p->d_scratch) cudaFree(p->d_scratch);
   if (p->d_xt) cudaFree(p->d_xt);
+  if (p->d_hash_ranges) cudaFree(p->d_hash_ranges);
   if (p->d_slabs) cudaFree(p->d_slabs);
   if (p->d_status) cudaFree(p->d_status);
   if (p->h_status) cudaFreeHost(p->h_status);
@@ -423,7 +445,7 @@ void xksv_plan_destroy(xksv_plan* p) {
 
 int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
-  if (!p || !d_payload || !d_out) return 1;
+  if (!p || !d_payload || !d_out || p->odd_dst || misaligned(d_out, 2)) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint8_t* pay = static_cast<const uint8_t*>(d_payload);
   uint8_t* out = static_cast<uint8_t*>(d_out);
@@ -447,7 +469,8 @@ int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, vo
 int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x, float* d_y,
                    size_t batch, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
-  if (!p || !d_payload || !d_x || !d_y || !batch || batch > std::numeric_limits<uint32_t>::max())
+  if (!p || !d_payload || !d_x || !d_y || !batch || batch > std::numeric_limits<uint32_t>::max() ||
+      misaligned(d_x, 4) || misaligned(d_y, 4))
     return 1;
   if (p->n_raw && !p->raw_gemm_ok) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -556,6 +579,31 @@ int xksv_plan_status(const xksv_plan* pc, void* stream) {
 }
 
 int xksv_plan_launches(const xksv_plan* p) { return p ? p->launches : 0; }
+
+int xksv_cuda_sha256(const uint64_t* ranges, size_t n, const void* d_base, void* d_digests, void* stream) {
+  if (!n) return 0;
+  if (!ranges || !d_base || !d_digests || n > std::numeric_limits<uint32_t>::max()) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* d_r = nullptr;  // stream-ordered: no device-wide synchronisation
+  if (cudaMallocAsync(&d_r, 2 * n * sizeof(uint64_t), st) != cudaSuccess) return 1;
+  cudaError_t e = cudaMemcpyAsync(d_r, ranges, 2 * n * sizeof(uint64_t), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess)
+    e = launch_sha256(static_cast<const uint64_t*>(d_r), uint32_t(n), static_cast<const uint8_t*>(d_base),
+                      static_cast<uint8_t*>(d_digests), st);
+  const cudaError_t f = cudaFreeAsync(d_r, st);
+  // the host ranges must outlive the copy
+  const cudaError_t g = cudaStreamSynchronize(st);
+  return e == cudaSuccess && f == cudaSuccess && g == cudaSuccess ? 0 : 1;
+}
+
+int xksv_plan_sha256(const xksv_plan* p, const void* d_out, void* d_digests, void* stream) {
+  if (!p || !d_out || !d_digests) return 1;
+  const uint32_t n = p->n_ser + p->n_par + p->n_raw;
+  return launch_sha256(p->d_hash_ranges, n, static_cast<const uint8_t*>(d_out), static_cast<uint8_t*>(d_digests),
+                       static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? 0
+             : 1;
+}
 
 int xksv_plan_index(xksv_plan* p, const void* d_payload, void* stream) {
   if (!p || !d_payload) return 1;

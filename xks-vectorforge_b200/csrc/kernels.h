@@ -75,4 +75,9 @@ size_t tc_gemm_smem_bytes(uint32_t npad);
 cudaError_t launch_tc_gemm(const TcGemmArgs& args, uint32_t ngroups, const float* x, uint64_t x_cols,
                            cudaStream_t st);
 
+// SHA-256 (FIPS 180-4) of n ranges {offset, length} (device array of 2n u64)
+// of d_base; 32-byte big-endian digests to d_digests.
+cudaError_t launch_sha256(const uint64_t* d_ranges, uint32_t n, const uint8_t* d_base, uint8_t* d_digests,
+                          cudaStream_t st);
+
 }  // namespace xksv

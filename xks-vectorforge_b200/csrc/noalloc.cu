@@ -42,7 +42,7 @@ extern "C" int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const 
                                         void* d_out, void* stream) {
   using namespace xksv;
   if (n > size_t(XKSV_NOALLOC_MAX_SLABS)) return 2;  // beyond the scratch array
-  if ((n && !slabs) || !d_payload || !d_out) return 1;
+  if ((n && !slabs) || !d_payload || !d_out || (reinterpret_cast<uintptr_t>(d_out) & 1)) return 1;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 1;
@@ -59,6 +59,7 @@ extern "C" int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const 
   for (size_t i = 0; i < n; ++i) {
     const xksv_slab& s = slabs[i];
     if (s.flags || s.codec > XKSV_CODEC_PARALLEL32) return 1;
+    if (s.codec != XKSV_CODEC_RAW && (s.dst_offset & 1)) return 1;  // BF16 stores need even offsets
     if (s.codec == XKSV_CODEC_TILE16 && (!s.rows || !s.cols || s.src_size < kHdr)) return 1;
     if (s.codec == XKSV_CODEC_PARALLEL32 && (!s.rows || s.rows > 16 || !s.cols || s.src_size < 32))
       return 1;

@@ -45,6 +45,9 @@ _SIGS = {
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_sha256": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_void_p,
+                          ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_sha256": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_tp_unique_id": ([ctypes.c_void_p], ctypes.c_int),
     "xksv_tp_comm_create": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                              ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
@@ -166,6 +169,11 @@ class Plan:
         """Builds the tile index (xksv_plan_index); returns 0, or 1 on a bad slab."""
         return self.lib.xksv_plan_index(self.handle, d_payload, stream)
 
+    def sha256(self, d_out, d_digests, stream=0):
+        """Enqueues the SHA-256 of every slab's decoded bytes (xksv_plan_sha256)."""
+        if self.lib.xksv_plan_sha256(self.handle, d_out, d_digests, stream):
+            raise RuntimeError("xksv_plan_sha256 failed")
+
     def status(self, stream=0):
         """0 when no slab reported an error since the last call, else 1."""
         return self.lib.xksv_plan_status(self.handle, stream)
@@ -267,3 +275,12 @@ class TPComm:
         if self.handle:
             self.lib.xksv_tp_comm_destroy(self.handle)
             self.handle = None
+
+
+def sha256_ranges(ranges, d_base, d_digests, stream=0, lib=None):
+    """SHA-256 of device byte ranges [(offset, length), ...] at d_base into
+    d_digests (n * 32 bytes, device); xksv_cuda_sha256."""
+    lib = lib or load()
+    flat = (ctypes.c_uint64 * max(1, 2 * len(ranges)))(*[v for r in ranges for v in r])
+    if lib.xksv_cuda_sha256(flat, len(ranges), d_base, d_digests, stream):
+        raise RuntimeError("xksv_cuda_sha256 failed")
