@@ -606,6 +606,25 @@ def main():
         except Exception:
             traffic = None
 
+    # integrity check on the device: SHA-256 of every decoded slab (the archive
+    # index's per-block digests, src/verify.cpp:262), spot-checked on the host
+    import hashlib
+    d_dig = torch.zeros(32 * len(slabs), dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+        plan.sha256(d_out.data_ptr(), d_dig.data_ptr(), h)
+        ts = time_steps(lambda: plan.sha256(d_out.data_ptr(), d_dig.data_ptr(), h), 3, stream)
+    assert plan.status(h) == 0
+    dig = d_dig.cpu().numpy().tobytes()
+    sha_ok = True
+    for i in range(0, len(slabs), max(1, len(slabs) // 16)):
+        s_ = slabs[i]
+        n_ = s_["src_size"] if s_["codec"] == 0 else s_["rows"] * s_["cols"] * 2
+        seg = d_out[s_["dst_offset"]:s_["dst_offset"] + n_].cpu().numpy().tobytes()
+        sha_ok &= hashlib.sha256(seg).digest() == dig[32 * i:32 * i + 32]
+    sha = dict(blocks=len(slabs), ms=round(ts / 3 * 1e3, 3), gbs=round(out_bytes * 3 / ts / 1e9, 1),
+               host_spot_check=bool(sha_ok))
+
     # end to end through the public API: pinned host payload -> device, decode,
     # status word back
     h_payload = torch.from_numpy(payload).pin_memory()
@@ -678,7 +697,7 @@ def main():
             e2e=dict(value=round(e2e_val, 2), unit="GB/s", h2d_bytes_per_step=comp_bytes,
                      d2h_bytes_per_step=4, steps=e2e_steps,
                      path="pinned host payload -> cudaMemcpyAsync -> xksv_plan_decode -> xksv_plan_status"),
-            clocks=clocks, gpu_launches=launches, fused_gemv=gemv, tp_fused_gemv=tp)
+            clocks=clocks, gpu_launches=launches, sha256_verify=sha, fused_gemv=gemv, tp_fused_gemv=tp)
         print(json.dumps(line), flush=True)
     plan.close()
     par_plan.close()
