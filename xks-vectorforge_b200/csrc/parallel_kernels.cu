@@ -45,13 +45,16 @@ struct WarpTabs {
   uint16_t lut[1 << PK][32];      // exponent << 7 | length; 0 = no code of length <= PK
   uint16_t lut2[(NE << K2) + 1][32];  // second level: 12-bit prefix - (L << K2); last row 0
   uint16_t cnt[PNL][32];          // number of codes of length PK+1+j
-  uint8_t lpos[PNL][32];          // fill cursor per long length (build only)
   uint8_t lsym[PLONG][32];        // long-code symbols, canonical (length, symbol) order
-  uint4 ring[RING][32];           // staged exponent-bit chunks (little-endian bytes)
+  union {
+    uint8_t lpos[PNL][32];        // fill cursor per long length (table build only)
+    uint4 ring[RING][32];         // staged exponent-bit chunks (little-endian bytes)
+  };
   uint4 smring[SMR][32];          // staged sign/mantissa chunks
-  float y[16 * PMAXB];            // GEMM accumulators for the slab's rows
 };
-constexpr size_t kSmemBytes = PWARPS * sizeof(WarpTabs);
+// decode: the warps' tables; GEMM adds [16][PMAXB] row accumulators per warp
+constexpr size_t kSmemTabs = PWARPS * sizeof(WarpTabs);
+constexpr size_t kSmemBytes[2] = {kSmemTabs, kSmemTabs + PWARPS * 16 * PMAXB * sizeof(float)};
 
 // Bit-serial tables for a substream the compact tables cannot hold; they
 // overlay the warp's first-level tables once the fast lanes are done.
@@ -574,6 +577,7 @@ __global__ void __launch_bounds__(PWARPS * 32)
   extern __shared__ __align__(16) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpTabs& W = reinterpret_cast<WarpTabs*>(smem)[warp];
+  float* ysm = MODE == 1 ? reinterpret_cast<float*>(smem + kSmemTabs) + warp * 16 * PMAXB : nullptr;
 
   for (uint32_t si = blockIdx.x * PWARPS + warp; si < nslabs; si += gridDim.x * PWARPS) {
     const Slab sd = slabs[si];
@@ -636,17 +640,18 @@ __global__ void __launch_bounds__(PWARPS * 32)
       if (lane == 0) atomicOr(status, kStatusCodebook);
       continue;
     }
+    __syncwarp();  // every lane's build is done before the bit ring (over lpos) fills
     Out o;
     o.out = reinterpret_cast<uint16_t*>(out + sd.dst);
     o.x = MODE == 1 ? x + sd.xoff * ld : nullptr;
-    o.ysm = W.y;
+    o.ysm = ysm;
     o.rows = uint32_t(rows);
     o.cols = uint32_t(cols);
     o.ld = ld;
     o.nb = nb;
     o.xvec = nb == 1 && ld == 1 && (reinterpret_cast<uintptr_t>(o.x) & 15) == 0;
     if (MODE == 1) {
-      for (int k = lane; k < 16 * PMAXB; k += 32) W.y[k] = 0.f;
+      for (int k = lane; k < 16 * PMAXB; k += 32) ysm[k] = 0.f;
       __syncwarp();
     }
     const bool nice = rows == 16 && (cols & 15) == 0 &&
@@ -679,7 +684,7 @@ __global__ void __launch_bounds__(PWARPS * 32)
       __syncwarp();
       for (uint32_t k = lane; k < uint32_t(rows) * nb; k += 32) {
         const uint32_t r = k / nb, b = k - r * nb;
-        y[(sd.dst + r) * ld + b] = W.y[r * PMAXB + b];
+        y[(sd.dst + r) * ld + b] = ysm[r * PMAXB + b];
       }
       __syncwarp();
     }
@@ -691,21 +696,21 @@ void set_attr_once() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 31 && ((done_mask >> dev) & 1)) return;
-  cudaFuncSetAttribute(parallel_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-  cudaFuncSetAttribute(parallel_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+  cudaFuncSetAttribute(parallel_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes[0]));
+  cudaFuncSetAttribute(parallel_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes[1]));
   if (dev < 31) done_mask |= 1 << dev;
 }
 
 }  // namespace
 
-size_t parallel_smem_bytes() { return kSmemBytes; }
+size_t parallel_smem_bytes() { return kSmemBytes[0]; }
 
 cudaError_t launch_parallel_decode(const Slab* slabs, uint32_t n, const uint8_t* payload,
                                    uint8_t* out, int* status, int grid, cudaStream_t st) {
   if (!n) return cudaSuccess;
   set_attr_once();
   const int need = int((n + PWARPS - 1) / PWARPS);
-  parallel_slab_kernel<0><<<grid < need ? grid : need, PWARPS * 32, kSmemBytes, st>>>(
+  parallel_slab_kernel<0><<<grid < need ? grid : need, PWARPS * 32, kSmemBytes[0], st>>>(
       slabs, n, payload, out, nullptr, nullptr, 1, 1, status);
   return cudaGetLastError();
 }
@@ -716,7 +721,7 @@ cudaError_t launch_parallel_gemm(const Slab* slabs, uint32_t n, const uint8_t* p
   if (!n) return cudaSuccess;
   set_attr_once();
   const int need = int((n + PWARPS - 1) / PWARPS);
-  parallel_slab_kernel<1><<<grid < need ? grid : need, PWARPS * 32, kSmemBytes, st>>>(
+  parallel_slab_kernel<1><<<grid < need ? grid : need, PWARPS * 32, kSmemBytes[1], st>>>(
       slabs, n, payload, nullptr, x + b0, y + b0, ld, nb, status);
   return cudaGetLastError();
 }
