@@ -361,7 +361,8 @@ def run_case(args):
 
     codec_name, shape, nslabs = args.case.split(":")
     gemv = codec_name.startswith("gemv-")
-    codec = {"serial": 1, "parallel": 2}[codec_name[5:] if gemv else codec_name]
+    indexed = codec_name == "iserial"  # serial codec, decoded through the plan's tile index
+    codec = {"serial": 1, "parallel": 2, "iserial": 1}[codec_name[5:] if gemv else codec_name]
     rows, cols = map(int, shape.split("x"))
     nslabs = int(nslabs)
     dev = "cuda:0"
@@ -394,6 +395,8 @@ def run_case(args):
         fn = lambda: plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), nb, h)
     else:
         d_out = torch.empty(out, dtype=torch.uint8, device=dev)
+        if indexed and plan.index(d_payload.data_ptr(), h):
+            raise RuntimeError("xksv_plan_index failed")
         fn = lambda: plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):

@@ -179,3 +179,40 @@ def test_index_rejects_corrupt_slab(xg):
     assert plan.status() == 0
     check(ws, mats, x, y, 1e-5)
     plan.close()
+
+
+@pytest.mark.parametrize("kind", ["normal002", "student3", "dense7"])
+def test_indexed_decode_bit_exact(xg, kind):
+    """xksv_plan_decode after xksv_plan_index decodes the 16-row serial slabs
+    one thread per tile; every slab's bytes equal the source, at 16-byte and at
+    2-byte aligned outputs, next to slabs the index does not cover."""
+    oracle = Oracle()
+    rng = np.random.default_rng(31 + len(kind))
+    shapes = [(16, 4096), (16, 4112), (7, 512), (16, 2050), (16, 256), (16, 8192)]
+    payload = bytearray(b"\x00" * 3)
+    entries, raws, out = [], [], 0
+    for i, (r, c) in enumerate(shapes):
+        if kind == "dense7":  # ~7-bit codes: several shared-memory rounds per CTA
+            w = ((rng.integers(0, 2, r * c, dtype=np.uint16) << 15) |
+                 (rng.integers(64, 192, r * c, dtype=np.uint16) << 7) |
+                 rng.integers(0, 128, r * c, dtype=np.uint16))
+        else:
+            w = words_for(kind, r * c, rng)
+        raw = w.astype("<u2").tobytes()
+        blob = oracle.pack(raw, r, c) if i % 3 != 2 else oracle.pack_parallel(raw, r, c)
+        entries.append(dict(src_offset=len(payload), src_size=len(blob), rows=r, cols=c,
+                            dst_offset=out, codec=1 if i % 3 != 2 else 2))
+        payload += blob
+        raws.append(raw)
+        out += len(raw) + (2 if i % 2 else 16)
+    d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
+    plan = xg.Plan(entries)
+    assert plan.index(d_payload.data_ptr()) == 0
+    for rep in range(2):
+        d_out = torch.full((out + 16,), 0xAB, dtype=torch.uint8, device="cuda")
+        plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+        assert plan.status() == 0
+        got = d_out.cpu().numpy().tobytes()
+        for e, raw in zip(entries, raws):
+            assert got[e["dst_offset"]:e["dst_offset"] + len(raw)] == raw, e
+    plan.close()

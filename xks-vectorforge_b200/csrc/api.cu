@@ -443,6 +443,25 @@ void xksv_plan_destroy(xksv_plan* p) {
   delete p;
 }
 
+namespace {
+// Indexed decode of the plan's 16-row serial slabs (slabs[0, n_ser_idx)) to
+// out + slab dst; the caller decodes the remaining serial slabs.
+cudaError_t tile_decode(xksv_plan* p, const xksv::Slab* slabs, const uint8_t* pay, uint8_t* out,
+                        cudaStream_t st) {
+  xksv::GemvArgs g{};
+  g.items = p->d_items;
+  g.nitems = p->n_items;
+  g.slabs = slabs;
+  g.tbase = p->d_tbase;
+  g.tidx = p->d_tidx;
+  g.payload = pay;
+  g.status = p->d_status;
+  g.out = out;
+  g.nb = 1;
+  return xksv::launch_serial_tile_decode(g, st);
+}
+}  // namespace
+
 int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
   if (!p || !d_payload || !d_out || p->odd_dst || misaligned(d_out, 2)) return 1;
@@ -451,8 +470,16 @@ int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, vo
   uint8_t* out = static_cast<uint8_t*>(d_out);
   p->launches = 0;
   cudaError_t e = cudaSuccess;
-  if (p->n_ser) {
-    e = launch_serial_decode(p->d_slabs, p->n_ser, pay, out, p->d_status, p->grid_ser, st);
+  // with a tile index of this payload, the 16-row serial slabs decode one
+  // thread per tile; the other serial slabs resynchronise their streams
+  const bool indexed = p->d_tidx && d_payload == p->indexed_payload && p->n_items;
+  const uint32_t ser0 = indexed ? p->n_ser_idx : 0;
+  if (indexed) {
+    e = tile_decode(p, p->d_slabs, pay, out, st);
+    ++p->launches;
+  }
+  if (e == cudaSuccess && p->n_ser > ser0) {
+    e = launch_serial_decode(p->d_slabs + ser0, p->n_ser - ser0, pay, out, p->d_status, p->grid_ser, st);
     ++p->launches;
   }
   if (e == cudaSuccess && p->n_par) {
@@ -489,8 +516,14 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
     if (!p->d_scratch && cudaMalloc(&p->d_scratch, std::max<uint64_t>(16, p->scratch_bytes)) != cudaSuccess)
       return 1;
     if (!p->d_xt && cudaMalloc(&p->d_xt, 256 * p->x_cols * 2) != cudaSuccess) return 1;
-    if (p->n_ser) {
-      e = launch_serial_decode(p->d_tc_slabs, p->n_ser, pay, p->d_scratch, p->d_status, p->grid_ser, st);
+    const uint32_t tser0 = indexed && p->n_items ? p->n_ser_idx : 0;
+    if (tser0) {
+      e = tile_decode(p, p->d_tc_slabs, pay, p->d_scratch, st);
+      ++p->launches;
+    }
+    if (e == cudaSuccess && p->n_ser > tser0) {
+      e = launch_serial_decode(p->d_tc_slabs + tser0, p->n_ser - tser0, pay, p->d_scratch, p->d_status,
+                               p->grid_ser, st);
       ++p->launches;
     }
     if (e == cudaSuccess && p->n_par) {

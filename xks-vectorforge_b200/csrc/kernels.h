@@ -49,9 +49,13 @@ struct GemvArgs {
   float* partials;         // [item][16][4] row sums of slabs split over several items
   uint32_t* counters;      // per slab, zero between launches
   int* status;
+  uint8_t* out;            // indexed decode: output base (slab dst = byte offset)
 };
 // Indexed fused GEMV/GEMM (nb <= 4) over 16-row serial-codec slabs.
 cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st);
+// Indexed decode of the same slabs to BF16 at args.out + slab dst (x, y,
+// partials and counters unused).
+cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st);
 
 // Tensor-core GEMM over decoded row groups (batch >= 16 path).
 struct TcGroup {

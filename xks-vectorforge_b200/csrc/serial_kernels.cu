@@ -671,8 +671,9 @@ __device__ __forceinline__ void fma4(float* acc, uint32_t e0, uint32_t e1, uint3
   }
 }
 
+// NB == 0: decode mode (BF16 tile rows to a.out + slab dst); NB >= 1: GEMV/GEMM.
 template <int NB>
-__global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   GemvShared& S = *reinterpret_cast<GemvShared*>(smem_raw);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -687,7 +688,8 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
       __syncthreads();
       continue;
     }
-    for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
+    if (NB > 0)
+      for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
     const uint32_t* ti = a.tidx + a.tbase[it.slab];
     const uint8_t* sm = p + kHdr;
     const uint8_t* bits = sm + count;
@@ -699,8 +701,10 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const float* xs = a.x + (sd.xoff + uint64_t(tile) * 16) * a.ld;
     // x[c][b] for the tile's 16 columns and the pass's nb <= NB batch columns
     // (zero beyond nb), in registers for the whole tile
-    float xr[16 * NB];
-    if (NB == 1 && a.ld == 1 && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+    float xr[NB > 0 ? 16 * NB : 1];
+    if (NB == 0) {
+      // decode mode: no x
+    } else if (NB == 1 && a.ld == 1 && (reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(xs) + q);
@@ -722,6 +726,7 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const uintptr_t sma = reinterpret_cast<uintptr_t>(sm + uint64_t(tile) * 256);
     const int soff = int(sma & 15);
     const uint4* sq = reinterpret_cast<const uint4*>(sma & ~uintptr_t(15));
+    const bool ostore16 = NB == 0 && ((reinterpret_cast<uintptr_t>(a.out + sd.dst) | (sd.cols * 2)) & 15) == 0;
     uint32_t ta = 0;
     while (ta < it.ntiles) {  // rounds (one, unless the tiles' bits exceed GCAP)
       const uint32_t base_bit = ti[it.tile0 + ta] & ~31u;
@@ -760,7 +765,7 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
         const int nr = row < 15 ? row + 1 : 15;
         nlo = ldg16(sq + nr);
         if (soff) nhi = ldg16(sq + nr + 1);
-        float acc[NB];
+        float acc[NB > 0 ? NB : 1];
 #pragma unroll
         for (int b = 0; b < NB; ++b) acc[b] = 0.f;
         // a row starts inside the staged bits: its 16 codes stay inside GPAD
@@ -768,7 +773,36 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
           atomicOr(a.status, kStatusStream);
           act = false;
         }
-        if (act) {
+        if (act && NB == 0) {
+          // decode: tile row `row` = 16 BF16 words, two 16-byte halves
+          const uint4 s16 = realign16(lo, hi, soff);
+          const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
+          uint8_t* orow = a.out + sd.dst + (uint64_t(row) * sd.cols + uint64_t(tile) * 16) * 2;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t e[8];
+            r.refill_to<4 * SK>();
+            code4<7>(S, r, dead, e[0], e[1], e[2], e[3]);
+            r.refill_to<4 * SK>();
+            code4<7>(S, r, dead, e[4], e[5], e[6], e[7]);
+            const uint32_t slo = sw[2 * hh], shi = sw[2 * hh + 1];
+            uint4 w;
+            w.x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
+            w.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
+            w.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
+            w.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
+            uint8_t* o = orow + 16 * hh;
+            if (ostore16) {
+              *reinterpret_cast<uint4*>(o) = w;
+            } else {  // 2-byte aligned output
+              uint16_t* o2 = reinterpret_cast<uint16_t*>(o);
+              o2[0] = uint16_t(w.x); o2[1] = uint16_t(w.x >> 16);
+              o2[2] = uint16_t(w.y); o2[3] = uint16_t(w.y >> 16);
+              o2[4] = uint16_t(w.z); o2[5] = uint16_t(w.z >> 16);
+              o2[6] = uint16_t(w.w); o2[7] = uint16_t(w.w >> 16);
+            }
+          }
+        } else if (act) {
           const uint4 s16 = realign16(lo, hi, soff);
           const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
 #pragma unroll
@@ -791,6 +825,10 @@ __global__ void __launch_bounds__(GT, NB == 1 ? 4 : 2) serial_tile_gemv_kernel(G
       ta = tb;
     }
     (void)nbits;
+    if (NB == 0) {
+      __syncthreads();
+      continue;
+    }
     // combine: row r, column b
     const bool comb = uint32_t(t) < 16u * a.nb;
     const uint32_t rr = uint32_t(t) / a.nb, bb = uint32_t(t) - rr * a.nb;
@@ -828,6 +866,7 @@ void serial_set_attr() {
   cudaFuncSetAttribute(serial_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   cudaFuncSetAttribute(serial_tile_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   cudaFuncSetAttribute(serial_tile_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   cudaFuncSetAttribute(serial_tile_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
@@ -879,6 +918,13 @@ cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st) {
     serial_tile_gemv_kernel<2><<<g, GT, sizeof(GemvShared), st>>>(args);
   else
     serial_tile_gemv_kernel<4><<<g, GT, sizeof(GemvShared), st>>>(args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st) {
+  if (!args.nitems) return cudaSuccess;
+  serial_set_attr();
+  serial_tile_gemv_kernel<0><<<args.nitems, GT, sizeof(GemvShared), st>>>(args);
   return cudaGetLastError();
 }
 
