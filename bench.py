@@ -486,15 +486,48 @@ def tp_gemv(args, dev, stream, threads, rank, world):
     # the all-gather placed every rank's shard at its rank's block
     g0 = groups[-1]
     own = bool(torch.equal(g0["yfull"][rank * g0["rows"]:(rank + 1) * g0["rows"]], g0["y"]))
+    ms = t / args.gemv_steps * 1e3
+
+    # fused all-gather: the GEMV epilogue stores rows into every rank's gathered
+    # buffer over NVLink, then a bounded flag wait (xksv_tp_fused_gemm)
+    fused = xksv_gpu.TPFused(rank, world, max(g["rows"] for g in groups), 1)
+
+    def forward_fused():
+        for g in groups:
+            g["fused_y"] = fused.gemm(g["plan"], d_payload.data_ptr(), x.data_ptr(), g["rows"], 1, h)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            forward_fused()
+    stream.synchronize()
+    bad += sum(g["plan"].status(h) for g in groups)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        tf = time_steps(forward_fused, args.gemv_steps, stream)
+    bad += sum(g["plan"].status(h) for g in groups)
+    tt = torch.tensor([tf], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_f = float(tt.item()) / args.gemv_steps * 1e3
+    # same gathered rows as the NCCL path (last group, this rank's block)
+    chk = torch.empty(world * g0["rows"], device=dev)
+    fused.gemm(g0["plan"], d_payload.data_ptr(), x.data_ptr(), g0["rows"], 1, h, chk.data_ptr())
+    stream.synchronize()
+    fused_match = bool(torch.allclose(chk, g0["yfull"], rtol=1e-5, atol=1e-6))
+    torch.cuda.synchronize()
+    dist.barrier()
+    fused.close()
     for g in groups:
         g["plan"].close()
     comm.close()
-    ms = t / args.gemv_steps * 1e3
-    return dict(metric="TP fused-GEMV tok/s Llama-8B b=1", value=round(1e3 / ms, 2), unit="tok/s",
-                ms_per_token=round(ms, 4), n_gpus=world, compressed_bytes_per_rank=int(payload.nbytes),
-                launches_per_token=len(groups), all_gathers_per_token=len(groups),
-                status_errors=int(bad), own_shard_gathered=own,
-                note="rows sharded per GPU in whole slabs; xksv_tp_gemm = fused plan GEMV + ncclAllGather")
+    return dict(metric="TP fused-GEMV tok/s Llama-8B b=1", value=round(1e3 / ms_f, 2), unit="tok/s",
+                ms_per_token=round(ms_f, 4), n_gpus=world, compressed_bytes_per_rank=int(payload.nbytes),
+                launches_per_token=2 * len(groups), status_errors=int(bad), matches_nccl_path=fused_match,
+                nccl_allgather=dict(value=round(1e3 / ms, 2), ms_per_token=round(ms, 4),
+                                    own_shard_gathered=own),
+                note="rows sharded per GPU in whole slabs; value: xksv_tp_fused_gemm (GEMV epilogue stores "
+                     "rows into every rank's buffer over NVLink + flag wait); nccl_allgather: xksv_tp_gemm "
+                     "(plan GEMV + ncclAllGather)")
 
 
 def main():

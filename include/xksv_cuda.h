@@ -160,6 +160,36 @@ int xksv_host_pack_tensor(const void* data, size_t nbytes, size_t rows, size_t c
 int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload,
                              void* d_out, void* stream);
 
+/* Fused variant: no separate collective.  The indexed GEMV kernel writes its
+ * output rows into this rank's block of its own gathered buffer; the grid's
+ * last CTA copies the block into every other rank's buffer (CUDA IPC peer
+ * mappings, stores over NVLink), fences once and raises this rank's flag on
+ * every rank; a one-warp kernel on each rank then waits (bounded, about a
+ * second; an error bit in the plan's status word after that) until all
+ * ranks' flags reach this call.  Plain peer stores only, no multicast.  The
+ * gathered buffers alternate between two halves on successive calls, so a
+ * result stays valid until the call after next on any rank. */
+#define XKSV_TP_IPC_BYTES 64
+typedef struct xksv_tp_fused xksv_tp_fused;
+
+/* Allocates this rank's gathered buffers (2 x nranks * max_rows_shard *
+ * max_batch floats, max_batch <= 4) and flags on the current device and
+ * returns its IPC handle (XKSV_TP_IPC_BYTES) for the other ranks.  0 or 1. */
+int xksv_tp_fused_create(int nranks, int rank, size_t max_rows_shard, size_t max_batch, xksv_tp_fused** ctx,
+                         void* ipc_handle);
+/* Opens the peers' buffers: handles = every rank's handle, in rank order. */
+int xksv_tp_fused_open(xksv_tp_fused* ctx, const void* handles);
+/* Enqueues the fused GEMV/GEMM (batch <= max_batch) of this rank's plan,
+ * which must hold only 16-row serial-codec slabs with a tile index for
+ * d_payload (xksv_plan_index).  The gathered Y [nranks * rows_shard, batch]
+ * (rank order) is copied to d_y_full when it is not NULL, and its address in
+ * the context's buffers is stored to *d_gathered when that is not NULL.
+ * Collective: every rank makes the same calls in the same order.  1 for bad
+ * arguments or launch errors. */
+int xksv_tp_fused_gemm(xksv_tp_fused* ctx, const xksv_plan* plan, const void* d_payload, const float* d_x,
+                       size_t rows_shard, size_t batch, float* d_y_full, float** d_gathered, void* stream);
+void xksv_tp_fused_destroy(xksv_tp_fused* ctx);
+
 /* ---------------- Part 6: SHA-256 of decoded bytes on the GPU ----------- */
 /* The archive index stores the SHA-256 of every block's and tensor's decoded
  * BF16 bytes (reference src/compile.cpp:255, 483; checked after decoding in

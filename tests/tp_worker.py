@@ -138,3 +138,50 @@ def gpu_tp_check(rank, world, port, out):
         Path(out).write_text(json.dumps(dict(err=err, rows=int(len(full)), shards=sizes)))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def gpu_tp_fused_check(rank, world, port, out):
+    """One GPU per rank: xksv_tp_fused_gemm (indexed GEMV whose epilogue
+    stores each row into every rank's gathered buffer over NVLink, then a
+    bounded flag wait), three successive calls with different X and batch,
+    each against an FP32 matmul of the weights."""
+    import numpy as np
+    import torch
+    import xksv_gpu
+    from helpers import bf16_to_f32
+    torch.cuda.set_device(rank)
+    dist = init_group(rank, world, port, "gloo")
+    lib = xksv_gpu.load()
+    payload, entries, ws, xn, yn = make_archive(
+        lambda raw, r, c: xksv_gpu.host_pack(raw, r, c, 1, lib))
+    local, rows_shard, runs = xksv_gpu.shard_entries(entries, world, rank, rows_of)
+    sizes = [None] * world
+    dist.all_gather_object(sizes, rows_shard)
+    pad = max(sizes)
+    all_runs = [None] * world
+    dist.all_gather_object(all_runs, runs)
+    idx = torch.from_numpy(xksv_gpu.gathered_to_full(None, world, all_runs, pad)).cuda()
+    d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
+    plan = xksv_gpu.Plan(local, lib)
+    assert plan.index(d_payload.data_ptr()) == 0
+    fused = xksv_gpu.TPFused(rank, world, pad, 4, lib)
+    stream = torch.cuda.current_stream().cuda_stream
+    errs = []
+    for call, batch in enumerate((1, 3, 4, 2)):
+        xs = np.random.default_rng(call).standard_normal((xn, batch)).astype(np.float32)
+        x = torch.from_numpy(xs).cuda()
+        y_full = torch.full((world * pad, batch), float("nan"), device="cuda")
+        fused.gemm(plan, d_payload.data_ptr(), x.data_ptr(), pad, batch, stream, y_full.data_ptr())
+        assert plan.status(stream) == 0
+        full = y_full[idx].cpu().numpy()
+        ref = np.concatenate([bf16_to_f32(w) @ xs[o:o + w.shape[1]]
+                              for w, o in zip(ws, np.cumsum([0] + [w.shape[1] for w in ws])[:-1])])
+        errs.append(float(np.linalg.norm(full - ref) / np.linalg.norm(ref)))
+    torch.cuda.synchronize()
+    dist.barrier()  # no rank frees its IPC-shared buffers while another may still use them
+    plan.close()
+    fused.close()
+    if rank == 0:
+        Path(out).write_text(json.dumps(dict(err=max(errs), rows=int(len(idx)), shards=sizes)))
+    dist.barrier()
+    dist.destroy_process_group()

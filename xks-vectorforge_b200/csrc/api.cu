@@ -697,4 +697,137 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, void* stream) {
   return 0;
 }
 
+// ------------------------------------------------ fused tensor parallel ---
+}  // extern "C"
+
+struct xksv_tp_fused {
+  int device = 0, world = 1, rank = 0;
+  size_t max_rows = 0, max_batch = 0;
+  uint8_t* base = nullptr;  // [2 gathered buffers][flags per rank][epoch][done]
+  size_t buf_bytes = 0, flags_off = 0, epoch_off = 0, done_off = 0;
+  std::vector<void*> opened;  // peers' mappings (nullptr for this rank)
+  float** d_peer_y[2] = {nullptr, nullptr};
+  uint32_t** d_peer_flags = nullptr;
+  uint64_t calls = 0;
+};
+
+extern "C" {
+
+int xksv_tp_fused_create(int world, int rank, size_t max_rows_shard, size_t max_batch, xksv_tp_fused** out,
+                         void* ipc_handle) {
+  if (!out || !ipc_handle || world < 1 || rank < 0 || rank >= world || !max_rows_shard || !max_batch ||
+      max_batch > 4)
+    return 1;
+  *out = nullptr;
+  auto* c = new xksv_tp_fused();
+  cudaGetDevice(&c->device);
+  c->world = world;
+  c->rank = rank;
+  c->max_rows = max_rows_shard;
+  c->max_batch = max_batch;
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  c->buf_bytes = up(size_t(world) * max_rows_shard * max_batch * sizeof(float));
+  c->flags_off = 2 * c->buf_bytes;
+  c->epoch_off = c->flags_off + up(size_t(world) * sizeof(uint32_t));
+  c->done_off = c->epoch_off + 256;
+  const size_t total = c->done_off + 256;
+  cudaIpcMemHandle_t h;
+  const bool ok = cudaMalloc(&c->base, total) == cudaSuccess && cudaMemset(c->base, 0, total) == cudaSuccess &&
+                  cudaIpcGetMemHandle(&h, c->base) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  if (!ok) {
+    xksv_tp_fused_destroy(c);
+    return 1;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *out = c;
+  return 0;
+}
+
+int xksv_tp_fused_open(xksv_tp_fused* c, const void* handles) {
+  if (!c || !handles) return 1;
+  c->opened.assign(c->world, nullptr);
+  std::vector<float*> y0(c->world), y1(c->world);
+  std::vector<uint32_t*> fl(c->world);
+  for (int g = 0; g < c->world; ++g) {
+    uint8_t* b = c->base;
+    if (g != c->rank) {
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, static_cast<const uint8_t*>(handles) + g * sizeof(h), sizeof(h));
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return 1;
+      c->opened[g] = p;
+      b = static_cast<uint8_t*>(p);
+    }
+    y0[g] = reinterpret_cast<float*>(b);
+    y1[g] = reinterpret_cast<float*>(b + c->buf_bytes);
+    fl[g] = reinterpret_cast<uint32_t*>(b + c->flags_off);
+  }
+  const size_t pb = c->world * sizeof(void*);
+  const bool ok = cudaMalloc(&c->d_peer_y[0], pb) == cudaSuccess && cudaMalloc(&c->d_peer_y[1], pb) == cudaSuccess &&
+                  cudaMalloc(&c->d_peer_flags, pb) == cudaSuccess &&
+                  cudaMemcpy(c->d_peer_y[0], y0.data(), pb, cudaMemcpyHostToDevice) == cudaSuccess &&
+                  cudaMemcpy(c->d_peer_y[1], y1.data(), pb, cudaMemcpyHostToDevice) == cudaSuccess &&
+                  cudaMemcpy(c->d_peer_flags, fl.data(), pb, cudaMemcpyHostToDevice) == cudaSuccess &&
+                  cudaStreamSynchronize(nullptr) == cudaSuccess;
+  return ok ? 0 : 1;
+}
+
+int xksv_tp_fused_gemm(xksv_tp_fused* c, const xksv_plan* pc, const void* d_payload, const float* d_x,
+                       size_t rows_shard, size_t batch, float* d_y_full, float** d_gathered, void* stream) {
+  auto* p = const_cast<xksv_plan*>(pc);
+  if (!c || !p || !d_payload || !d_x || !c->d_peer_flags || !batch || batch > c->max_batch ||
+      rows_shard > c->max_rows || misaligned(d_x, 4) || misaligned(d_y_full, 4))
+    return 1;
+  // every slab must be on the indexed tile path for this payload
+  const uint32_t n = p->n_ser + p->n_par + p->n_raw;
+  if (!p->d_tidx || d_payload != p->indexed_payload || p->n_ser_idx != n || !p->n_items) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int parity = int(c->calls & 1);
+  GemvArgs g{};
+  g.items = p->d_items;
+  g.nitems = p->n_items;
+  g.slabs = p->d_slabs;
+  g.tbase = p->d_tbase;
+  g.tidx = p->d_tidx;
+  g.payload = static_cast<const uint8_t*>(d_payload);
+  g.x = d_x;
+  g.ld = uint32_t(batch);
+  g.nb = uint32_t(batch);
+  g.partials = p->d_partials;
+  g.counters = p->d_counters;
+  g.status = p->d_status;
+  g.peer_y = c->d_peer_y[parity];
+  g.peer_flags = c->d_peer_flags;
+  g.npeers = uint32_t(c->world);
+  g.rank = uint32_t(c->rank);
+  g.peer_row0 = uint64_t(c->rank) * rows_shard;
+  g.peer_rows = rows_shard;
+  g.done = reinterpret_cast<uint32_t*>(c->base + c->done_off);
+  g.epoch = reinterpret_cast<uint32_t*>(c->base + c->epoch_off);
+  cudaError_t e = launch_serial_tile_gemm(g, st);
+  if (e == cudaSuccess)
+    e = launch_tp_wait(reinterpret_cast<const uint32_t*>(c->base + c->flags_off), uint32_t(c->world), g.epoch,
+                       p->d_status, st);
+  p->launches = 2;
+  float* gathered = reinterpret_cast<float*>(c->base + parity * c->buf_bytes);
+  if (e == cudaSuccess && d_y_full)
+    e = cudaMemcpyAsync(d_y_full, gathered, size_t(c->world) * rows_shard * batch * sizeof(float),
+                        cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return 1;
+  if (d_gathered) *d_gathered = gathered;
+  ++c->calls;
+  return 0;
+}
+
+void xksv_tp_fused_destroy(xksv_tp_fused* c) {
+  if (!c) return;
+  for (void* q : c->opened)
+    if (q) cudaIpcCloseMemHandle(q);
+  if (c->d_peer_y[0]) cudaFree(c->d_peer_y[0]);
+  if (c->d_peer_y[1]) cudaFree(c->d_peer_y[1]);
+  if (c->d_peer_flags) cudaFree(c->d_peer_flags);
+  if (c->base) cudaFree(c->base);
+  delete c;
+}
+
 }  // extern "C"

@@ -50,9 +50,22 @@ struct GemvArgs {
   uint32_t* counters;      // per slab, zero between launches
   int* status;
   uint8_t* out;            // indexed decode: output base (slab dst = byte offset)
+  // fused tensor-parallel all-gather (npeers > 0): output rows go to this
+  // rank's block (rows peer_row0 ..) of its own gathered buffer; the grid's
+  // last CTA copies the block into every other rank's buffer over NVLink and
+  // raises this rank's flag on every rank
+  float* const* peer_y;    // [npeers] gathered buffers (this call's half)
+  uint32_t* const* peer_flags;  // [npeers] flag arrays, indexed by source rank
+  uint32_t npeers, rank;
+  uint64_t peer_row0, peer_rows;  // this rank's block of the gathered Y
+  uint32_t* done;          // grid completion counter (zero between launches)
+  uint32_t* epoch;         // this rank's completed fused calls
 };
 // Indexed fused GEMV/GEMM (nb <= 4) over 16-row serial-codec slabs.
 cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st);
+// Fused TP: waits (bounded) until every rank's flag reaches this rank's epoch.
+cudaError_t launch_tp_wait(const uint32_t* flags, uint32_t world, const uint32_t* epoch, int* status,
+                           cudaStream_t st);
 // Indexed decode of the same slabs to BF16 at args.out + slab dst (x, y,
 // partials and counters unused).
 cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st);

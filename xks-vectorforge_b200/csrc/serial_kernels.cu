@@ -655,6 +655,13 @@ __device__ __forceinline__ float wfloat(uint32_t e, uint32_t sw) {
   return __uint_as_float((s & 0x807FFFFFu) | ((e << 16) & 0x7F800000u));
 }
 
+// Y[row, b] = v: the local output, or (fused tensor parallel) this rank's
+// block of its own gathered buffer.
+__device__ __forceinline__ void store_y(const GemvArgs& a, uint64_t row, uint32_t b, float v) {
+  float* y = a.npeers ? a.peer_y[a.rank] + a.peer_row0 * a.ld : a.y;
+  y[row * a.ld + b] = v;
+}
+
 // acc[b] += w(e_k, byte k of sw) * x[4q + k][b] for the block's four codes;
 // xr4 holds the block's x values, column-major in k then b (NB per column).
 template <int NB>
@@ -836,7 +843,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     if (comb)
       for (int w = 0; w < GT / 32; ++w) v += S.red[rr][w][bb];
     if (it.nitems == 1) {
-      if (comb) a.y[(sd.dst + rr) * a.ld + bb] = v;
+      if (comb) store_y(a, sd.dst + rr, bb, v);
     } else {
       if (comb) a.partials[uint64_t(ii) * 16 * GNB + rr * GNB + bb] = v;
       __threadfence();
@@ -849,13 +856,62 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
           float sum = 0.f;
           for (uint32_t j = 0; j < it.nitems; ++j)
             sum += __ldcg(&a.partials[uint64_t(it.first + j) * 16 * GNB + rr * GNB + bb]);
-          a.y[(sd.dst + rr) * a.ld + bb] = sum;
+          store_y(a, sd.dst + rr, bb, sum);
         }
         if (t == 0) a.counters[it.slab] = 0;
       }
     }
     __syncthreads();
   }
+  if (NB > 0 && a.npeers) {
+    // fused all-gather: the last CTA to finish copies this rank's block of Y
+    // into every other rank's gathered buffer (peer stores over NVLink), makes
+    // them visible system-wide, and publishes the new epoch to every rank
+    __threadfence();
+    __syncthreads();
+    if (t == 0) S.flag = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (S.flag) {
+      __threadfence();
+      const uint64_t n = a.peer_rows * a.ld, off = a.peer_row0 * a.ld;
+      const float* src = a.peer_y[a.rank] + off;
+      for (uint64_t i = t; i < n; i += GT) {
+        const float v = __ldcg(src + i);
+        for (uint32_t g = 0; g < a.npeers; ++g)
+          if (g != a.rank) a.peer_y[g][off + i] = v;
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (t == 0) {
+        *a.done = 0;
+        const uint32_t e = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;
+        *reinterpret_cast<volatile uint32_t*>(a.epoch) = e;
+        __threadfence_system();
+        for (uint32_t g = 0; g < a.npeers; ++g)
+          *reinterpret_cast<volatile uint32_t*>(a.peer_flags[g] + a.rank) = e;
+      }
+    }
+  }
+}
+
+// One thread per rank polls that rank's flag until it reaches this rank's
+// epoch (every rank makes the same sequence of fused calls); the wait is
+// bounded (about a second), after which the status word gets an error bit.
+__global__ void tp_wait_kernel(const uint32_t* flags, uint32_t world, const uint32_t* epoch, int* status) {
+  const uint32_t g = threadIdx.x;
+  if (g < world) {
+    const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(epoch);
+    const volatile uint32_t* f = flags + g;
+    uint32_t i = 0;
+    while (int32_t(*f - target) < 0) {
+      if (++i > (1u << 23)) {
+        atomicOr(status, kStatusInternal);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __threadfence_system();
 }
 
 void serial_set_attr() {
@@ -925,6 +981,12 @@ cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
   serial_set_attr();
   serial_tile_gemv_kernel<0><<<args.nitems, GT, sizeof(GemvShared), st>>>(args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tp_wait(const uint32_t* flags, uint32_t world, const uint32_t* epoch, int* status,
+                           cudaStream_t st) {
+  tp_wait_kernel<<<1, 32 * ((world + 31) / 32), 0, st>>>(flags, world, epoch, status);
   return cudaGetLastError();
 }
 

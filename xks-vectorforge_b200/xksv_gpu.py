@@ -48,6 +48,13 @@ _SIGS = {
     "xksv_cuda_sha256": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_void_p,
                           ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_sha256": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_fused_create": ([ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t,
+                              ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_fused_open": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_fused_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                            ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                            ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_fused_destroy": ([ctypes.c_void_p], None),
     "xksv_tp_unique_id": ([ctypes.c_void_p], ctypes.c_int),
     "xksv_tp_comm_create": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                              ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
@@ -284,3 +291,41 @@ def sha256_ranges(ranges, d_base, d_digests, stream=0, lib=None):
     flat = (ctypes.c_uint64 * max(1, 2 * len(ranges)))(*[v for r in ranges for v in r])
     if lib.xksv_cuda_sha256(flat, len(ranges), d_base, d_digests, stream):
         raise RuntimeError("xksv_cuda_sha256 failed")
+
+
+class TPFused:
+    """Fused tensor-parallel GEMV/GEMM (xksv_tp_fused_*): the GEMV epilogue
+    stores each output row into every rank's gathered buffer over NVLink; the
+    IPC handles travel over a torch.distributed group."""
+
+    IPC_BYTES = 64
+
+    def __init__(self, rank, world, max_rows_shard, max_batch=1, lib=None):
+        import torch.distributed as dist
+        self.lib = lib or load()
+        h = ctypes.create_string_buffer(self.IPC_BYTES)
+        ctx = ctypes.c_void_p()
+        if self.lib.xksv_tp_fused_create(world, rank, max_rows_shard, max_batch, ctypes.byref(ctx), h):
+            raise RuntimeError("xksv_tp_fused_create failed")
+        self.handle = ctx
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(h.raw))
+        joined = ctypes.create_string_buffer(b"".join(handles), self.IPC_BYTES * world)
+        if self.lib.xksv_tp_fused_open(ctx, joined):
+            self.close()
+            raise RuntimeError("xksv_tp_fused_open failed")
+        dist.barrier()
+
+    def gemm(self, plan, d_payload, d_x, rows_shard, batch, stream=0, d_y_full=None):
+        """Enqueues the fused call (and a copy of the gathered Y to d_y_full
+        when given); returns the device address of the gathered Y."""
+        y = ctypes.c_void_p()
+        if self.lib.xksv_tp_fused_gemm(self.handle, plan.handle, d_payload, d_x, rows_shard, batch,
+                                       d_y_full, ctypes.byref(y), stream):
+            raise RuntimeError("xksv_tp_fused_gemm failed")
+        return y.value
+
+    def close(self):
+        if self.handle:
+            self.lib.xksv_tp_fused_destroy(self.handle)
+            self.handle = None
