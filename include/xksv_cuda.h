@@ -141,6 +141,20 @@ int xksv_host_pack_tensor(const void* data, size_t nbytes, size_t rows, size_t c
                           int threads, uint64_t dst_base, void** payload, size_t* payload_size,
                           xksv_slab** table, size_t* nslabs);
 
+/* GPU encoder: the slabs of xksv_host_pack_tensor, byte-identical, built on
+ * the current device from a row-major BF16 [rows, cols] tensor in device
+ * memory (histograms, Huffman lengths with the reference's tie order,
+ * canonical codes and bit packing in kernels; src/compile.cpp:247-285,
+ * 449-479, src/c_api.cpp:18-28, 44-65, src/codec.cpp:32-58).  *d_payload is
+ * device memory allocated by the library (release with xksv_cuda_free), the
+ * slab table host memory as for xksv_host_pack_tensor.  Synchronises
+ * `stream`; 0 on success, 1 on bad arguments, a CUDA error, or a code longer
+ * than 32 bits (not produced for the compiler's <= 1 MiB slabs). */
+int xksv_cuda_pack_tensor(const void* d_data, size_t rows, size_t cols, int codec, uint64_t dst_base,
+                          void** d_payload, size_t* payload_size, xksv_slab** table, size_t* nslabs,
+                          void* stream);
+void xksv_cuda_free(void* d_ptr);
+
 /* ---------------- Part 4: decode without device allocation -------------- */
 /* No counterpart in the reference.  For callers that cannot let a library
  * allocate device memory -- a server that has reserved the whole GPU for its

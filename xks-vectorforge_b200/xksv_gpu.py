@@ -48,6 +48,11 @@ _SIGS = {
     "xksv_cuda_sha256": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_void_p,
                           ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_sha256": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_pack_tensor": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int,
+                               ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
+                               ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_void_p),
+                               ctypes.POINTER(ctypes.c_size_t), ctypes.c_void_p], ctypes.c_int),
+    "xksv_cuda_free": ([ctypes.c_void_p], None),
     "xksv_tp_fused_create": ([ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t,
                               ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p], ctypes.c_int),
     "xksv_tp_fused_open": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
@@ -150,6 +155,30 @@ def host_pack_tensor(ptr, nbytes, rows, cols, codec, threads=0, dst_base=0, lib=
         lib.xksv_host_free(pay)
         lib.xksv_host_free(tab)
     return payload, slabs
+
+
+def cuda_pack_tensor(d_ptr, rows, cols, codec, dst_base=0, stream=0, lib=None):
+    """GPU encoder (xksv_cuda_pack_tensor) of a row-major BF16 tensor at device
+    address `d_ptr`.  Returns (device payload address, payload bytes, slab
+    dicts); release the payload with free_device()."""
+    lib = lib or load()
+    pay, psize = ctypes.c_void_p(), ctypes.c_size_t()
+    tab, ns = ctypes.c_void_p(), ctypes.c_size_t()
+    if lib.xksv_cuda_pack_tensor(d_ptr, rows, cols, codec, dst_base, ctypes.byref(pay), ctypes.byref(psize),
+                                 ctypes.byref(tab), ctypes.byref(ns), stream):
+        raise ValueError("xksv_cuda_pack_tensor failed")
+    try:
+        arr = (Slab * max(1, ns.value)).from_address(tab.value)
+        slabs = [dict(src_offset=s.src_offset, src_size=s.src_size, rows=s.rows, cols=s.cols,
+                      dst_offset=s.dst_offset, x_offset=s.x_offset, codec=s.codec)
+                 for s in arr[:ns.value]]
+    finally:
+        lib.xksv_host_free(tab)
+    return pay.value, psize.value, slabs
+
+
+def free_device(d_ptr, lib=None):
+    (lib or load()).xksv_cuda_free(d_ptr)
 
 
 class Plan:
