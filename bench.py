@@ -661,6 +661,36 @@ def main():
     sha = dict(blocks=len(slabs), ms=round(ts / 3 * 1e3, 3), gbs=round(out_bytes * 3 / ts / 1e9, 1),
                host_spot_check=bool(sha_ok))
 
+    # GPU encoder: the largest tensor of the checkpoint compiled on the device,
+    # byte-compared with the host encoder's payload for the same tensor
+    enc = None
+    try:
+        name, er, ec, _ = max(tensors, key=lambda t: t[1] * t[2])
+        g2 = torch.Generator(device=dev).manual_seed(11)
+        wt = (torch.randn(er, ec, generator=g2, device=dev) * 0.02).to(torch.bfloat16)
+        with torch.cuda.stream(stream):
+            dptr, nbytes_e, sl_e = xksv_gpu.cuda_pack_tensor(wt.data_ptr(), er, ec, 2, 0, h)
+            xksv_gpu.free_device(dptr)
+            t0 = time.perf_counter()
+            dptr, nbytes_e, sl_e = xksv_gpu.cuda_pack_tensor(wt.data_ptr(), er, ec, 2, 0, h)
+            te_enc = time.perf_counter() - t0
+        hw = wt.view(torch.int16).cpu().numpy()
+        hp, hs = xksv_gpu.host_pack_tensor(hw.ctypes.data, hw.nbytes, er, ec, 2, threads=threads)
+        dpay = torch.empty(nbytes_e, dtype=torch.uint8, device=dev)
+        cp = xksv_gpu.Plan([dict(src_offset=0, src_size=nbytes_e, rows=1, cols=1, dst_offset=0, codec=0)])
+        cp.decode(dptr, dpay.data_ptr(), h)
+        same = cp.status(h) == 0 and sl_e == hs and bool(np.array_equal(dpay.cpu().numpy(), hp))
+        cp.close()
+        xksv_gpu.free_device(dptr)
+        enc = dict(tensor=name, shape=[er, ec], codec="bf16-huffman-parallel32",
+                   ms=round(te_enc * 1e3, 2), gbs=round(wt.numel() * 2 / te_enc / 1e9, 1),
+                   identical_to_host_encoder=same,
+                   note="wall time of one xksv_cuda_pack_tensor call (synchronous: kernels, host "
+                        "offsets, allocation)")
+        del wt
+    except Exception as ex:  # reported, never silently replaced
+        enc = dict(error=f"{type(ex).__name__}: {ex}")
+
     # end to end through the public API: pinned host payload -> device, decode,
     # status word back
     h_payload = torch.from_numpy(payload).pin_memory()
@@ -733,7 +763,8 @@ def main():
             e2e=dict(value=round(e2e_val, 2), unit="GB/s", h2d_bytes_per_step=comp_bytes,
                      d2h_bytes_per_step=4, steps=e2e_steps,
                      path="pinned host payload -> cudaMemcpyAsync -> xksv_plan_decode -> xksv_plan_status"),
-            clocks=clocks, gpu_launches=launches, sha256_verify=sha, fused_gemv=gemv, tp_fused_gemv=tp)
+            clocks=clocks, gpu_launches=launches, sha256_verify=sha, gpu_encoder=enc, fused_gemv=gemv,
+            tp_fused_gemv=tp)
         print(json.dumps(line), flush=True)
     plan.close()
     par_plan.close()
