@@ -18,9 +18,10 @@
 //     register window refilled from the ring once per 4 codes without a
 //     data-dependent branch;
 //   * sign/mantissa bytes arrive 16 at a time through a 3-deep register ring;
-//   * 16 decoded BF16 words (one tile row) leave as two 16-byte stores,
-//     un-tiled on the fly, for 16-row slabs with cols % 16 == 0 and 16-byte
-//     aligned output; other shapes use an element-wise store path.
+//   * 16 decoded BF16 words (one tile row) leave as one 32-byte store (two
+//     16-byte stores when the output is only 16-byte aligned), un-tiled on the
+//     fly, for 16-row slabs with cols % 16 == 0; other shapes use an
+//     element-wise store path.
 // A substream whose codebook the compact tables cannot hold (a length above
 // PK+PNL or more than PLONG long codes, e.g. near-uniform exponents) is decoded
 // afterwards by lane 0 with the bit-serial canonical decoder.
@@ -424,6 +425,7 @@ struct Out {
   float* ysm;      // GEMM: [16][PMAXB] warp accumulators
   uint32_t rows, cols, ld, nb;
   bool xvec;       // GEMM: nb == 1, ld == 1, 16-byte aligned x
+  bool out32;      // decode: 32-byte aligned output (one 256-bit store per tile row)
 };
 
 template <int MODE>
@@ -475,8 +477,12 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
         v1.z = (__byte_perm(e[12], e[13], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.w, 0, 0x1100) & 0x807F807Fu);
         v1.w = (__byte_perm(e[14], e[15], 0x5410) & 0x7F807F80u) | (__byte_perm(s16.w, 0, 0x3322) & 0x807F807Fu);
         uint4* dst = reinterpret_cast<uint4*>(o.out + size_t(r) * o.cols + c);
-        dst[0] = v0;
-        dst[1] = v1;
+        if (o.out32) {
+          st_global_32B(dst, v0, v1);
+        } else {
+          dst[0] = v0;
+          dst[1] = v1;
+        }
       } else {
         float wf[16];
         const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
@@ -650,6 +656,7 @@ __global__ void __launch_bounds__(PWARPS * 32)
     o.ld = ld;
     o.nb = nb;
     o.xvec = nb == 1 && ld == 1 && (reinterpret_cast<uintptr_t>(o.x) & 15) == 0;
+    o.out32 = (reinterpret_cast<uintptr_t>(o.out) & 31) == 0;
     if (MODE == 1) {
       for (int k = lane; k < 16 * PMAXB; k += 32) ysm[k] = 0.f;
       __syncwarp();

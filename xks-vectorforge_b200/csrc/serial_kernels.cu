@@ -295,6 +295,7 @@ struct SOut {
   uint64_t rows, cols;
   uint32_t ld, nb;
   bool nice, xvec;
+  bool out32;  // decode: 32-byte aligned slab output (one 256-bit store per tile row)
 };
 
 template <int MODE>
@@ -316,7 +317,7 @@ __device__ __forceinline__ void semit_one(const SOut& o, uint32_t p, uint32_t wo
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict__ slabs,
+__global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restrict__ slabs,
                                                          uint32_t nslabs, SerialArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SerialShared& S = *reinterpret_cast<SerialShared*>(smem_raw);
@@ -363,6 +364,7 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
     o.nice = rows == 16 && (cols & 15) == 0 &&
              (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
     o.xvec = MODE == 1 && a.nb == 1 && a.ld == 1 && (reinterpret_cast<uintptr_t>(o.x) & 15) == 0;
+    o.out32 = MODE == 0 && (reinterpret_cast<uintptr_t>(o.out) & 31) == 0;
     if (MODE == 1) {
       for (int k = t; k < 16 * SMAXB; k += ST) S.y[k] = 0.f;
       if (!o.nice)
@@ -531,7 +533,43 @@ __global__ void __launch_bounds__(ST) serial_slab_kernel(const Slab* __restrict_
         bool dead = false;
         uint32_t g = base + my_off;
         const uint32_t gend = g + myN;
-        if (o.nice) {
+        if (MODE == 0 && o.nice) {
+          // whole tile rows: 16 codes -> one 32-byte store (two 16-byte
+          // stores when the output is only 16-byte aligned)
+          for (; g < gend && (g & 15); ++g) {
+            r.refill();
+            const uint32_t e = code1<7>(S, r, dead);
+            semit_one<MODE>(o, g, merge1(e, __ldg(sm + g)));
+          }
+          if (g + 16 <= gend) {
+            ByteReader8 smr;
+            smr.init(sm + g, sm + cnt32);
+            for (; g + 16 <= gend; g += 16) {
+              uint4 wv[2];
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const uint64_t s8 = smr.take();
+                uint32_t e[8];
+                r.refill_to<4 * SK>();
+                code4<7>(S, r, dead, e[0], e[1], e[2], e[3]);
+                r.refill_to<4 * SK>();
+                code4<7>(S, r, dead, e[4], e[5], e[6], e[7]);
+                const uint32_t slo = uint32_t(s8), shi = uint32_t(s8 >> 32);
+                wv[hh].x = (__byte_perm(e[0], e[1], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x1100) & 0x807F807Fu);
+                wv[hh].y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
+                wv[hh].z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
+                wv[hh].w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
+              }
+              uint16_t* dst = o.out + size_t((g >> 4) & 15) * cols + (g >> 8) * 16;
+              if (o.out32) {
+                st_global_32B(dst, wv[0], wv[1]);
+              } else {
+                reinterpret_cast<uint4*>(dst)[0] = wv[0];
+                reinterpret_cast<uint4*>(dst)[1] = wv[1];
+              }
+            }
+          }
+        } else if (o.nice) {
           for (; g < gend && (g & 7); ++g) {
             r.refill();
             const uint32_t e = code1<7>(S, r, dead);
@@ -734,6 +772,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const int soff = int(sma & 15);
     const uint4* sq = reinterpret_cast<const uint4*>(sma & ~uintptr_t(15));
     const bool ostore16 = NB == 0 && ((reinterpret_cast<uintptr_t>(a.out + sd.dst) | (sd.cols * 2)) & 15) == 0;
+    const bool ostore32 = NB == 0 && ((reinterpret_cast<uintptr_t>(a.out + sd.dst) | (sd.cols * 2)) & 31) == 0;
     uint32_t ta = 0;
     while (ta < it.ntiles) {  // rounds (one, unless the tiles' bits exceed GCAP)
       const uint32_t base_bit = ti[it.tile0 + ta] & ~31u;
@@ -785,6 +824,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
           const uint4 s16 = realign16(lo, hi, soff);
           const uint32_t sw[4] = {s16.x, s16.y, s16.z, s16.w};
           uint8_t* orow = a.out + sd.dst + (uint64_t(row) * sd.cols + uint64_t(tile) * 16) * 2;
+          uint4 wrow[2];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             uint32_t e[8];
@@ -798,15 +838,22 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
             w.y = (__byte_perm(e[2], e[3], 0x5410) & 0x7F807F80u) | (__byte_perm(slo, 0, 0x3322) & 0x807F807Fu);
             w.z = (__byte_perm(e[4], e[5], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x1100) & 0x807F807Fu);
             w.w = (__byte_perm(e[6], e[7], 0x5410) & 0x7F807F80u) | (__byte_perm(shi, 0, 0x3322) & 0x807F807Fu);
-            uint8_t* o = orow + 16 * hh;
-            if (ostore16) {
-              *reinterpret_cast<uint4*>(o) = w;
-            } else {  // 2-byte aligned output
-              uint16_t* o2 = reinterpret_cast<uint16_t*>(o);
-              o2[0] = uint16_t(w.x); o2[1] = uint16_t(w.x >> 16);
-              o2[2] = uint16_t(w.y); o2[3] = uint16_t(w.y >> 16);
-              o2[4] = uint16_t(w.z); o2[5] = uint16_t(w.z >> 16);
-              o2[6] = uint16_t(w.w); o2[7] = uint16_t(w.w >> 16);
+            wrow[hh] = w;
+          }
+          if (ostore32) {
+            st_global_32B(orow, wrow[0], wrow[1]);
+          } else if (ostore16) {
+            reinterpret_cast<uint4*>(orow)[0] = wrow[0];
+            reinterpret_cast<uint4*>(orow)[1] = wrow[1];
+          } else {  // 2-byte aligned output
+            uint16_t* o2 = reinterpret_cast<uint16_t*>(orow);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint4 w = wrow[hh];
+              o2[8 * hh + 0] = uint16_t(w.x); o2[8 * hh + 1] = uint16_t(w.x >> 16);
+              o2[8 * hh + 2] = uint16_t(w.y); o2[8 * hh + 3] = uint16_t(w.y >> 16);
+              o2[8 * hh + 4] = uint16_t(w.z); o2[8 * hh + 5] = uint16_t(w.z >> 16);
+              o2[8 * hh + 6] = uint16_t(w.w); o2[8 * hh + 7] = uint16_t(w.w >> 16);
             }
           }
         } else if (act) {

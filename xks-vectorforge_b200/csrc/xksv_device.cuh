@@ -348,6 +348,15 @@ __device__ __forceinline__ uint4 ld16_any(const uint8_t* p) {
                     __funnelshift_r(w2, w3, bs), __funnelshift_r(w3, w4, bs));
 }
 
+// One 32-byte store (a whole L2 sector) from eight words; dst must be 32-byte
+// aligned.  sm_100 has 256-bit global stores: a lane's tile row then reaches
+// L2 as one full-sector write instead of two half-sector writes.
+__device__ __forceinline__ void st_global_32B(void* dst, const uint4& a, const uint4& b) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(a.x), "r"(a.y),
+               "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+
 // ---------------------------------------------------- BF16 assembly -------
 // Two BF16 words from two exponent bytes (e0 in bits 0-7, e1 in bits 8-15)
 // and two sign/mantissa bytes (same places), packed low word first.
