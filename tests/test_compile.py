@@ -1,0 +1,65 @@
+"""Archive compiler (host encoder, no GPU): reproduces the archives the
+reference's own compile_model wrote (tests/golden/make_archives.py) byte for
+byte, and splits tensors into blocks by the reference's rule."""
+import json
+
+import pytest
+
+import xksv_compile as xc
+import xksv_runtime as rt
+from golden.make_archives import HERE as GOLDEN, LLAMA_CONFIG, checkpoint_tensors, write_safetensors
+
+
+def make_source(tmp_path, kind):
+    src = tmp_path / kind
+    src.mkdir()
+    write_safetensors(src / "model.safetensors", checkpoint_tensors(kind))
+    if kind == "llama":
+        (src / "config.json").write_text(json.dumps(LLAMA_CONFIG, indent=1))
+    return src
+
+
+@pytest.mark.parametrize("kind", ["llama", "misc"])
+@pytest.mark.parametrize("pref,tag", [("dfloat11", "tile16"), ("dfloat11-parallel", "parallel32")])
+def test_host_compile_is_byte_identical_to_reference(tmp_path, kind, pref, tag):
+    src = make_source(tmp_path, kind)
+    out = xc.compile_checkpoint(src, tmp_path / "out.xksv", pref, encoder="host", verify=False)
+    assert out.read_bytes() == (GOLDEN / f"{kind}_{tag}.xksv").read_bytes()
+    assert not (tmp_path / "out.xksv.partial").exists()
+
+
+def test_compile_refuses_existing_output(tmp_path):
+    src = make_source(tmp_path, "misc")
+    (tmp_path / "o.xksv").write_bytes(b"x")
+    with pytest.raises(rt.ArchiveError, match="already exists"):
+        xc.compile_checkpoint(src, tmp_path / "o.xksv", encoder="host", verify=False)
+
+
+@pytest.mark.parametrize("dtype,shape,want", [
+    # 1-D BF16: 4096-wide rows, 16 at a time, then the partial rows, then the tail
+    ("BF16", [100000], [(0, 131072, 16, 4096), (131072, 65536, 8, 4096), (196608, 3392, 1, 1696)]),
+    # wider than 32768 columns: fewer than 16 rows per 1 MiB block
+    ("BF16", [20, 65536], [(0, 1 << 20, 8, 65536), (1 << 20, 1 << 20, 8, 65536), (2 << 20, 1 << 19, 4, 65536)]),
+    # rows of more than 1 MiB: split as a flat tensor
+    ("BF16", [1, 600000], [(i * 131072, 131072, 16, 4096) for i in range(9)]
+     + [(9 * 131072, 2 * 4096 * 2, 2, 4096), (9 * 131072 + 16384, 1984 * 2, 1, 1984)]),
+    ("BF16", [0, 16], []),
+    ("F32", [300000], [(0, 1 << 20, 0, 0), (1 << 20, 300000 * 4 - (1 << 20), 0, 0)]),
+    ("BF16", [3, 4, 5], [(0, 120, 1, 60)]),
+])
+def test_block_layout(dtype, shape, want):
+    n = 1
+    for d in shape:
+        n *= d
+    size = n * xc.DTYPE_SIZES[dtype]
+    got = xc.block_layout(dtype, shape, size)
+    assert got == want
+    assert sum(b[1] for b in got) == size
+
+
+def test_checkpoint_rejects_gaps(tmp_path):
+    src = make_source(tmp_path, "misc")
+    p = src / "model.safetensors"
+    p.write_bytes(p.read_bytes() + b"\0")
+    with pytest.raises(rt.ArchiveError, match="unreferenced data"):
+        xc.checkpoint(src)

@@ -1,0 +1,375 @@
+"""Archive compiler on this library's encoders: Safetensors checkpoint ->
+.xksv archive, byte-identical to the reference's ``compile_model``
+(python/xksv.py:197-300; fresh compiles, without its resume journal).
+
+The reference encodes block by block on a CPU thread pool through
+``xksv_pack`` / ``xksv_pack_parallel``.  Here each run of equal-width blocks
+of a tensor is one call of ``xksv_cuda_pack_tensor`` (GPU: histograms,
+Huffman lengths, canonical codes and bit packing in kernels) or of
+``xksv_host_pack_tensor`` (all host cores), both byte-identical to the
+reference's per-block encoder.  The block layout, the raw fallback, the
+index fields and their order, the asset list and the JSON encoding follow
+the reference, so the reference's own ``verify`` accepts the output and the
+golden archives it compiled are reproduced byte for byte.
+"""
+import base64
+import hashlib
+import json
+import os
+import struct
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+import xksv_gpu
+from xksv_runtime import DTYPE_SIZES, HEADER, MAGIC, RAW_CHUNK, fail
+
+MAX_HEADER = 100_000_000
+# files copied into the archive as assets, in this order (python/xksv.py:248)
+ASSET_NAMES = ("config.json", "generation_config.json", "tokenizer.json", "tokenizer_config.json",
+               "vocab.json", "merges.txt", "special_tokens_map.json", "added_tokens.json",
+               "chat_template.jinja", "tokenizer.model", "vocab.txt", "preprocessor_config.json",
+               "processor_config.json", "video_preprocessor_config.json", "LICENSE", "NOTICE", "README.md")
+CODEC_NAMES = {"dfloat11": "bf16-huffman-tile16", "dfloat11-parallel": "bf16-huffman-parallel32"}
+
+
+def parse_json(data):
+    """Strict JSON: duplicate keys and NaN/Infinity rejected (python/xksv.py:30-40)."""
+    def pairs(items):
+        out = {}
+        for k, v in items:
+            if k in out:
+                fail(f"duplicate JSON key: {k}")
+            out[k] = v
+        return out
+
+    def bad_constant(_):
+        fail("invalid JSON number")
+    return json.loads(data, object_pairs_hook=pairs, parse_constant=bad_constant)
+
+
+def tensor_role(name):
+    """The index's role label of a tensor name (python/xksv.py:43-57)."""
+    if "embed_tokens" in name or "word_embeddings" in name:
+        return "token_embedding"
+    if "lm_head" in name or "output_projection" in name:
+        return "language_model_head"
+    if "visual" in name or "vision" in name:
+        return "vision_component"
+    if "linear_attn" in name:
+        if "conv" in name:
+            return "deltanet_convolution"
+        if "in_proj" in name:
+            return "deltanet_input_projection"
+        if "out_proj" in name:
+            return "deltanet_output_projection"
+        return "deltanet_state_parameter"
+    if "self_attn" in name or ".attention." in name:
+        return "attention_parameter"
+    if "expert" in name:
+        return "moe_expert"
+    if "router" in name:
+        return "moe_router"
+    if ".mlp." in name or ".feed_forward." in name:
+        return "feed_forward_parameter"
+    if "norm" in name:
+        return "normalization_parameter"
+    return "other"
+
+
+def contiguous_strides(shape):
+    out, stride = [], 1
+    for dim in reversed(shape):
+        out.append(stride)
+        stride *= dim
+    return list(reversed(out))
+
+
+def checkpoint(path):
+    """Shards of a Safetensors checkpoint (a file, or a directory with an
+    optional model.safetensors.index.json) with the reference's checks
+    (python/xksv.py:83-135): known dtypes, extents matching shapes, tensors
+    tiling the data section exactly."""
+    path = Path(path)
+    index_path = path / "model.safetensors.index.json" if path.is_dir() else None
+    mapping = None
+    if index_path and index_path.is_file():
+        mapping = parse_json(index_path.read_bytes()).get("weight_map")
+        if not isinstance(mapping, dict) or any(not isinstance(v, str) or Path(v).name != v
+                                                or not v.endswith(".safetensors") for v in mapping.values()):
+            fail("invalid shard index")
+        files = [path / name for name in sorted(set(mapping.values()))]
+    else:
+        files = sorted(path.glob("*.safetensors")) if path.is_dir() else [path]
+    if not files:
+        fail("no Safetensors shards found")
+    shards, names = [], set()
+    for file in files:
+        if not file.is_file() or file.suffix != ".safetensors":
+            fail(f"not a Safetensors file: {file}")
+        size = file.stat().st_size
+        with file.open("rb") as f:
+            prefix = f.read(8)
+            if len(prefix) != 8:
+                fail(f"truncated header: {file}")
+            hlen = struct.unpack("<Q", prefix)[0]
+            if hlen > MAX_HEADER or hlen > size - 8:
+                fail(f"invalid header length: {file}")
+            header = f.read(hlen)
+        j = parse_json(header)
+        if not isinstance(j, dict):
+            fail("invalid Safetensors header")
+        tensors, ranges = [], []
+        for name, desc in j.items():
+            if name == "__metadata__":
+                continue
+            if name in names:
+                fail(f"duplicate tensor: {name}")
+            names.add(name)
+            if not isinstance(desc, dict):
+                fail(f"invalid descriptor: {name}")
+            dtype, shape, offsets = desc.get("dtype"), desc.get("shape"), desc.get("data_offsets")
+            if dtype not in DTYPE_SIZES:
+                fail(f"unsupported dtype {dtype} for {name}")
+            if not isinstance(shape, list) or any(type(x) is not int or x < 0 for x in shape):
+                fail(f"invalid shape: {name}")
+            if not isinstance(offsets, list) or len(offsets) != 2 or any(type(x) is not int for x in offsets):
+                fail(f"invalid offsets: {name}")
+            start, end = offsets
+            num = 1
+            for dim in shape:
+                num *= dim
+            if start < 0 or end < start or end > size - 8 - hlen or end - start != num * DTYPE_SIZES[dtype]:
+                fail(f"invalid tensor extent: {name}")
+            tensors.append(dict(name=name, dtype=dtype, shape=shape, strides=contiguous_strides(shape),
+                                role=tensor_role(name), start=start, size=end - start))
+            if end > start:
+                ranges.append((start, end))
+        ranges.sort()
+        cursor = 0
+        for start, end in ranges:
+            if start != cursor:
+                fail(f"overlapping or noncontiguous tensors in {file}")
+            cursor = end
+        if cursor != size - 8 - hlen:
+            fail(f"unreferenced data in {file}")
+        tensors.sort(key=lambda x: x["start"])
+        shards.append(dict(name=file.name, path=str(file), header=base64.b64encode(header).decode("ascii"),
+                           header_size=hlen, tensors=tensors))
+    if mapping is not None:
+        actual = {t["name"]: s["name"] for s in shards for t in s["tensors"]}
+        if mapping != actual:
+            fail("shard index does not match discovered tensor names and files")
+    return shards
+
+
+def block_layout(dtype, shape, size):
+    """[(byte offset, bytes, rows, cols)] of a tensor's blocks: the
+    compiler's split (python/xksv.py:262, 283-286; src/compile.cpp:449-479).
+    rows == 0 marks a raw block of a non-BF16 tensor."""
+    if dtype == "BF16":
+        cols = shape[1] if len(shape) == 2 and shape[1] and shape[1] * 2 <= RAW_CHUNK else min(4096, size // 2)
+    else:
+        cols = 0
+    out, pos, remaining = [], 0, size
+    while remaining:
+        rows = min(16, RAW_CHUNK // (cols * 2), remaining // (cols * 2)) if cols else 0
+        if cols and not rows:
+            cols = min(4096, remaining // 2)
+            rows = 1
+        length = rows * cols * 2 if cols else min(remaining, RAW_CHUNK)
+        out.append((pos, length, rows, cols))
+        pos += length
+        remaining -= length
+    return out
+
+
+def coded_runs(layout):
+    """Consecutive BF16 blocks of equal width as (first byte, rows, cols, n)."""
+    runs = []
+    for off, length, rows, cols in layout:
+        if not rows:
+            continue
+        if runs and runs[-1][2] == cols and runs[-1][0] + runs[-1][1] * cols * 2 == off:
+            r = runs[-1]
+            runs[-1] = (r[0], r[1] + rows, cols, r[3] + 1)
+        else:
+            runs.append((off, rows, cols, 1))
+    return runs
+
+
+class _DevicePayload:
+    """Zero-copy torch view of library-allocated device bytes."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+class ArchiveWriter:
+    """Writes an archive in the reference's layout: header, assets, blocks in
+    tensor order, JSON index.  ``encoder`` is "gpu" (xksv_cuda_pack_tensor on
+    `device`) or "host" (xksv_host_pack_tensor on all cores)."""
+
+    def __init__(self, output, codec_preference="dfloat11", encoder="gpu", device="cuda:0", threads=0):
+        if codec_preference not in CODEC_NAMES:
+            fail(f"unsupported codec preference: {codec_preference}")
+        if encoder not in ("gpu", "host"):
+            fail(f"unknown encoder: {encoder}")
+        self.output = Path(output).absolute()
+        if self.output.exists():
+            fail("output already exists")
+        self.partial = self.output.with_name(self.output.name + ".partial")
+        if self.partial.exists():
+            fail("partial compilation exists; choose another output")
+        self.codec_name = CODEC_NAMES[codec_preference]
+        self.codec = xksv_gpu.CODEC_BY_NAME[self.codec_name]
+        self.encoder, self.device, self.threads = encoder, device, threads
+        self.lib = xksv_gpu.load()
+        self.pool = ThreadPoolExecutor(max_workers=max(2, min(32, os.cpu_count() or 2)))
+        fd = os.open(self.partial, os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
+        self.f = os.fdopen(fd, "w+b")
+        self.f.write(HEADER.pack(MAGIC, 0))
+        self.index = dict(version=1, format="safetensors", codec_preference=codec_preference, shards=[],
+                          assets=[])
+
+    def add_asset(self, name, data):
+        self.index["assets"].append(dict(name=name, offset=self.f.tell(), size=len(data),
+                                         sha256=hashlib.sha256(data).hexdigest()))
+        self.f.write(data)
+
+    def begin_shard(self, name, header_b64, source_sha256):
+        self.index["shards"].append(dict(name=name, header=header_b64, source_sha256=source_sha256, tensors=[]))
+
+    def _encode(self, raw, off, rows, cols):
+        """(payload bytes, slab dicts) of rows x cols BF16 at raw[off:]."""
+        nbytes = rows * cols * 2
+        if self.encoder == "host":
+            ptr = raw.ctypes.data + off
+            payload, slabs = xksv_gpu.host_pack_tensor(ptr, nbytes, rows, cols, self.codec, self.threads,
+                                                       0, lib=self.lib)
+            return payload, slabs
+        import torch
+        d = torch.from_numpy(raw[off:off + nbytes]).to(self.device)
+        with torch.cuda.device(d.device):
+            stream = torch.cuda.current_stream().cuda_stream
+            ptr, n, slabs = xksv_gpu.cuda_pack_tensor(d.data_ptr(), rows, cols, self.codec, 0, stream,
+                                                      lib=self.lib)
+            try:
+                payload = torch.as_tensor(_DevicePayload(ptr, n), device=d.device).cpu().numpy() if n else \
+                    np.zeros(0, np.uint8)
+            finally:
+                xksv_gpu.free_device(ptr, lib=self.lib)
+        return payload, slabs
+
+    def add_tensor(self, desc, raw, shard=-1):
+        """desc: name, dtype, shape, strides, role, start, size (the checkpoint
+        descriptor); raw: the tensor's bytes (bytes or a uint8 numpy array);
+        shard: position of the shard entry that lists the tensor."""
+        raw = np.frombuffer(raw, dtype=np.uint8) if not isinstance(raw, np.ndarray) else raw
+        if raw.size != desc["size"]:
+            fail(f"tensor bytes differ from descriptor: {desc['name']}")
+        t = dict(desc)
+        t["blocks"] = []
+        layout = block_layout(desc["dtype"], desc["shape"], desc["size"])
+        # digests on host threads while the blocks encode
+        tensor_digest = self.pool.submit(lambda: hashlib.sha256(raw).hexdigest())
+        block_digests = [self.pool.submit(lambda o=o, n=n: hashlib.sha256(raw[o:o + n]).hexdigest())
+                         for o, n, _, _ in layout]
+        encoded = {}
+        for off, rows, cols, nblocks in coded_runs(layout):
+            payload, slabs = self._encode(raw, off, rows, cols)
+            if len(slabs) != nblocks:
+                fail(f"encoder block split differs from the compiler's: {desc['name']}")
+            for s in slabs:
+                encoded[off + s["dst_offset"]] = (s, payload)
+        for i, (off, length, rows, cols) in enumerate(layout):
+            if rows:
+                s, payload = encoded.get(off, (None, None))
+                if s is None or s["rows"] != rows or s["cols"] != cols:
+                    fail(f"encoder block split differs from the compiler's: {desc['name']}")
+                if s["codec"] != xksv_gpu.CODEC_RAW:
+                    data = payload[s["src_offset"]:s["src_offset"] + s["src_size"]]
+                    codec = self.codec_name
+                else:
+                    data, codec = raw[off:off + length], "raw"
+            else:
+                data, codec = raw[off:off + length], "raw"
+            t["blocks"].append(dict(offset=self.f.tell(), size=int(data.size), raw_size=length, codec=codec,
+                                    rows=rows if codec != "raw" else 0, cols=cols if codec != "raw" else 0,
+                                    sha256=block_digests[i].result()))
+            self.f.write(memoryview(data))
+        t["sha256"] = tensor_digest.result()
+        self.index["shards"][shard]["tensors"].append(t)
+        return t
+
+    def close(self):
+        """Writes the index and the header and moves the file into place."""
+        offset = self.f.tell()
+        self.f.write(json.dumps(self.index, separators=(",", ":"), ensure_ascii=False).encode())
+        self.f.seek(0)
+        self.f.write(HEADER.pack(MAGIC, offset))
+        self.f.flush()
+        os.fsync(self.f.fileno())
+        self.f.close()
+        self.pool.shutdown()
+        os.link(self.partial, self.output)
+        os.unlink(self.partial)
+        return self.output
+
+    def abort(self):
+        self.f.close()
+        self.pool.shutdown()
+        if self.partial.exists():
+            self.partial.unlink()
+
+
+def compile_checkpoint(source, output, codec_preference="dfloat11", encoder="gpu", device="cuda:0", verify=True):
+    """``compile_model(source, output, codec_preference=...)`` on this
+    library's encoders.  With `verify`, the archive is then loaded and checked
+    on the device (every block decoded, every SHA-256 compared)."""
+    shards = checkpoint(source)
+    output = Path(output).absolute()
+    for s in shards:
+        if Path(s["path"]).resolve() == output.resolve():
+            fail("output would overwrite source")
+    w = ArchiveWriter(output, codec_preference, encoder, device)
+    try:
+        digests = [w.pool.submit(lambda p=s["path"]: _sha_file(p)) for s in shards]
+        for s, d in zip(shards, digests):
+            w.begin_shard(s["name"], s["header"], d.result())
+        if Path(source).is_dir():
+            for name in ASSET_NAMES:
+                p = Path(source) / name
+                if p.is_file():
+                    if p.stat().st_size > 100_000_000:
+                        fail(f"asset too large: {name}")
+                    w.add_asset(name, p.read_bytes())
+        for i, s in enumerate(shards):
+            with open(s["path"], "rb") as src:
+                for t in s["tensors"]:
+                    src.seek(8 + s["header_size"] + t["start"])
+                    raw = np.empty(t["size"], dtype=np.uint8)
+                    if t["size"] and src.readinto(memoryview(raw)) != t["size"]:
+                        fail("unexpected end of file")
+                    w.add_tensor(t, raw, shard=i)
+    except BaseException:
+        w.abort()
+        raise
+    path = w.close()
+    if verify:
+        import xksv_runtime
+        a = xksv_runtime.ResidentArchive(path, device)
+        a.verify()
+        a.close()
+    return path
+
+
+def _sha_file(path):
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        while True:
+            b = f.read(1 << 24)
+            if not b:
+                return h.hexdigest()
+            h.update(b)
