@@ -422,6 +422,117 @@ def run_case(args):
     print(json.dumps(line), flush=True)
 
 
+def run_runtime(args):
+    """`--case runtime`: the archive path around the kernels on the config-2
+    checkpoint.  Writes the seeded checkpoint as Safetensors to a temporary
+    directory, compiles it with the GPU encoder and with the host encoder (all
+    cores; byte-identical outputs checked), then loads the archive as the
+    runtime does: upload of the block region to HBM, device verification
+    (every block decoded, block digests on the device, tensor digests on host
+    threads), and whole-checkpoint decode into tensors (one plan).  Wall
+    times with the device synchronised; the file is in the page cache."""
+    import filecmp
+    import shutil
+    import tempfile
+
+    import numpy as np
+    import torch
+    import xksv_compile as xc
+    import xksv_runtime as rt
+
+    dev = "cuda:0"
+    torch.cuda.set_device(0)
+    tmp = Path(tempfile.mkdtemp(prefix="xksv-bench-"))
+    try:
+        gen = torch.Generator(device=dev).manual_seed(1)
+        header, parts, pos = {}, [], 0
+        for name, rows, cols, kind in llama_tensors(**CONFIG2):
+            if kind == "norm":
+                t, shape = torch.ones(cols, dtype=torch.bfloat16, device=dev), [cols]
+            else:
+                t = (torch.randn(rows, cols, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+                shape = [rows, cols]
+            b = t.view(torch.int16).cpu().numpy()
+            header[name] = dict(dtype="BF16", shape=shape, data_offsets=[pos, pos + b.nbytes])
+            parts.append(b)
+            pos += b.nbytes
+        h = json.dumps(header, separators=(",", ":")).encode()
+        h += b" " * (-len(h) % 8)
+        src = tmp / "ckpt"
+        src.mkdir()
+        with open(src / "model.safetensors", "wb") as f:
+            f.write(len(h).to_bytes(8, "little") + h)
+            for b in parts:
+                f.write(memoryview(b))
+        del parts
+        raw_bytes = pos
+
+        def timed(fn):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            r = fn()
+            torch.cuda.synchronize()
+            return r, time.perf_counter() - t0
+
+        arch = tmp / "gpu.xksv"
+        _, t_gpu = timed(lambda: xc.compile_checkpoint(src, arch, "dfloat11-parallel", encoder="gpu",
+                                                        device=dev, verify=False))
+        _, t_host = timed(lambda: xc.compile_checkpoint(src, tmp / "host.xksv", "dfloat11-parallel",
+                                                         encoder="host", verify=False))
+        identical = filecmp.cmp(arch, tmp / "host.xksv", shallow=False)
+        (tmp / "host.xksv").unlink()
+        a, t_up = timed(lambda: rt.ResidentArchive(arch, dev))
+        _, t_ver = timed(a.verify)
+        a.decode_all()  # first call: allocator growth
+        dec = []
+        for _ in range(max(1, args.steps)):
+            out, t = timed(a.decode_all)
+            dec.append(t)
+            del out
+        t_dec = statistics.median(dec)
+        # the reference's caller pattern (python/runtime.py:89-99) through this
+        # library's legacy entry points: per block a file read, a ctypes
+        # string buffer and one blocking decode call, on a sample of blocks
+        import xksv_gpu
+        lib = xksv_gpu.load()
+        blocks = [(t, b) for t in a.tensors.values() for b in t["blocks"]]
+        sample = blocks[:1000]
+        scratch = torch.empty(1 << 21, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        with open(arch, "rb") as f:
+            for t, b in sample:
+                f.seek(b["offset"])
+                data = f.read(b["size"])
+                if b["codec"] == "raw":
+                    scratch[:len(data)].copy_(torch.frombuffer(bytearray(data), dtype=torch.uint8))
+                    continue
+                buf = ctypes.create_string_buffer(data)
+                rc = (lib.xksv_cuda_decode_parallel(buf, len(data), scratch.data_ptr())
+                      if b["codec"] == "bf16-huffman-parallel32" else
+                      lib.xksv_cuda_decode(buf, len(data), b["rows"], b["cols"], scratch.data_ptr()))
+                assert rc == 0
+        torch.cuda.synchronize()
+        t_legacy = (time.perf_counter() - t0) / len(sample) * len(blocks)
+        arch_bytes = arch.stat().st_size
+        line = dict(case="runtime", config="configs[1] Llama-1.1B shape, dfloat11-parallel",
+                    checkpoint_bytes=raw_bytes, archive_bytes=arch_bytes, blocks=sum(
+                        len(t["blocks"]) for t in a.tensors.values()),
+                    compile_gpu_s=round(t_gpu, 3), compile_gpu_gbs=round(raw_bytes / t_gpu / 1e9, 2),
+                    compile_host_s=round(t_host, 3), compile_host_threads=os.cpu_count(),
+                    compile_outputs_identical=identical,
+                    upload_s=round(t_up, 3), upload_gbs=round(arch_bytes / t_up / 1e9, 2),
+                    verify_s=round(t_ver, 3), verify_gbs=round(raw_bytes / t_ver / 1e9, 2),
+                    decode_all_ms=round(t_dec * 1e3, 2), decode_all_gbs=round(raw_bytes / t_dec / 1e9, 1),
+                    load_s=round(t_up + t_ver + t_dec, 3),
+                    per_block_abi_decode_s_est=round(t_legacy, 2),
+                    per_block_abi_sample_blocks=len(sample))
+        a.close()
+        print(json.dumps(line), flush=True)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def tp_gemv(args, dev, stream, threads, rank, world):
     """Tensor-parallel batch-1 fused GEMV over every linear of the
     Llama-3-8B-shaped model: each rank encodes and holds only its row shard
@@ -546,6 +657,9 @@ def main():
                          "gemv-serial:16x4096:1024 runs the indexed batch-1 GEMV instead")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.case == "runtime":
+        run_runtime(args)
+        return
     if args.case:
         run_case(args)
         return

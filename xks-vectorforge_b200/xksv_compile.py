@@ -227,6 +227,7 @@ class ArchiveWriter:
         self.encoder, self.device, self.threads = encoder, device, threads
         self.lib = xksv_gpu.load()
         self.pool = ThreadPoolExecutor(max_workers=max(2, min(32, os.cpu_count() or 2)))
+        self._pending, self._max_pending = [], 2 * self.pool._max_workers
         fd = os.open(self.partial, os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
         self.f = os.fdopen(fd, "w+b")
         self.f.write(HEADER.pack(MAGIC, 0))
@@ -239,6 +240,7 @@ class ArchiveWriter:
         self.f.write(data)
 
     def begin_shard(self, name, header_b64, source_sha256):
+        """source_sha256: hex digest, or a Future of one (resolved at close)."""
         self.index["shards"].append(dict(name=name, header=header_b64, source_sha256=source_sha256, tensors=[]))
 
     def _encode(self, raw, off, rows, cols):
@@ -299,12 +301,25 @@ class ArchiveWriter:
                                     rows=rows if codec != "raw" else 0, cols=cols if codec != "raw" else 0,
                                     sha256=block_digests[i].result()))
             self.f.write(memoryview(data))
-        t["sha256"] = tensor_digest.result()
+        # the tensor digest is one sequential pass: collect it later, keeping
+        # a bounded number of tensors in flight
+        self._pending.append((t, tensor_digest))
+        while len(self._pending) > self._max_pending:
+            self._settle_one()
         self.index["shards"][shard]["tensors"].append(t)
         return t
 
+    def _settle_one(self):
+        t, fut = self._pending.pop(0)
+        t["sha256"] = fut.result()
+
     def close(self):
         """Writes the index and the header and moves the file into place."""
+        while self._pending:
+            self._settle_one()
+        for sh in self.index["shards"]:
+            if hasattr(sh["source_sha256"], "result"):
+                sh["source_sha256"] = sh["source_sha256"].result()
         offset = self.f.tell()
         self.f.write(json.dumps(self.index, separators=(",", ":"), ensure_ascii=False).encode())
         self.f.seek(0)
@@ -335,9 +350,8 @@ def compile_checkpoint(source, output, codec_preference="dfloat11", encoder="gpu
             fail("output would overwrite source")
     w = ArchiveWriter(output, codec_preference, encoder, device)
     try:
-        digests = [w.pool.submit(lambda p=s["path"]: _sha_file(p)) for s in shards]
-        for s, d in zip(shards, digests):
-            w.begin_shard(s["name"], s["header"], d.result())
+        for s in shards:
+            w.begin_shard(s["name"], s["header"], w.pool.submit(_sha_file, s["path"]))
         if Path(source).is_dir():
             for name in ASSET_NAMES:
                 p = Path(source) / name
@@ -345,14 +359,14 @@ def compile_checkpoint(source, output, codec_preference="dfloat11", encoder="gpu
                     if p.stat().st_size > 100_000_000:
                         fail(f"asset too large: {name}")
                     w.add_asset(name, p.read_bytes())
-        for i, s in enumerate(shards):
-            with open(s["path"], "rb") as src:
-                for t in s["tensors"]:
-                    src.seek(8 + s["header_size"] + t["start"])
-                    raw = np.empty(t["size"], dtype=np.uint8)
-                    if t["size"] and src.readinto(memoryview(raw)) != t["size"]:
-                        fail("unexpected end of file")
-                    w.add_tensor(t, raw, shard=i)
+        # the next tensor is read while the current one encodes
+        jobs = [(i, s, t) for i, s in enumerate(shards) for t in s["tensors"]]
+        with ThreadPoolExecutor(max_workers=1) as reader:
+            nxt = reader.submit(_read_tensor, *jobs[0][1:]) if jobs else None
+            for k, (i, s, t) in enumerate(jobs):
+                raw = nxt.result()
+                nxt = reader.submit(_read_tensor, *jobs[k + 1][1:]) if k + 1 < len(jobs) else None
+                w.add_tensor(t, raw, shard=i)
     except BaseException:
         w.abort()
         raise
@@ -363,6 +377,15 @@ def compile_checkpoint(source, output, codec_preference="dfloat11", encoder="gpu
         a.verify()
         a.close()
     return path
+
+
+def _read_tensor(shard, t):
+    raw = np.empty(t["size"], dtype=np.uint8)
+    with open(shard["path"], "rb") as f:
+        f.seek(8 + shard["header_size"] + t["start"])
+        if t["size"] and f.readinto(memoryview(raw)) != t["size"]:
+            fail("unexpected end of file")
+    return raw
 
 
 def _sha_file(path):

@@ -108,8 +108,23 @@ def load(path=None):
     return lib
 
 
+def slab_dtype():
+    """numpy structured dtype with the memory layout of xksv_slab."""
+    import numpy as np
+    return np.dtype({"names": [f for f, _ in Slab._fields_],
+                     "formats": ["<u8"] * 6 + ["<u4"] * 2,
+                     "offsets": [getattr(Slab, f).offset for f, _ in Slab._fields_],
+                     "itemsize": ctypes.sizeof(Slab)})
+
+
 def slab_table(entries):
-    """entries: iterable of dicts/tuples with the xksv_slab fields."""
+    """entries: iterable of dicts/tuples with the xksv_slab fields, or a
+    numpy array of slab_dtype() (used in place, no per-row Python work)."""
+    if hasattr(entries, "dtype") and entries.dtype == slab_dtype():
+        import numpy as np
+        arr = np.ascontiguousarray(entries)
+        # the pointer keeps a reference to the array
+        return arr.ctypes.data_as(ctypes.POINTER(Slab)), len(arr)
     entries = list(entries)
     arr = (Slab * max(1, len(entries)))()
     for i, e in enumerate(entries):
@@ -314,11 +329,15 @@ class TPComm:
 
 
 def sha256_ranges(ranges, d_base, d_digests, stream=0, lib=None):
-    """SHA-256 of device byte ranges [(offset, length), ...] at d_base into
-    d_digests (n * 32 bytes, device); xksv_cuda_sha256."""
+    """SHA-256 of device byte ranges [(offset, length), ...] (or an n x 2
+    integer array) at d_base into d_digests (n * 32 bytes, device);
+    xksv_cuda_sha256."""
+    import numpy as np
     lib = lib or load()
-    flat = (ctypes.c_uint64 * max(1, 2 * len(ranges)))(*[v for r in ranges for v in r])
-    if lib.xksv_cuda_sha256(flat, len(ranges), d_base, d_digests, stream):
+    flat = np.ascontiguousarray(np.asarray(ranges, dtype=np.uint64).reshape(-1))
+    n = flat.size // 2
+    ptr = flat.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
+    if lib.xksv_cuda_sha256(ptr, n, d_base, d_digests, stream):
         raise RuntimeError("xksv_cuda_sha256 failed")
 
 

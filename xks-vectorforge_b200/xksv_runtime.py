@@ -211,7 +211,8 @@ class ResidentArchive:
     decodes one; ``fused(name)`` returns a resident fused-GEMV/GEMM weight.
     """
 
-    def __init__(self, path, device="cuda", chunk_bytes=64 << 20):
+    def __init__(self, path, device="cuda", chunk_bytes=32 << 20, readers=8):
+        import numpy as np
         import torch
         self.path = str(path)
         self.device = torch.device(device)
@@ -222,60 +223,99 @@ class ResidentArchive:
         self.lib = xksv_gpu.load()
         with open(self.path, "rb") as f:
             self.index, self.limit = load_index(f)
-            self.tensors = check_index(self.index, self.limit)
-            self.assets = {a["name"]: a for a in self.index.get("assets", [])}
-            self.payload = self._upload(f, chunk_bytes)
+        self.tensors = check_index(self.index, self.limit)
+        self.assets = {a["name"]: a for a in self.index.get("assets", [])}
+        # every block once, as a slab-table template: payload offsets relative
+        # to byte 16, rows/cols 0 for raw blocks; per tensor its first block,
+        # block count, and each block's byte offset inside the tensor
+        blocks = [b for t in self.tensors.values() for b in t["blocks"]]
+        tab = np.zeros(len(blocks), dtype=xksv_gpu.slab_dtype())
+        if blocks:
+            tab["src_offset"] = np.fromiter((b["offset"] for b in blocks), np.uint64, len(blocks)) - HEADER.size
+            tab["src_size"] = np.fromiter((b["size"] for b in blocks), np.uint64, len(blocks))
+            tab["rows"] = np.fromiter((b["rows"] for b in blocks), np.uint64, len(blocks))
+            tab["cols"] = np.fromiter((b["cols"] for b in blocks), np.uint64, len(blocks))
+            tab["codec"] = np.fromiter((xksv_gpu.CODEC_BY_NAME[b["codec"]] for b in blocks), np.uint32, len(blocks))
+        raw = np.fromiter((b["raw_size"] for b in blocks), np.uint64, len(blocks))
+        self._raw = raw
+        self._block_sha = [b.get("sha256") for b in blocks]
+        self._table, self._first, self._nblocks = tab, {}, {}
+        self._local = np.zeros(len(blocks), dtype=np.uint64)
+        k = 0
+        for name, t in self.tensors.items():
+            n = len(t["blocks"])
+            self._first[name], self._nblocks[name] = k, n
+            if n:
+                self._local[k + 1:k + n] = np.cumsum(raw[k:k + n - 1])
+            k += n
+        self.payload = self._upload(chunk_bytes, readers)
         self._check_parallel_headers()
         self.verified = False
         self._plans = {}
 
-    # the block region, streamed through two pinned buffers
-    def _upload(self, f, chunk):
+    def _upload(self, chunk, readers):
+        """Reads the block region into HBM: `readers` threads each pread
+        chunk after chunk into their own two pinned buffers and copy them on
+        their own stream, so file reads and host->device copies overlap."""
         import torch
+        from concurrent.futures import ThreadPoolExecutor
         n = self.limit - HEADER.size
         dev = torch.empty(max(n, 1), dtype=torch.uint8, device=self.device)
         if not n:
             return dev
         chunk = max(1 << 20, min(chunk, n))
-        pins = [torch.empty(chunk, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
-        done = [None, None]
-        copy_stream = torch.cuda.Stream(self.device)
-        f.seek(HEADER.size)
-        pos, k = 0, 0
-        with torch.cuda.stream(copy_stream):
-            while pos < n:
-                m = min(chunk, n - pos)
-                if done[k] is not None:
-                    done[k].synchronize()  # the copy that last used this buffer
-                view = memoryview(pins[k].numpy())[:m]
-                got = f.readinto(view)
-                if got != m:
-                    fail("unexpected end of file")
-                dev[pos:pos + m].copy_(pins[k][:m], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(copy_stream)
-                done[k] = ev
-                pos += m
-                k ^= 1
-        copy_stream.synchronize()
+        chunks = [(pos, min(chunk, n - pos)) for pos in range(0, n, chunk)]
+        readers = max(1, min(readers, len(chunks), os.cpu_count() or 1))
+        fd = os.open(self.path, os.O_RDONLY)
+
+        def reader(tid):
+            with torch.cuda.device(self.device):
+                stream = torch.cuda.Stream(self.device)
+                pins = [torch.empty(chunk, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+                done = [None, None]
+                k = 0
+                for pos, m in chunks[tid::readers]:
+                    if done[k] is not None:
+                        done[k].synchronize()  # the copy that last used this buffer
+                    view = memoryview(pins[k].numpy())[:m]
+                    got = 0
+                    while got < m:
+                        r = os.preadv(fd, [view[got:]], HEADER.size + pos + got)
+                        if r <= 0:
+                            fail("unexpected end of file")
+                        got += r
+                    with torch.cuda.stream(stream):
+                        dev[pos:pos + m].copy_(pins[k][:m], non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record(stream)
+                    done[k] = ev
+                    k ^= 1
+                stream.synchronize()
+
+        try:
+            with ThreadPoolExecutor(max_workers=readers) as ex:
+                for fut in [ex.submit(reader, i) for i in range(readers)]:
+                    fut.result()
+        finally:
+            os.close(fd)
         return dev
 
     def _check_parallel_headers(self):
         """Parallel blocks' stored rows/cols must match the index
         (python/runtime.py:93, python/xksv.py:369)."""
+        import numpy as np
         import torch
-        blocks = [b for t in self.tensors.values() for b in t["blocks"]
-                  if b["codec"] == "bf16-huffman-parallel32"]
-        if not blocks:
+        tab = self._table
+        sel = np.nonzero(tab["codec"] == xksv_gpu.CODEC_PARALLEL32)[0]
+        if not len(sel):
             return
-        if any(b["size"] < 24 for b in blocks):
+        if (tab["src_size"][sel] < 24).any():
             fail("parallel block dimensions disagree with index")
-        off = torch.tensor([b["offset"] - HEADER.size + 8 for b in blocks], dtype=torch.int64, device=self.device)
+        off = torch.from_numpy((tab["src_offset"][sel] + 8).astype(np.int64)).to(self.device)
         idx = off[:, None] + torch.arange(16, device=self.device)
         got = self.payload[idx].cpu().numpy().view("<u8").reshape(-1, 2)
-        for b, (r, c) in zip(blocks, got):
-            if (int(r), int(c)) != (b["rows"], b["cols"]):
-                fail("parallel block dimensions disagree with index")
+        if (got[:, 0] != tab["rows"][sel]).any() or (got[:, 1] != tab["cols"][sel]).any():
+            fail("parallel block dimensions disagree with index")
 
     @property
     def payload_ptr(self):
@@ -301,19 +341,41 @@ class ResidentArchive:
             pos += -(-self.tensors[name]["size"] // TENSOR_ALIGN) * TENSOR_ALIGN
         return offs, pos
 
-    def _decode_into(self, names, offs, out, stream):
-        entries = []
-        for name in names:
-            entries += decode_entries(self.tensors[name]["blocks"], offs[name])
-        if not entries:
+    def _decode_table(self, names, offs):
+        """(slab table decoding `names` to their offsets `offs`, the blocks'
+        indices in archive order)."""
+        import numpy as np
+        idx = [np.arange(self._first[n], self._first[n] + self._nblocks[n]) for n in names]
+        idx = np.concatenate(idx) if idx else np.zeros(0, np.int64)
+        tab = self._table[idx]
+        counts = [self._nblocks[n] for n in names]
+        base = np.repeat(np.array([offs[n] for n in names], dtype=np.uint64), counts)
+        tab["dst_offset"] = base + self._local[idx]
+        return tab, idx
+
+    def _decode_plan(self, names, offs):
+        key = tuple(names)
+        plan = self._plans.get(key)
+        if plan is None:
+            tab, _ = self._decode_table(names, offs)
+            if not len(tab):
+                return None
+            plan = xksv_gpu.Plan(tab, lib=self.lib)
+            self._plans[key] = plan
+        return plan
+
+    def _decode_into(self, names, offs, out, stream, keep=True):
+        plan = self._decode_plan(names, offs)
+        if plan is None:
             return
-        plan = xksv_gpu.Plan(entries, lib=self.lib)
         try:
             plan.decode(self.payload_ptr, out.data_ptr(), stream)
             if plan.status(stream):
                 fail(f"GPU block decode failed: {names[0] if len(names) == 1 else 'archive'}")
         finally:
-            plan.close()
+            if not keep:
+                self._plans.pop(tuple(names), None)
+                plan.close()
 
     def _stream(self):
         import torch
@@ -340,12 +402,19 @@ class ResidentArchive:
             fail(f"archive lacks tensor {name}")
         return self.decode_all([name])[name]
 
-    def verify(self, max_scratch=8 << 30):
+    def verify(self, max_scratch=4 << 30):
         """Decodes every block on the device and checks the SHA-256 of each
         block and of each tensor against the index (python/xksv.py:361-375),
-        plus the assets on the host.  Tensors are processed in groups whose
+        plus the assets on the host.  Block digests (at most 1 MiB each, many
+        independent messages) run on the device, one thread per block; a
+        tensor digest is one sequential message of up to gigabytes, which one
+        GPU thread hashes at tens of MB/s against GB/s for a host core with
+        SHA instructions, so those run on host threads over one device->host
+        copy of the decoded group.  Tensors are processed in groups whose
         decoded bytes fit `max_scratch`.  Returns (tensors, bytes)."""
+        import numpy as np
         import torch
+        from concurrent.futures import ThreadPoolExecutor
         for name in self.assets:
             self.asset(name)
         names = list(self.tensors)
@@ -360,37 +429,40 @@ class ResidentArchive:
         if cur:
             groups.append(cur)
         nbytes = 0
-        with torch.cuda.device(self.device):
-            stream = self._stream()
-            for group in groups:
-                offs, total = self._layout(group)
-                flat = torch.empty(max(total, 1), dtype=torch.uint8, device=self.device)
-                self._decode_into(group, offs, flat, stream)
-                # one range per block and one per tensor; the long tensor
-                # ranges first so their threads start early
-                ranges, want, what = [], [], []
-                for name in sorted(group, key=lambda n: -self.tensors[n]["size"]):
-                    t = self.tensors[name]
-                    ranges.append((offs[name], t["size"]))
-                    want.append(t.get("sha256"))
-                    what.append(f"tensor verification failed: {name}")
-                for name in group:
-                    pos = offs[name]
-                    for b in self.tensors[name]["blocks"]:
-                        ranges.append((pos, b["raw_size"]))
-                        want.append(b.get("sha256"))
-                        what.append(f"block checksum failed: {name}")
-                        pos += b["raw_size"]
-                dig = torch.empty(32 * len(ranges), dtype=torch.uint8, device=self.device)
-                xksv_gpu.sha256_ranges(ranges, flat.data_ptr(), dig.data_ptr(), stream, lib=self.lib)
-                got = dig.cpu().numpy().tobytes()
-                # report block failures before the tensor that holds them
-                order = list(range(len(group), len(ranges))) + list(range(len(group)))
-                for i in order:
-                    if got[32 * i:32 * i + 32].hex() != want[i]:
-                        fail(what[i])
-                nbytes += sum(self.tensors[n]["size"] for n in group)
-                del flat
+        pool = ThreadPoolExecutor(max_workers=max(1, min(32, os.cpu_count() or 1)))
+        try:
+            with torch.cuda.device(self.device):
+                stream = self._stream()
+                for group in groups:
+                    offs, total = self._layout(group)
+                    flat = torch.empty(max(total, 1), dtype=torch.uint8, device=self.device)
+                    self._decode_into(group, offs, flat, stream, keep=len(groups) == 1)
+                    # block digests on the device, one thread per block
+                    tab, idx = self._decode_table(group, offs)
+                    if len(idx):
+                        ranges = np.stack([tab["dst_offset"], self._raw[idx]], axis=1)
+                        dig = torch.empty(32 * len(idx), dtype=torch.uint8, device=self.device)
+                        xksv_gpu.sha256_ranges(ranges, flat.data_ptr(), dig.data_ptr(), stream, lib=self.lib)
+                        got = dig.cpu().numpy().tobytes()
+                        for j, i in enumerate(idx):
+                            if got[32 * j:32 * j + 32].hex() != self._block_sha[i]:
+                                name = next(n for n in group
+                                            if self._first[n] <= i < self._first[n] + self._nblocks[n])
+                                fail(f"block checksum failed: {name}")
+                    # tensor digests on host threads, largest first; each
+                    # tensor's copy overlaps the hashing of the previous ones
+                    order = sorted(group, key=lambda n: -self.tensors[n]["size"])
+                    futs = []
+                    for n in order:
+                        host = flat[offs[n]:offs[n] + self.tensors[n]["size"]].cpu().numpy()
+                        futs.append(pool.submit(lambda h=host: hashlib.sha256(memoryview(h)).hexdigest()))
+                    for name, fut in zip(order, futs):
+                        if fut.result() != self.tensors[name].get("sha256"):
+                            fail(f"tensor verification failed: {name}")
+                    nbytes += sum(self.tensors[n]["size"] for n in group)
+                    del flat
+        finally:
+            pool.shutdown()
         self.verified = True
         return len(names), nbytes
 
