@@ -211,8 +211,9 @@ class ArchiveWriter:
     tensor order, JSON index.  ``encoder`` is "gpu" (xksv_cuda_pack_tensor on
     `device`) or "host" (xksv_host_pack_tensor on all cores)."""
 
-    def __init__(self, output, codec_preference="dfloat11", encoder="gpu", device="cuda:0", threads=0):
-        if codec_preference not in CODEC_NAMES:
+    def __init__(self, output, codec_preference="dfloat11", encoder="gpu", device="cuda:0", threads=0,
+                 tuning=None):
+        if codec_preference not in CODEC_NAMES and codec_preference != "autotune":
             fail(f"unsupported codec preference: {codec_preference}")
         if encoder not in ("gpu", "host"):
             fail(f"unknown encoder: {encoder}")
@@ -222,8 +223,16 @@ class ArchiveWriter:
         self.partial = self.output.with_name(self.output.name + ".partial")
         if self.partial.exists():
             fail("partial compilation exists; choose another output")
-        self.codec_name = CODEC_NAMES[codec_preference]
-        self.codec = xksv_gpu.CODEC_BY_NAME[self.codec_name]
+        # autotune: both codecs are encoded and the tuner picks per block
+        # (python/xksv.py:206-208, 269, 274-275)
+        self.tuner = None
+        if codec_preference == "autotune":
+            import xksv_tune
+            self.tuner = xksv_tune.GpuTuner(tuning, device)
+            self.codec_name, self.codec = None, None
+        else:
+            self.codec_name = CODEC_NAMES[codec_preference]
+            self.codec = xksv_gpu.CODEC_BY_NAME[self.codec_name]
         self.encoder, self.device, self.threads = encoder, device, threads
         self.lib = xksv_gpu.load()
         self.pool = ThreadPoolExecutor(max_workers=max(2, min(32, os.cpu_count() or 2)))
@@ -233,6 +242,8 @@ class ArchiveWriter:
         self.f.write(HEADER.pack(MAGIC, 0))
         self.index = dict(version=1, format="safetensors", codec_preference=codec_preference, shards=[],
                           assets=[])
+        if self.tuner:
+            self.index["tuning"] = self.tuner.profile
 
     def add_asset(self, name, data):
         self.index["assets"].append(dict(name=name, offset=self.f.tell(), size=len(data),
@@ -243,19 +254,19 @@ class ArchiveWriter:
         """source_sha256: hex digest, or a Future of one (resolved at close)."""
         self.index["shards"].append(dict(name=name, header=header_b64, source_sha256=source_sha256, tensors=[]))
 
-    def _encode(self, raw, off, rows, cols):
+    def _encode(self, raw, off, rows, cols, codec):
         """(payload bytes, slab dicts) of rows x cols BF16 at raw[off:]."""
         nbytes = rows * cols * 2
         if self.encoder == "host":
             ptr = raw.ctypes.data + off
-            payload, slabs = xksv_gpu.host_pack_tensor(ptr, nbytes, rows, cols, self.codec, self.threads,
+            payload, slabs = xksv_gpu.host_pack_tensor(ptr, nbytes, rows, cols, codec, self.threads,
                                                        0, lib=self.lib)
             return payload, slabs
         import torch
         d = torch.from_numpy(raw[off:off + nbytes]).to(self.device)
         with torch.cuda.device(d.device):
             stream = torch.cuda.current_stream().cuda_stream
-            ptr, n, slabs = xksv_gpu.cuda_pack_tensor(d.data_ptr(), rows, cols, self.codec, 0, stream,
+            ptr, n, slabs = xksv_gpu.cuda_pack_tensor(d.data_ptr(), rows, cols, codec, 0, stream,
                                                       lib=self.lib)
             try:
                 payload = torch.as_tensor(_DevicePayload(ptr, n), device=d.device).cpu().numpy() if n else \
@@ -278,25 +289,37 @@ class ArchiveWriter:
         tensor_digest = self.pool.submit(lambda: hashlib.sha256(raw).hexdigest())
         block_digests = [self.pool.submit(lambda o=o, n=n: hashlib.sha256(raw[o:o + n]).hexdigest())
                          for o, n, _, _ in layout]
-        encoded = {}
+        codecs = ([xksv_gpu.CODEC_TILE16, xksv_gpu.CODEC_PARALLEL32] if self.tuner else [self.codec])
+        encoded = {c: {} for c in codecs}
         for off, rows, cols, nblocks in coded_runs(layout):
-            payload, slabs = self._encode(raw, off, rows, cols)
-            if len(slabs) != nblocks:
-                fail(f"encoder block split differs from the compiler's: {desc['name']}")
-            for s in slabs:
-                encoded[off + s["dst_offset"]] = (s, payload)
-        for i, (off, length, rows, cols) in enumerate(layout):
-            if rows:
-                s, payload = encoded.get(off, (None, None))
-                if s is None or s["rows"] != rows or s["cols"] != cols:
+            for c in codecs:
+                payload, slabs = self._encode(raw, off, rows, cols, c)
+                if len(slabs) != nblocks:
                     fail(f"encoder block split differs from the compiler's: {desc['name']}")
-                if s["codec"] != xksv_gpu.CODEC_RAW:
-                    data = payload[s["src_offset"]:s["src_offset"] + s["src_size"]]
-                    codec = self.codec_name
-                else:
-                    data, codec = raw[off:off + length], "raw"
-            else:
-                data, codec = raw[off:off + length], "raw"
+                for s in slabs:
+                    encoded[c][off + s["dst_offset"]] = (s, payload)
+
+        def blob(c, off, rows, cols, length):
+            """The block's encoding under codec c, or None when the encoding
+            is not smaller than the raw bytes (the encoder's raw fallback)."""
+            s, payload = encoded[c].get(off, (None, None))
+            if s is None or s["rows"] != rows or s["cols"] != cols:
+                fail(f"encoder block split differs from the compiler's: {desc['name']}")
+            if s["codec"] == xksv_gpu.CODEC_RAW:
+                return None
+            return payload[s["src_offset"]:s["src_offset"] + s["src_size"]]
+
+        for i, (off, length, rows, cols) in enumerate(layout):
+            data, codec = raw[off:off + length], "raw"
+            if rows and self.tuner:
+                ser = blob(xksv_gpu.CODEC_TILE16, off, rows, cols, length)
+                par = blob(xksv_gpu.CODEC_PARALLEL32, off, rows, cols, length)
+                codec, data = self.tuner.select(data if ser is None else ser, data if par is None else par,
+                                                data, rows, cols)
+            elif rows:
+                enc = blob(self.codec, off, rows, cols, length)
+                if enc is not None:
+                    data, codec = enc, self.codec_name
             t["blocks"].append(dict(offset=self.f.tell(), size=int(data.size), raw_size=length, codec=codec,
                                     rows=rows if codec != "raw" else 0, cols=cols if codec != "raw" else 0,
                                     sha256=block_digests[i].result()))
@@ -339,16 +362,19 @@ class ArchiveWriter:
             self.partial.unlink()
 
 
-def compile_checkpoint(source, output, codec_preference="dfloat11", encoder="gpu", device="cuda:0", verify=True):
+def compile_checkpoint(source, output, codec_preference="dfloat11", encoder="gpu", device="cuda:0", verify=True,
+                       tuning=None):
     """``compile_model(source, output, codec_preference=...)`` on this
-    library's encoders.  With `verify`, the archive is then loaded and checked
-    on the device (every block decoded, every SHA-256 compared)."""
+    library's encoders; codec_preference "dfloat11", "dfloat11-parallel" or
+    "autotune" (GpuTuner per block; `tuning` resumes a saved profile).  With
+    `verify`, the archive is then loaded and checked on the device (every
+    block decoded, every SHA-256 compared)."""
     shards = checkpoint(source)
     output = Path(output).absolute()
     for s in shards:
         if Path(s["path"]).resolve() == output.resolve():
             fail("output would overwrite source")
-    w = ArchiveWriter(output, codec_preference, encoder, device)
+    w = ArchiveWriter(output, codec_preference, encoder, device, tuning=tuning)
     try:
         for s in shards:
             w.begin_shard(s["name"], s["header"], w.pool.submit(_sha_file, s["path"]))
