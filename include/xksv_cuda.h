@@ -91,6 +91,19 @@ void xksv_plan_destroy(xksv_plan* plan);
  * are found by xksv_plan_status(). */
 int xksv_plan_decode(const xksv_plan* plan, const void* d_payload, void* d_out, void* stream);
 
+/* The same decode from a HOST payload (pinned memory for overlap): the first
+ * payload_size bytes at h_payload are copied into d_payload (device, at least
+ * as large) in 8 pieces on a plan-owned stream while the slabs of each piece
+ * that has landed are decoded on `stream`, so the copy and the decode
+ * overlap.  The copies wait for work already enqueued on `stream`.  Needs
+ * each codec's slabs in increasing payload order (an archive's block order;
+ * otherwise, and for a plan indexed on d_payload, it copies once and then
+ * decodes).  Returns 1 as xksv_plan_decode does, and when a slab lies past
+ * payload_size.  No reference counterpart (the reference stages one slab per
+ * blocking call, cuda/decode.cu:47-83). */
+int xksv_plan_decode_host(const xksv_plan* plan, const void* h_payload, size_t payload_size,
+                          void* d_payload, void* d_out, void* stream);
+
 /* Enqueues Y[dst_offset + r, b] = sum_c W[r, c] * X[x_offset + c, b] for every
  * slab, X FP32 row-major [*, batch] and Y FP32 row-major [*, batch] (rows of
  * Y not covered by a slab are left untouched). */

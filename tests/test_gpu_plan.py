@@ -150,3 +150,36 @@ def test_misaligned_outputs_are_refused(xg):
     assert ok.status() == 0
     assert d_out[:len(raw)].cpu().numpy().tobytes() == raw
     ok.close()
+
+
+@pytest.mark.parametrize("order", ["archive", "shuffled"])
+def test_plan_decode_host_matches_device_decode(xg, order):
+    """xksv_plan_decode_host: pinned host payload copied in pieces while the
+    landed slabs decode (archive order), or one copy then the decode
+    (shuffled table): both bit-exact; a payload_size short of the last slab
+    is refused."""
+    oracle = Oracle()
+    rng = np.random.default_rng(9)
+    shapes = [(16, 2048), (16, 5632), (1, 2048), (16, 4096), (7, 19), (16, 32), (16, 4097), (33, 35)] * 8
+    kinds = ["normal002", "student3", "single", "normal1e4", "uniform", "three_exp"] * 11
+    payload, entries, raws = build_archive(oracle, shapes, kinds, rng)
+    if order == "shuffled":
+        idx = rng.permutation(len(entries))
+        entries, raws = [entries[i] for i in idx], [raws[i] for i in idx]
+    h_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).pin_memory()
+    d_payload = torch.empty(len(payload), dtype=torch.uint8, device="cuda")
+    total = sum(len(r) for r in raws)
+    d_out = torch.full((total + 64,), 0xCD, dtype=torch.uint8, device="cuda")
+    plan = xg.Plan(entries)
+    for _ in range(2):  # the second call reuses the plan's copy stream and events
+        d_out.fill_(0xCD)
+        plan.decode_host(h_payload.data_ptr(), len(payload), d_payload.data_ptr(), d_out.data_ptr())
+        assert plan.status() == 0
+        got = d_out.cpu().numpy().tobytes()
+        for e, raw in zip(entries, raws):
+            assert got[e["dst_offset"]:e["dst_offset"] + len(raw)] == raw
+    assert plan.launches() >= (4 if order == "archive" else 1)
+    short = max(e["src_offset"] + e["src_size"] for e in entries) - 1
+    assert xg.load().xksv_plan_decode_host(plan.handle, h_payload.data_ptr(), short, d_payload.data_ptr(),
+                                           d_out.data_ptr(), None) == 1
+    plan.close()

@@ -202,6 +202,9 @@ struct xksv_plan {
   uint8_t* d_scratch = nullptr;
   void* d_xt = nullptr;  // BF16 X^T [256][x_cols]
   uint64_t* d_hash_ranges = nullptr;  // per slab in creation order: {dst, decoded bytes}
+  // xksv_plan_decode_host: copy stream and per-chunk events (created on first use)
+  cudaStream_t copy_st = nullptr;
+  cudaEvent_t chunk_ev[9] = {};
 };
 
 namespace {
@@ -440,6 +443,9 @@ void xksv_plan_destroy(xksv_plan* p) {
   if (p->d_slabs) cudaFree(p->d_slabs);
   if (p->d_status) cudaFree(p->d_status);
   if (p->h_status) cudaFreeHost(p->h_status);
+  for (cudaEvent_t ev : p->chunk_ev)
+    if (ev) cudaEventDestroy(ev);
+  if (p->copy_st) cudaStreamDestroy(p->copy_st);
   delete p;
 }
 
@@ -489,6 +495,92 @@ int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, vo
   if (e == cudaSuccess && p->n_raw) {
     e = launch_raw_decode(p->d_slabs + p->n_ser + p->n_par, p->n_raw, pay, out, p->grid_raw, st);
     ++p->launches;
+  }
+  return e == cudaSuccess ? 0 : 1;
+}
+
+
+// Host payload -> device -> decode, with the copy and the decode overlapped:
+// the payload crosses PCIe in kHostChunks pieces on the plan's copy stream,
+// and the slabs that end inside each piece are decoded on the caller's
+// stream as soon as it has landed (event wait), so only the last piece's
+// decode is exposed.  Needs each codec group's slabs in increasing payload
+// order (an archive's block order); otherwise one copy, then the decode.
+namespace {
+constexpr int kHostChunks = 8;
+static_assert(sizeof(xksv_plan::chunk_ev) / sizeof(cudaEvent_t) == kHostChunks + 1, "one event per chunk + 1");
+uint64_t chunk_end(uint64_t end, int c) {  // end * (c + 1) / kHostChunks without overflow
+  const uint64_t q = end / kHostChunks, r = end % kHostChunks;
+  return q * uint64_t(c + 1) + r * uint64_t(c + 1) / kHostChunks;
+}
+}  // namespace
+
+int xksv_plan_decode_host(const xksv_plan* pc, const void* h_payload, size_t payload_size, void* d_payload,
+                          void* d_out, void* stream) {
+  auto* p = const_cast<xksv_plan*>(pc);
+  if (!p || !h_payload || !d_payload || !d_out || p->odd_dst || misaligned(d_out, 2)) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto& hs = p->h_slabs;
+  uint64_t end = 0;
+  for (const Slab& s : hs) end = std::max(end, s.src + s.size);
+  if (end > payload_size) return 1;  // a slab outside the host payload
+  // groups: tile-indexable serial slabs, the other serial slabs (plan
+  // creation keeps each part in table order), parallel, raw
+  constexpr int NG = 4;
+  const uint32_t lo[NG] = {0, p->n_ser_idx, p->n_ser, p->n_ser + p->n_par};
+  const uint32_t hi[NG] = {p->n_ser_idx, p->n_ser, p->n_ser + p->n_par, p->n_ser + p->n_par + p->n_raw};
+  const bool indexed = p->d_tidx && d_payload == p->indexed_payload && p->n_items;
+  bool ordered = !indexed && end > 0;
+  for (int g = 0; g < NG && ordered; ++g)
+    for (uint32_t i = lo[g] + 1; i < hi[g] && ordered; ++i)
+      ordered = hs[i].src + hs[i].size >= hs[i - 1].src + hs[i - 1].size;
+  if (!ordered) {
+    if (end && cudaMemcpyAsync(d_payload, h_payload, end, cudaMemcpyHostToDevice, st) != cudaSuccess) return 1;
+    return xksv_plan_decode(p, d_payload, d_out, stream);
+  }
+  if (!p->copy_st && cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking) != cudaSuccess) return 1;
+  for (cudaEvent_t& ev : p->chunk_ev)
+    if (!ev && cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return 1;
+  const uint8_t* h = static_cast<const uint8_t*>(h_payload);
+  uint8_t* pay = static_cast<uint8_t*>(d_payload);
+  uint8_t* out = static_cast<uint8_t*>(d_out);
+  // the copies must not overwrite bytes that earlier work on `st` still reads
+  cudaError_t e = cudaEventRecord(p->chunk_ev[kHostChunks], st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(p->copy_st, p->chunk_ev[kHostChunks], 0);
+  uint64_t a = 0;
+  for (int c = 0; c < kHostChunks && e == cudaSuccess; ++c) {
+    const uint64_t b = chunk_end(end, c);
+    if (b > a) e = cudaMemcpyAsync(pay + a, h + a, b - a, cudaMemcpyHostToDevice, p->copy_st);
+    if (e == cudaSuccess) e = cudaEventRecord(p->chunk_ev[c], p->copy_st);
+    a = b;
+  }
+  p->launches = 0;
+  uint32_t done[NG] = {lo[0], lo[1], lo[2], lo[3]};
+  for (int c = 0; c < kHostChunks && e == cudaSuccess; ++c) {
+    const uint64_t b = chunk_end(end, c);
+    uint32_t upto[NG];
+    bool any = false;
+    for (int g = 0; g < NG; ++g) {
+      upto[g] = done[g];
+      while (upto[g] < hi[g] && hs[upto[g]].src + hs[upto[g]].size <= b) ++upto[g];
+      any = any || upto[g] > done[g];
+    }
+    if (!any) continue;
+    e = cudaStreamWaitEvent(st, p->chunk_ev[c], 0);
+    for (int g = 0; g < 2 && e == cudaSuccess; ++g)
+      if (upto[g] > done[g]) {
+        e = launch_serial_decode(p->d_slabs + done[g], upto[g] - done[g], pay, out, p->d_status, p->grid_ser, st);
+        ++p->launches;
+      }
+    if (e == cudaSuccess && upto[2] > done[2]) {
+      e = launch_parallel_decode(p->d_slabs + done[2], upto[2] - done[2], pay, out, p->d_status, p->grid_par, st);
+      ++p->launches;
+    }
+    if (e == cudaSuccess && upto[3] > done[3]) {
+      e = launch_raw_decode(p->d_slabs + done[3], upto[3] - done[3], pay, out, p->grid_raw, st);
+      ++p->launches;
+    }
+    for (int g = 0; g < NG; ++g) done[g] = upto[g];
   }
   return e == cudaSuccess ? 0 : 1;
 }

@@ -40,6 +40,8 @@ _SIGS = {
     "xksv_plan_destroy": ([ctypes.c_void_p], None),
     "xksv_plan_decode": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
                          ctypes.c_int),
+    "xksv_plan_decode_host": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                               ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                         ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
@@ -211,6 +213,12 @@ class Plan:
     def decode(self, d_payload, d_out, stream=0):
         if self.lib.xksv_plan_decode(self.handle, d_payload, d_out, stream):
             raise RuntimeError("xksv_plan_decode launch failed")
+
+    def decode_host(self, h_payload, size, d_payload, d_out, stream=0):
+        """Host payload -> d_payload -> decode, copy and decode overlapped
+        (xksv_plan_decode_host)."""
+        if self.lib.xksv_plan_decode_host(self.handle, h_payload, size, d_payload, d_out, stream):
+            raise RuntimeError("xksv_plan_decode_host failed")
 
     def gemm(self, d_payload, d_x, d_y, batch, stream=0):
         if self.lib.xksv_plan_gemm(self.handle, d_payload, d_x, d_y, batch, stream):
