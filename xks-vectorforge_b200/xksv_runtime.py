@@ -474,6 +474,10 @@ class ResidentArchive:
         return FusedWeight(self, t)
 
     def close(self):
+        """Releases the resident payload and the cached decode plans."""
+        for plan in self._plans.values():
+            plan.close()
+        self._plans.clear()
         self.payload = None
 
 
