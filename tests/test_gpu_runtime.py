@@ -114,6 +114,9 @@ def test_fused_llama_matches_decoded_model():
     assert tok is None  # the fixture has no tokenizer files
     fused = [n for n, m in model.named_modules() if hasattr(m, "xksv_fused")]
     assert len(fused) == 7
+    # fused weights stay compressed: their parameters hold no decoded bytes
+    mods = dict(model.named_modules())
+    assert all(mods[n].weight.numel() == 0 for n in fused)
     ids = torch.tensor([[3, 17, 99, 4, 64, 1, 127]], device="cuda:0")
     with torch.no_grad():
         for inp in (ids[:, :1], ids):

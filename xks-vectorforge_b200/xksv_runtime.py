@@ -606,10 +606,20 @@ def load_archive(path, device, model=None, verify=True, fused_gemv=False):
             if any((Path(assets) / n).is_file() for n in ("tokenizer.json", "tokenizer.model", "vocab.json")):
                 tokenizer = AutoTokenizer.from_pretrained(assets, local_files_only=True, trust_remote_code=False)
     model.eval()
-    assign_tensors(model, archive.decode_all())
+    # fused linears keep their weights compressed in HBM: those tensors are
+    # not decoded, and the parameter becomes a zero-element placeholder (the
+    # fused forward never reads it), so the model holds the compressed bytes
+    # once instead of compressed + decoded
+    fused = [n + ".weight" for n in fused_candidates(model, archive.tensors)] if fused_gemv else []
+    if fused_gemv and not fused:
+        fail("no compatible linear layers for fused GEMV")
+    keep = [n for n in archive.tensors if n not in set(fused)]
+    tensors = archive.decode_all(keep)
+    for name in fused:
+        tensors[name] = torch.empty(0, dtype=torch.bfloat16, device=archive.device)
+    assign_tensors(model, tensors)
     model.to(archive.device)
     if fused_gemv:
-        if not install_fused_gemv(model, archive):
-            fail("no compatible linear layers for fused GEMV")
+        install_fused_gemv(model, archive)
     torch.cuda.synchronize(archive.device)
     return model, tokenizer, archive
