@@ -422,6 +422,404 @@ def run_case(args):
     print(json.dumps(line), flush=True)
 
 
+CONFIG4 = dict(hidden=8192, layers=80, q_heads=64, kv_heads=8, head_dim=128, ffn=28672, vocab=128256)
+
+
+class _DeviceBytes:
+    """Zero-copy torch view of library-allocated device bytes."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+def device_archive(specs, codec, dev, stream, bound):
+    """Encodes tensors on the GPU (xksv_cuda_pack_tensor) into one device
+    payload.  specs: (name, rows, cols, make) with make() -> BF16 [rows, cols]
+    on `dev`.  The payload buffer is allocated once at `bound` x the raw bytes
+    (each tensor's slabs start 16-byte aligned).  Returns (payload, [dict(name,
+    rows, cols, slabs)], compressed bytes, raw bytes)."""
+    import torch
+    import xksv_gpu
+    raw = sum(r * c * 2 for _, r, c, _ in specs)
+    buf = torch.empty(int(raw * bound) + (64 << 20), dtype=torch.uint8, device=dev)
+    h = stream.cuda_stream
+    pos, info = 0, []
+    for name, rows, cols, make in specs:
+        t = make()
+        stream.wait_stream(torch.cuda.current_stream(dev))  # t is made on the current stream
+        with torch.cuda.stream(stream):
+            ptr, n, sl = xksv_gpu.cuda_pack_tensor(t.data_ptr(), rows, cols, codec, 0, h)
+            try:
+                if pos + n > buf.numel():
+                    raise RuntimeError("compressed payload exceeds its preallocated bound")
+                if n:
+                    buf[pos:pos + n].copy_(torch.as_tensor(_DeviceBytes(ptr, n), device=dev))
+            finally:
+                xksv_gpu.free_device(ptr)
+        for s in sl:
+            s["src_offset"] += pos
+        info.append(dict(name=name, rows=rows, cols=cols, slabs=sl))
+        pos = (pos + n + 15) // 16 * 16
+        del t
+    stream.synchronize()
+    return buf, info, pos, raw
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _max_over_ranks(v, world, dev):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def config4_specs(world, rank, dev, sigma=0.015, seed=3):
+    """The Llama-3-70B tensors in checkpoint order, this
+    rank's rows (whole 16-row slabs; the 1-row norms on rank 0), generated on
+    the GPU from one seeded stream (every rank draws the full tensors, so the
+    shards partition one model)."""
+    import torch
+    import xksv_gpu
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    out = []
+    for name, rows, cols, kind in llama_tensors(**CONFIG4):
+        if kind == "norm":
+            if rank == 0:
+                out.append((name, rows, cols, lambda r=rows, c=cols: torch.ones(r, c, dtype=torch.bfloat16, device=dev)))
+            continue
+        r0, r1 = xksv_gpu.shard_rows(rows, world, rank)
+
+        def make(rows=rows, cols=cols, r0=r0, r1=r1):
+            full = (torch.randn(rows, cols, generator=gen, device=dev) * sigma).to(torch.bfloat16)
+            return full[r0:r1].contiguous()
+        out.append((name, r1 - r0, cols, make))
+    return out
+
+
+def run_config4_decode(args):
+    """`--case config4-decode`: whole-model decode of the Llama-3-70B-shaped
+    model, `dfloat11-parallel`, row-sharded over the
+    ranks.  The rank's compressed shard (~94 GB / N) is resident; a step
+    decodes every slab once, layer by layer (one plan per layer), into an
+    output buffer reused by every layer (compressed + decoded = 235 GB does
+    not fit one GPU).  Before timing, every decoded tensor is compared bit for
+    bit with its source regenerated from the seed."""
+    import torch
+    import xksv_gpu
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device(dev))
+    xksv_gpu.load()
+    stream = torch.cuda.Stream(device=dev)
+    h = stream.cuda_stream
+    t0 = time.perf_counter()
+    specs = config4_specs(world, rank, dev)
+    payload, info, comp, raw = device_archive(specs, 2, dev, stream, 0.78)
+    build_s = time.perf_counter() - t0
+    # one plan per 4 layers (embed and lm_head with the first and last): a
+    # launch of ~10 waves keeps each plan's tail short; within a plan the
+    # longest slabs start first
+    groups, cur, nl = [], [], 0
+    for t in info:
+        cur.append(t)
+        if t["name"].endswith("post_attention_layernorm.weight"):
+            nl += 1
+            if nl % 4 == 0:
+                groups.append(cur)
+                cur = []
+    if cur:
+        groups.append(cur)
+    plans, spans, max_out = [], [], 0
+    for g in groups:
+        entries, base, span = [], 0, []
+        for t in g:
+            for s in t["slabs"]:
+                e = dict(s)
+                e["dst_offset"] = base + s["dst_offset"]
+                entries.append(e)
+            span.append((t["name"], base, t["rows"] * t["cols"] * 2))
+            base += (t["rows"] * t["cols"] * 2 + 255) // 256 * 256
+        entries.sort(key=lambda e: -e["src_size"])
+        plans.append(xksv_gpu.Plan(entries))
+        spans.append(span)
+        max_out = max(max_out, base)
+    out = torch.empty(max_out, dtype=torch.uint8, device=dev)
+
+    def step():
+        for pl in plans:
+            pl.decode(payload.data_ptr(), out.data_ptr(), h)
+
+    # bit-exact check of every tensor against its regenerated source
+    check = config4_specs(world, rank, dev)
+    k = 0
+    mismatches = 0
+    with torch.cuda.stream(stream):
+        for pl, span in zip(plans, spans):
+            pl.decode(payload.data_ptr(), out.data_ptr(), h)
+            if pl.status(h):
+                raise RuntimeError("decode reported a slab error")
+            for name, off, n in span:
+                _, rows, cols, make = check[k]
+                assert name == check[k][0]
+                src = make().view(torch.int16).reshape(-1)
+                got = out[off:off + n].view(torch.int16)
+                mismatches += int(not torch.equal(src, got))
+                k += 1
+    if mismatches:
+        raise RuntimeError(f"{mismatches} tensors differ from their source")
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        t = time_steps(step, args.steps, stream)
+    t = _max_over_ranks(t, world, dev)
+    bad = sum(pl.status(h) for pl in plans)
+    ms = t / args.steps * 1e3
+    peak, peak_src = measured_peak()
+    line = dict(case="config4-decode", config="configs[3] Llama-3-70B shapes, N(0,0.015) seed 3, dfloat11-parallel, "
+                "rows sharded in whole slabs", n_gpus=world, steps=args.steps, ms_per_step=round(ms, 3),
+                per_rank_out_bytes=raw, per_rank_compressed_bytes=comp,
+                value=round(world * raw / (ms / 1e3) / 1e9, 1), unit="GB/s BF16 out (all ranks)",
+                per_gpu_out_gbs=round(raw / (ms / 1e3) / 1e9, 1),
+                roofline=dict(bound="hbm", achieved=round((raw + comp) / (ms / 1e3) / 1e9, 1), peak=peak,
+                              frac=round((raw + comp) / (ms / 1e3) / 1e9 / peak, 4), peak_source=peak_src),
+                launches_per_step=sum(pl.launches() for pl in plans), plans=len(plans),
+                bit_exact_tensors=len(check), status_errors=bad, build_s=round(build_s, 1),
+                note="output buffer reused per 4-layer plan; inputs larger than L2")
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for pl in plans:
+        pl.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_config4_gemv(args):
+    """`--case config4-gemv`: fused decode-GEMV/GEMM over the linears of the
+    Llama-3-70B-shaped model, `dfloat11` with the tile
+    index, 1 GPU: the full forward of linears (320 dependent plan launches,
+    one CUDA graph) at batch 1 and 4 on the CUDA cores, and layer 0's four
+    linear groups at batch 8 and 16 on the tensor cores (the tensor-core path
+    decodes a plan's weights into a per-plan BF16 scratch, which for all 80
+    layers would not fit next to the resident archive)."""
+    import torch
+    import xksv_gpu
+    torch.cuda.set_device(0)
+    dev = "cuda:0"
+    xksv_gpu.load()
+    stream = torch.cuda.Stream(device=dev)
+    h = stream.cuda_stream
+    cfg = CONFIG4
+    specs = [s for s in config4_specs(1, 0, dev) if "layers." in s[0] and not s[0].endswith("norm.weight")]
+    t0 = time.perf_counter()
+    payload, info, comp, raw = device_archive(specs, 1, dev, stream, 0.72)
+    build_s = time.perf_counter() - t0
+    by = {t["name"]: t for t in info}
+    plans, xs, ys, groups = [], 0, 0, []
+    for L in range(cfg["layers"]):
+        p = f"model.layers.{L}."
+        for members in ([p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight", p + "self_attn.v_proj.weight"],
+                        [p + "self_attn.o_proj.weight"],
+                        [p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"],
+                        [p + "mlp.down_proj.weight"]):
+            entries, y0 = [], ys
+            for m in members:
+                t = by[m]
+                for s in t["slabs"]:
+                    e = dict(s)
+                    e["dst_offset"] = ys + s["dst_offset"] // (2 * t["cols"])
+                    e["x_offset"] = xs
+                    entries.append(e)
+                ys += t["rows"]
+            groups.append((members, xs, y0, ys - y0, by[members[0]]["cols"]))
+            xs += by[members[0]]["cols"]
+            plans.append(xksv_gpu.Plan(entries))
+    t_idx = time.perf_counter()
+    for pl in plans:
+        if pl.index(payload.data_ptr(), h):
+            raise RuntimeError("xksv_plan_index failed")
+    index_s = time.perf_counter() - t_idx
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(5)
+    for batch in (1, 4):
+        x = torch.randn(xs, batch, generator=g, device=dev).to(torch.bfloat16).float()
+        y = torch.empty(ys, batch, device=dev)
+
+        def forward():
+            for pl in plans:
+                pl.gemm(payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch, h)
+        with torch.cuda.stream(stream):
+            forward()
+        assert all(pl.status(h) == 0 for pl in plans)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            forward()
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                graph.replay()
+            t = time_steps(graph.replay, max(3, args.gemv_steps // 4), stream)
+        ms = t / max(3, args.gemv_steps // 4) * 1e3
+        # layer 0 down_proj against an FP32 matmul of its decoded weights
+        members, x0, y0, nrows, cols = groups[3]
+        td = by[members[0]]
+        dplan = xksv_gpu.Plan(td["slabs"])
+        w = torch.empty(td["rows"] * td["cols"] * 2, dtype=torch.uint8, device=dev)
+        dplan.decode(payload.data_ptr(), w.data_ptr(), h)
+        assert dplan.status(h) == 0
+        dplan.close()
+        W = w.view(torch.bfloat16).view(td["rows"], td["cols"]).float()
+        ref = W @ x[x0:x0 + cols]
+        rel = float((y[y0:y0 + nrows] - ref).norm() / ref.norm())
+        res[f"batch{batch}"] = dict(ms_per_forward=round(ms, 3), tok_per_s=round(batch * 1e3 / ms, 2),
+                                    compressed_gbs=round(comp / (ms / 1e3) / 1e9, 1),
+                                    frac_of_hbm=round(comp / (ms / 1e3) / 1e9 / measured_peak()[0], 4),
+                                    rel_l2_layer0_down=rel)
+        del graph
+    # batch 8 and 16: layer 0 on the tensor cores
+    for batch in (8, 16):
+        x = torch.randn(xs, batch, generator=g, device=dev).to(torch.bfloat16).float()
+        y = torch.empty(ys, batch, device=dev)
+
+        def layer0():
+            for pl in plans[:4]:
+                pl.gemm(payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch, h)
+        with torch.cuda.stream(stream):
+            layer0()
+            for _ in range(2):
+                layer0()
+            t = time_steps(layer0, 10, stream)
+        assert all(pl.status(h) == 0 for pl in plans[:4])
+        ms = t / 10 * 1e3
+        members, x0, y0, nrows, cols = groups[3]
+        td = by[members[0]]
+        dplan = xksv_gpu.Plan(td["slabs"])
+        w = torch.empty(td["rows"] * td["cols"] * 2, dtype=torch.uint8, device=dev)
+        dplan.decode(payload.data_ptr(), w.data_ptr(), h)
+        assert dplan.status(h) == 0
+        dplan.close()
+        W = w.view(torch.bfloat16).view(td["rows"], td["cols"]).float()
+        ref = W @ x[x0:x0 + cols]
+        rel = float((y[y0:y0 + nrows] - ref).norm() / ref.norm())
+        weights0 = sum(n * c for _, _, _, n, c in groups[:4])
+        comp0 = sum(s["src_size"] for mm in groups[:4] for m in mm[0] for s in by[m]["slabs"])
+        res[f"batch{batch}_layer0"] = dict(ms_per_layer=round(ms, 3),
+                                           tflops=round(2 * weights0 * batch / (ms / 1e3) / 1e12, 2),
+                                           compressed_gbs=round(comp0 / (ms / 1e3) / 1e9, 1),
+                                           rel_l2_layer0_down=rel)
+    line = dict(case="config4-gemv", config="configs[3] Llama-3-70B linears (80 layers), N(0,0.015) seed 3, "
+                "dfloat11 + tile index, 1 GPU", compressed_bytes=comp, weights=raw // 2,
+                index_build_s=round(index_s, 2), build_s=round(build_s, 1), launches_per_forward=len(plans),
+                **res)
+    print(json.dumps(line), flush=True)
+    for pl in plans:
+        pl.close()
+
+
+def run_config5(args):
+    """`--case config5`: the adversarial exponent mix of BASELINE configs[4]:
+    64 tensors of 8192x8192 BF16 from seed 4 -- 32 Student-t(3) x 0.02, 16
+    N(0, 1e-4), 16 uniform 16-bit patterns (raw-fallback slabs) -- encoded on
+    the GPU in both codecs and decoded whole (one plan per codec), bit-exact
+    against the source; tensors split over the ranks (tensor i on rank
+    i % N)."""
+    import torch
+    import xksv_gpu
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device(dev))
+    xksv_gpu.load()
+    stream = torch.cuda.Stream(device=dev)
+    h = stream.cuda_stream
+    n = 8192
+    torch.manual_seed(4)
+    torch.cuda.manual_seed(4)
+    srcs, names = [], []
+    for i in range(64):
+        if i < 32:  # Student-t(3): z / sqrt(chi2_3 / 3), chi2_3 = 2 * Gamma(1.5)
+            z = torch.randn(n, n, device=dev)
+            chi2 = 2.0 * torch._standard_gamma(torch.full((n, n), 1.5, device=dev))
+            w = (z / torch.sqrt(chi2 / 3.0) * 0.02).to(torch.bfloat16)
+            kind = "student3"
+        elif i < 48:
+            w = (torch.randn(n, n, device=dev) * 1e-4).to(torch.bfloat16)
+            kind = "normal1e-4"
+        else:
+            w = torch.randint(-32768, 32768, (n, n), device=dev, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+            kind = "uniform16"
+        if i % world == rank:
+            srcs.append(w)
+            names.append(f"t{i}.{kind}")
+        else:
+            del w
+    raw_bytes = sum(s.numel() * 2 for s in srcs)
+    results = {}
+    for codec, cname in ((1, "bf16-huffman-tile16"), (2, "bf16-huffman-parallel32")):
+        specs = [(nm, n, n, (lambda s=s: s)) for nm, s in zip(names, srcs)]
+        payload, info, comp, raw = device_archive(specs, codec, dev, stream, 1.02)
+        entries, base = [], 0
+        for t in info:
+            for s in t["slabs"]:
+                e = dict(s)
+                e["dst_offset"] = base + s["dst_offset"]
+                entries.append(e)
+            base += t["rows"] * t["cols"] * 2
+        plan = xksv_gpu.Plan(entries)
+        out = torch.empty(base, dtype=torch.uint8, device=dev)
+        with torch.cuda.stream(stream):
+            plan.decode(payload.data_ptr(), out.data_ptr(), h)
+        if plan.status(h):
+            raise RuntimeError("decode reported a slab error")
+        exact = all(torch.equal(out[k * n * n * 2:(k + 1) * n * n * 2].view(torch.int16),
+                                s.view(torch.int16).reshape(-1)) for k, s in enumerate(srcs))
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                plan.decode(payload.data_ptr(), out.data_ptr(), h)
+            stream.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+            t = time_steps(lambda: plan.decode(payload.data_ptr(), out.data_ptr(), h), args.steps, stream)
+        t = _max_over_ranks(t, world, dev)
+        ms = t / args.steps * 1e3
+        kinds = {}
+        for e in entries:
+            kinds[e["codec"]] = kinds.get(e["codec"], 0) + 1
+        peak = measured_peak()[0]
+        results[cname] = dict(ms_per_step=round(ms, 3), value=round(world * raw / (ms / 1e3) / 1e9, 1),
+                              per_gpu_out_gbs=round(raw / (ms / 1e3) / 1e9, 1), compressed_bytes=comp,
+                              ratio=round(comp / raw, 4), slabs_by_codec=kinds,
+                              roofline_frac=round((raw + comp) / (ms / 1e3) / 1e9 / peak, 4),
+                              bit_exact=exact, status_errors=plan.status(h))
+        plan.close()
+        del payload, out
+        torch.cuda.empty_cache()
+    line = dict(case="config5", config="configs[4] 64 x 8192x8192 BF16, seed 4: 32 Student-t(3)*0.02, "
+                "16 N(0,1e-4), 16 uniform 16-bit", n_gpus=world, per_rank_out_bytes=raw_bytes,
+                unit="GB/s BF16 out (all ranks)", **results)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def run_runtime(args):
     """`--case runtime`: the archive path around the kernels on the config-2
     checkpoint.  Writes the seeded checkpoint as Safetensors to a temporary
@@ -657,8 +1055,10 @@ def main():
                          "gemv-serial:16x4096:1024 runs the indexed batch-1 GEMV instead")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    if args.case == "runtime":
-        run_runtime(args)
+    named = {"runtime": run_runtime, "config4-decode": run_config4_decode,
+             "config4-gemv": run_config4_gemv, "config5": run_config5}
+    if args.case in named:
+        named[args.case](args)
         return
     if args.case:
         run_case(args)
