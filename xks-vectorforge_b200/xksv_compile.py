@@ -236,7 +236,8 @@ class ArchiveWriter:
         self.encoder, self.device, self.threads = encoder, device, threads
         self.lib = xksv_gpu.load()
         self.pool = ThreadPoolExecutor(max_workers=max(2, min(32, os.cpu_count() or 2)))
-        self._pending, self._max_pending = [], 2 * self.pool._max_workers
+        # tensors whose digest is still running keep their bytes alive: bound them
+        self._pending, self._pending_bytes, self._max_pending_bytes = [], 0, 4 << 30
         fd = os.open(self.partial, os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
         self.f = os.fdopen(fd, "w+b")
         self.f.write(HEADER.pack(MAGIC, 0))
@@ -326,15 +327,17 @@ class ArchiveWriter:
             self.f.write(memoryview(data))
         # the tensor digest is one sequential pass: collect it later, keeping
         # a bounded number of tensors in flight
-        self._pending.append((t, tensor_digest))
-        while len(self._pending) > self._max_pending:
+        self._pending.append((t, tensor_digest, raw.size))
+        self._pending_bytes += raw.size
+        while len(self._pending) > 1 and self._pending_bytes > self._max_pending_bytes:
             self._settle_one()
         self.index["shards"][shard]["tensors"].append(t)
         return t
 
     def _settle_one(self):
-        t, fut = self._pending.pop(0)
+        t, fut, n = self._pending.pop(0)
         t["sha256"] = fut.result()
+        self._pending_bytes -= n
 
     def close(self):
         """Writes the index and the header and moves the file into place."""
