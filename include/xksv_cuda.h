@@ -110,6 +110,18 @@ int xksv_plan_decode_host(const xksv_plan* plan, const void* h_payload, size_t p
 int xksv_plan_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y,
                    size_t batch, void* stream);
 
+/* The tensor-core path (batch > 4) decodes the plan's weights into a BF16
+ * scratch before its GEMM; by default each plan allocates its own on first
+ * use and keeps it, i.e. a decoded copy of its weights.  Plans whose calls
+ * are serialised on one stream can share one caller-owned scratch instead:
+ * xksv_plan_scratch_bytes gives the bytes a plan needs (0 when it has no
+ * tensor-core path) and xksv_plan_set_scratch lends it a device buffer of at
+ * least that size, 256-byte aligned (the plan's own scratch, if any, is
+ * freed; NULL returns to an own scratch).  Returns 1 for a buffer too small
+ * or misaligned.  The caller keeps the buffer alive while the plan uses it. */
+size_t xksv_plan_scratch_bytes(const xksv_plan* plan);
+int xksv_plan_set_scratch(xksv_plan* plan, void* d_scratch, size_t bytes);
+
 /* Synchronises `stream`, returns 0 when no slab reported an error since the
  * last call (then clears the word), else 1. */
 int xksv_plan_status(const xksv_plan* plan, void* stream);

@@ -103,6 +103,26 @@ def test_fused_weight_mixed_codecs(tag, batch):
     fw.close()
 
 
+def test_fused_weights_share_one_scratch():
+    """Batch > 4 on two fused weights of one archive: both borrow the
+    archive's single tensor-core scratch and stay correct."""
+    a = rt.ResidentArchive(path_of("llama", "tile16"), "cuda:0")
+    a.verify()
+    names = ["model.layers.0.mlp.gate_proj.weight", "model.layers.0.mlp.down_proj.weight"]
+    fws = [a.fused(n) for n in names]
+    g = torch.Generator(device="cuda:0").manual_seed(9)
+    for _ in range(2):
+        for n, fw in zip(names, fws):
+            W = a.tensor(n).float()
+            x = torch.randn(12, W.shape[1], device="cuda:0", generator=g)
+            y = fw(x)
+            ref = x.bfloat16().float() @ W.t()
+            assert float((y - ref).norm() / ref.norm()) < 1e-2
+    assert all(fw._lent is a.shared_scratch() for fw in fws if fw._scratch_need)
+    for fw in fws:
+        fw.close()
+
+
 def test_fused_llama_matches_decoded_model():
     """load_archive builds the model from the archive's config asset, decodes
     every weight in one plan; the fused model's logits match the decoded one

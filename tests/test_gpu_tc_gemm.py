@@ -106,3 +106,34 @@ def test_tc_gemm_reports_corrupt_slab(xg):
     plan.gemm(d_bad.data_ptr(), x.data_ptr(), y.data_ptr(), 16)
     assert plan.status() == 1
     plan.close()
+
+
+@pytest.mark.parametrize("batch", [8, 16])
+def test_tc_gemm_shared_scratch_and_x_base(xg, batch):
+    """Two plans over disjoint parts of one X (the second's lowest x_offset is
+    not 0, so its X^T covers only its own columns) share one caller-owned
+    scratch; results match an FP32 matmul.  A too-small scratch is refused."""
+    oracle = Oracle()
+    rng = np.random.default_rng(40 + batch)
+    mats = [(64, 512), (48, 1024), (32, 2048)]
+    payload, entries, ws, xn, yn = archive(oracle, mats, rng, codecs=(1, 2, 0))
+    d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
+    x = torch.randn(xn, batch, device="cuda")
+    first = [e for e in entries if e["x_offset"] == 0]
+    rest = [e for e in entries if e["x_offset"] > 0]
+    p1, p2 = xg.Plan(first), xg.Plan(rest)
+    need = max(p1.scratch_bytes(), p2.scratch_bytes())
+    assert need > 0
+    with pytest.raises(ValueError):
+        p2.set_scratch(torch.empty(16, dtype=torch.uint8, device="cuda").data_ptr(), 16)
+    scratch = torch.empty(need, dtype=torch.uint8, device="cuda")
+    for p in (p1, p2):
+        p.set_scratch(scratch.data_ptr(), need)
+    for _ in range(2):
+        y = torch.full((yn, batch), float("nan"), device="cuda")
+        p1.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+        p2.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+        assert p1.status() == 0 and p2.status() == 0
+        check(ws, x, y)
+    p1.close()
+    p2.close()

@@ -198,9 +198,10 @@ struct xksv_plan {
   uint32_t ngroups = 0, tc_ksplit = 1;
   xksv::TcGroup* d_groups = nullptr;
   xksv::Slab* d_tc_slabs = nullptr;  // d_slabs with dst = scratch byte offsets
-  uint64_t scratch_bytes = 0, x_cols = 0;
+  uint64_t scratch_bytes = 0, x_cols = 0, x_base = 0;  // X rows [x_base, x_base + x_cols)
   uint8_t* d_scratch = nullptr;
-  void* d_xt = nullptr;  // BF16 X^T [256][x_cols]
+  bool scratch_owned = true;  // false: lent by the caller (xksv_plan_set_scratch)
+  void* d_xt = nullptr;  // BF16 X^T [256][x_cols] of X rows from x_base
   uint64_t* d_hash_ranges = nullptr;  // per slab in creation order: {dst, decoded bytes}
   // xksv_plan_decode_host: copy stream and per-chunk events (created on first use)
   cudaStream_t copy_st = nullptr;
@@ -229,10 +230,13 @@ bool tile_indexable(const xksv::Slab& s) {
 
 // Row groups for the tensor-core GEMM: slabs sharing X columns (x_offset,
 // cols) whose output rows are contiguous, up to 128 rows per group; fills
-// the scratch slab table (same order as `all`).  False when a slab is not
-// 16-byte aligned for cp.async (cols or x_offset not a multiple of 8).
+// the scratch slab table (same order as `all`).  The X columns the plan reads
+// are [x_base, x_base + x_cols); groups hold offsets relative to x_base.
+// False when a slab is not 16-byte aligned for cp.async (cols or x_offset not
+// a multiple of 8).
 bool build_tc_groups(const std::vector<xksv::Slab>& all, std::vector<xksv::TcGroup>& groups,
-                     std::vector<xksv::Slab>& tc_slabs, uint64_t& scratch, uint64_t& x_cols) {
+                     std::vector<xksv::Slab>& tc_slabs, uint64_t& scratch, uint64_t& x_cols,
+                     uint64_t& x_base) {
   using xksv::Slab;
   const size_t n = all.size();
   if (!n) return false;
@@ -248,17 +252,19 @@ bool build_tc_groups(const std::vector<xksv::Slab>& all, std::vector<xksv::TcGro
   });
   tc_slabs = all;
   scratch = 0;
+  x_base = ~uint64_t(0);
+  for (const Slab& s : all) x_base = std::min(x_base, s.xoff);
   x_cols = 0;
   xksv::TcGroup cur{};
   bool open = false;
   for (size_t k = 0; k < n; ++k) {
     const Slab& s = all[idx[k]];
-    x_cols = std::max<uint64_t>(x_cols, s.xoff + s.cols);
-    const bool extend = open && s.xoff == cur.xoff && s.cols == cur.cols &&
+    x_cols = std::max<uint64_t>(x_cols, s.xoff + s.cols - x_base);
+    const bool extend = open && s.xoff - x_base == cur.xoff && s.cols == cur.cols &&
                         s.dst == cur.y_row0 + cur.rows && cur.rows + s.rows <= 128;
     if (!extend) {
       if (open) groups.push_back(cur);
-      cur = xksv::TcGroup{scratch, s.dst, s.xoff, 0, uint32_t(s.cols)};
+      cur = xksv::TcGroup{scratch, s.dst, s.xoff - x_base, 0, uint32_t(s.cols)};
       open = true;
     }
     tc_slabs[idx[k]].dst = cur.a_off + uint64_t(cur.rows) * s.cols * 2;
@@ -406,7 +412,7 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   {
     std::vector<TcGroup> groups;
     std::vector<Slab> tc_slabs;
-    if (ok && raw_gemm_ok && build_tc_groups(all, groups, tc_slabs, p->scratch_bytes, p->x_cols)) {
+    if (ok && raw_gemm_ok && build_tc_groups(all, groups, tc_slabs, p->scratch_bytes, p->x_cols, p->x_base)) {
       p->ngroups = uint32_t(groups.size());
       uint32_t minch = ~0u;
       for (const TcGroup& g : groups) minch = std::min<uint32_t>(minch, (g.cols + 63) / 64);
@@ -437,7 +443,7 @@ void xksv_plan_destroy(xksv_plan* p) {
   free_index(p);
   if (p->d_groups) cudaFree(p->d_groups);
   if (p->d_tc_slabs) cudaFree(p->d_tc_slabs);
-  if (p->d_scratch) cudaFree(p->d_scratch);
+  if (p->d_scratch && p->scratch_owned) cudaFree(p->d_scratch);
   if (p->d_xt) cudaFree(p->d_xt);
   if (p->d_hash_ranges) cudaFree(p->d_hash_ranges);
   if (p->d_slabs) cudaFree(p->d_slabs);
@@ -642,7 +648,7 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
       g.tmem_cols = 32;
       while (g.tmem_cols < g.npad) g.tmem_cols *= 2;
       g.status = p->d_status;
-      e = launch_tc_gemm(g, p->ngroups, d_x + b0, p->x_cols, st);
+      e = launch_tc_gemm(g, p->ngroups, d_x + p->x_base * ld + b0, p->x_cols, st);
       p->launches += g.ksplit > 1 ? 3 : 2;
     }
     return e == cudaSuccess ? 0 : 1;
@@ -688,6 +694,20 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
     }
   }
   return e == cudaSuccess ? 0 : 1;
+}
+
+size_t xksv_plan_scratch_bytes(const xksv_plan* p) {
+  return p && p->tc_ok ? size_t(std::max<uint64_t>(16, p->scratch_bytes)) : 0;
+}
+
+int xksv_plan_set_scratch(xksv_plan* p, void* d_scratch, size_t bytes) {
+  if (!p) return 1;
+  if (!p->tc_ok) return 0;  // no tensor-core path: nothing uses a scratch
+  if (d_scratch && (bytes < xksv_plan_scratch_bytes(p) || misaligned(d_scratch, 256))) return 1;
+  if (p->d_scratch && p->scratch_owned) cudaFree(p->d_scratch);
+  p->d_scratch = static_cast<uint8_t*>(d_scratch);  // null: allocate an own one on next use
+  p->scratch_owned = d_scratch == nullptr;
+  return 0;
 }
 
 int xksv_plan_status(const xksv_plan* pc, void* stream) {

@@ -45,6 +45,8 @@ _SIGS = {
     "xksv_plan_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                         ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_scratch_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
+    "xksv_plan_set_scratch": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_cuda_sha256": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_void_p,
@@ -232,6 +234,15 @@ class Plan:
         """Enqueues the SHA-256 of every slab's decoded bytes (xksv_plan_sha256)."""
         if self.lib.xksv_plan_sha256(self.handle, d_out, d_digests, stream):
             raise RuntimeError("xksv_plan_sha256 failed")
+
+    def scratch_bytes(self):
+        """Bytes of BF16 scratch the tensor-core path needs (0: none)."""
+        return self.lib.xksv_plan_scratch_bytes(self.handle)
+
+    def set_scratch(self, d_scratch, nbytes):
+        """Lends the plan a caller-owned scratch (xksv_plan_set_scratch)."""
+        if self.lib.xksv_plan_set_scratch(self.handle, d_scratch, nbytes):
+            raise ValueError("scratch too small or misaligned")
 
     def status(self, stream=0):
         """0 when no slab reported an error since the last call, else 1."""

@@ -252,6 +252,9 @@ class ResidentArchive:
         self._check_parallel_headers()
         self.verified = False
         self._plans = {}
+        # one BF16 scratch shared by the fused weights' tensor-core path
+        # (their calls are serialised on the caller's stream)
+        self._tc_scratch, self._tc_need = None, 0
 
     def _upload(self, chunk, readers):
         """Reads the block region into HBM: `readers` threads each pread
@@ -473,11 +476,21 @@ class ResidentArchive:
             fail(f"tensor {name} is not a fusable BF16 matrix")
         return FusedWeight(self, t)
 
+    def shared_scratch(self):
+        """The tensor-core scratch shared by this archive's fused weights,
+        (re)allocated to the largest need registered so far."""
+        import torch
+        if self._tc_scratch is None or self._tc_scratch.numel() < self._tc_need:
+            self._tc_scratch = torch.empty(self._tc_need, dtype=torch.uint8, device=self.device)
+        return self._tc_scratch
+
     def close(self):
-        """Releases the resident payload and the cached decode plans."""
+        """Releases the resident payload, the cached decode plans and the
+        shared scratch."""
         for plan in self._plans.values():
             plan.close()
         self._plans.clear()
+        self._tc_scratch = None
         self.payload = None
 
 
@@ -498,6 +511,12 @@ class FusedWeight:
         with torch.cuda.device(archive.device):
             if self.plan.index(archive.payload_ptr, archive._stream()):
                 fail(f"fused GEMV failed: {self.name}")
+        # batch > 4 decodes the weight into a BF16 scratch for the tensor
+        # cores: borrow the archive's shared one instead of keeping a
+        # decoded copy per weight
+        self._scratch_need = self.plan.scratch_bytes()
+        archive._tc_need = max(archive._tc_need, self._scratch_need)
+        self._lent = None
 
     def __call__(self, x):
         import torch
@@ -509,6 +528,11 @@ class FusedWeight:
         if batch == 0:
             return x.new_empty(*lead, self.rows)
         stream = torch.cuda.current_stream(x.device).cuda_stream
+        if batch > 4 and self._scratch_need:
+            buf = self.archive.shared_scratch()
+            if self._lent is not buf:  # keeps the lent buffer alive while the plan points at it
+                self.plan.set_scratch(buf.data_ptr(), buf.numel())
+                self._lent = buf
         if batch == 1:  # x [cols] and y [rows]: the ABI's [cols, 1] and [rows, 1]
             xt = xb.reshape(self.cols).float().contiguous()
             y = torch.empty(self.rows, device=x.device, dtype=torch.float32)
