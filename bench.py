@@ -652,7 +652,7 @@ def run_config4_gemv(args):
         if pl.index(payload.data_ptr(), h):
             raise RuntimeError("xksv_plan_index failed")
     index_s = time.perf_counter() - t_idx
-    # batch > 4 runs on the tensor cores after decoding each plan's weights
+    # batch >= 4 runs on the tensor cores after decoding each plan's weights
     # into a BF16 scratch: one scratch, sized for the largest plan, is lent to
     # every plan (their calls are serialised on one stream)
     need = max(pl.scratch_bytes() for pl in plans)
@@ -692,10 +692,10 @@ def run_config4_gemv(args):
         assert dplan.status(h) == 0
         dplan.close()
         W = w.view(torch.bfloat16).view(td["rows"], td["cols"]).float()
-        ref = W @ (x[x0:x0 + cols] if batch <= 4 else x[x0:x0 + cols].bfloat16().float())
+        ref = W @ (x[x0:x0 + cols] if batch < 4 else x[x0:x0 + cols].bfloat16().float())
         rel = float((y[y0:y0 + nrows] - ref).norm() / ref.norm())
         res[f"batch{batch}"] = dict(ms_per_forward=round(ms, 3), tok_per_s=round(batch * 1e3 / ms, 2),
-                                    path="CUDA cores, FP32 x" if batch <= 4 else "tcgen05, x in BF16",
+                                    path="CUDA cores, FP32 x" if batch < 4 else "tcgen05, x in BF16",
                                     compressed_gbs=round(comp / (ms / 1e3) / 1e9, 1),
                                     frac_of_hbm=round(comp / (ms / 1e3) / 1e9 / peak, 4),
                                     tflops=round(2 * (raw // 2) * batch / (ms / 1e3) / 1e12, 2),

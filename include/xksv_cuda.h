@@ -110,7 +110,7 @@ int xksv_plan_decode_host(const xksv_plan* plan, const void* h_payload, size_t p
 int xksv_plan_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y,
                    size_t batch, void* stream);
 
-/* The tensor-core path (batch > 4) decodes the plan's weights into a BF16
+/* The tensor-core path (batch >= 4) decodes the plan's weights into a BF16
  * scratch before its GEMM; by default each plan allocates its own on first
  * use and keeps it, i.e. a decoded copy of its weights.  Plans whose calls
  * are serialised on one stream can share one caller-owned scratch instead:

@@ -10,6 +10,9 @@ import numpy as np
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden" / "golden.npz"
 FORMULA_PREFIXES = ("iota_", "all_patterns_")
+# xksv_plan_gemm runs batches from this size on the tensor cores (X rounded
+# to BF16) when the plan allows it (xksv_plan_scratch_bytes > 0)
+TC_MIN_BATCH = 4
 
 
 def bf16_bits(x):

@@ -9,7 +9,7 @@ import hashlib
 import numpy as np
 import pytest
 
-from helpers import bf16_bits, bf16_to_f32, rel_l2, words_for
+from helpers import TC_MIN_BATCH, bf16_bits, bf16_to_f32, rel_l2, words_for
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -68,7 +68,7 @@ def test_config4_slabs(xg, codec):
         y = torch.full((nrows, batch), float("nan"), device="cuda")
         gp.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
         assert gp.status() == 0
-        xr = x.to(torch.bfloat16).float() if batch > 4 else x
+        xr = x.to(torch.bfloat16).float() if batch >= TC_MIN_BATCH and gp.scratch_bytes() else x
         ro = co = 0
         for w in W:
             ref = w @ xr[co:co + w.shape[1]]

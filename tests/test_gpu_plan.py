@@ -7,7 +7,7 @@ import hashlib
 import numpy as np
 import pytest
 
-from helpers import bf16_to_f32, rel_l2, words_for
+from helpers import TC_MIN_BATCH, bf16_to_f32, rel_l2, words_for
 from oracle.oracle import Oracle
 
 pytestmark = pytest.mark.gpu
@@ -112,8 +112,8 @@ def test_plan_gemm_multi_tensor(xg, batch):
     plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
     assert plan.status() == 0
     xo = yo = 0
-    # batch > 4 runs on the tensor cores with X rounded to BF16
-    xr = x.to(torch.bfloat16).float() if batch > 4 else x
+    # from TC_MIN_BATCH the plan runs on the tensor cores with X rounded to BF16
+    xr = x.to(torch.bfloat16).float() if batch >= TC_MIN_BATCH and plan.scratch_bytes() else x
     for (R, C), w in zip(mats, ws):
         ref = torch.from_numpy(bf16_to_f32(w)).cuda() @ xr[xo:xo + C]
         got = y[yo:yo + R]

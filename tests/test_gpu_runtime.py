@@ -95,16 +95,16 @@ def test_fused_weight_mixed_codecs(tag, batch):
     x = torch.randn(batch, 1536, device="cuda:0", generator=g)
     y = fw(x if batch > 1 else x[0])
     ref = x @ W.t() if batch > 1 else W @ x[0]
-    if batch > 4:  # tensor-core path: x rounded to BF16
+    if batch >= 4:  # tensor-core path: x rounded to BF16
         ref = x.bfloat16().float() @ W.t()
     err = float((y.float() - ref).norm() / ref.norm())
-    assert err < (1e-5 if batch <= 4 else 1e-2), err
+    assert err < (1e-5 if batch < 4 else 1e-2), err
     assert y.shape == ref.shape
     fw.close()
 
 
 def test_fused_weights_share_one_scratch():
-    """Batch > 4 on two fused weights of one archive: both borrow the
+    """Batch >= 4 (tensor cores) on two fused weights of one archive: both borrow the
     archive's single tensor-core scratch and stay correct."""
     a = rt.ResidentArchive(path_of("llama", "tile16"), "cuda:0")
     a.verify()

@@ -7,7 +7,7 @@ through their own kernels in the same call."""
 import numpy as np
 import pytest
 
-from helpers import bf16_to_f32, rel_l2, words_for
+from helpers import TC_MIN_BATCH, bf16_to_f32, rel_l2, words_for
 from oracle.oracle import Oracle
 
 pytestmark = pytest.mark.gpu
@@ -45,11 +45,11 @@ def weights_archive(oracle, mats, kind, rng, codec_for=lambda mi, r0: 1, lead=3)
     return bytes(payload), entries, ws, xoff, yrow
 
 
-def check(ws, mats, x, y, tol):
-    """Against FP32 X up to batch 4 (CUDA-core kernels); beyond, the plan runs
-    on the tensor cores with X rounded to BF16."""
+def check(ws, mats, x, y, tol, plan=None):
+    """Against FP32 X below TC_MIN_BATCH (CUDA-core kernels); from there a
+    plan with a tensor-core path runs it with X rounded to BF16."""
     xo = yo = 0
-    if x.shape[1] > 4:
+    if plan is not None and x.shape[1] >= TC_MIN_BATCH and plan.scratch_bytes():
         x = x.to(torch.bfloat16).float()
     for (R, C), w in zip(mats, ws):
         ref = torch.from_numpy(bf16_to_f32(w)).cuda() @ x[xo:xo + C]
@@ -74,8 +74,8 @@ def test_indexed_gemm_matches_fp32(xg, kind, batch):
         y = torch.full((yn, batch), float("nan"), device="cuda")
         plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
         assert plan.status() == 0
-        check(ws, mats, x, y, 1e-5)
-    if batch <= 4:
+        check(ws, mats, x, y, 1e-5, plan)
+    if batch < TC_MIN_BATCH:
         assert plan.launches() == 1
     plan.close()
 

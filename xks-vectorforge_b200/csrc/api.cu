@@ -603,12 +603,13 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x,
   p->launches = 0;
   cudaError_t e = cudaSuccess;
   const uint32_t ld = uint32_t(batch);
-  // routing (measured on B200, 1024 slabs of 16x4096): up to batch 4 the
-  // CUDA-core kernels with FP32 X (the indexed tile kernel: 116-220 us);
-  // beyond, decode + tensor-core GEMM with X rounded to BF16 (~310 us for
-  // any batch <= 256, against 400-660 us for batch 6-12 on CUDA cores)
+  // routing (measured on B200 with the tile index): up to batch 3 the
+  // CUDA-core kernels with FP32 X (1024 slabs of 16x4096: 116 us at batch 1,
+  // 182 / 190 us at 2 / 3); from batch 4, decode + tensor-core GEMM with X
+  // rounded to BF16 (200 us for any batch <= 256, against 230 us for batch 4
+  // on the CUDA cores; the 70B linears: 164 ms against 226 ms at batch 4)
   const bool indexed = p->d_tidx && d_payload == p->indexed_payload;
-  if (p->tc_ok && batch > 4) {
+  if (p->tc_ok && batch >= 4) {
     // decode every slab into its BF16 row group, then the tensor-core GEMM,
     // up to 256 batch columns per pass over the same decoded scratch
     if (!p->d_scratch && cudaMalloc(&p->d_scratch, std::max<uint64_t>(16, p->scratch_bytes)) != cudaSuccess)

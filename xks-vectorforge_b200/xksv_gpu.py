@@ -85,6 +85,9 @@ _SIGS = {
 }
 
 NOALLOC_MAX_SLABS = 4096
+# xksv_plan_gemm: batches from this size run on the tensor cores (X rounded
+# to BF16) when the plan has a tensor-core path (xksv_plan_scratch_bytes > 0)
+TC_MIN_BATCH = 4
 
 EXPORTS = tuple(_SIGS)
 _lib = None

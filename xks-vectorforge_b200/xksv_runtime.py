@@ -511,7 +511,7 @@ class FusedWeight:
         with torch.cuda.device(archive.device):
             if self.plan.index(archive.payload_ptr, archive._stream()):
                 fail(f"fused GEMV failed: {self.name}")
-        # batch > 4 decodes the weight into a BF16 scratch for the tensor
+        # batch >= TC_MIN_BATCH decodes the weight into a BF16 scratch for the tensor
         # cores: borrow the archive's shared one instead of keeping a
         # decoded copy per weight
         self._scratch_need = self.plan.scratch_bytes()
@@ -528,7 +528,7 @@ class FusedWeight:
         if batch == 0:
             return x.new_empty(*lead, self.rows)
         stream = torch.cuda.current_stream(x.device).cuda_stream
-        if batch > 4 and self._scratch_need:
+        if batch >= xksv_gpu.TC_MIN_BATCH and self._scratch_need:
             buf = self.archive.shared_scratch()
             if self._lent is not buf:  # keeps the lent buffer alive while the plan points at it
                 self.plan.set_scratch(buf.data_ptr(), buf.numel())
