@@ -344,6 +344,11 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
       if (t == 0) atomicOr(a.status, kStatusInternal);
       continue;
     }
+    // warm L2 with the whole slab (at most 1 MiB, 32 lines per thread) while
+    // its tables are built: each round's bit staging and the exact pass's
+    // sign/mantissa loads then hit L2 instead of waiting on DRAM
+    for (uint64_t off = uint64_t(t) * 128; off < size; off += uint64_t(ST) * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
     if (!build_tables<7, true>(S, p + 16)) {
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       __syncthreads();
