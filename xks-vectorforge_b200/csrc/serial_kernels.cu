@@ -733,6 +733,23 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const uint8_t* p = a.payload + sd.src;
     const uint32_t count = uint32_t(sd.rows * sd.cols);
     const uint32_t nbits = uint32_t(ld_le64(p + 8));
+    // warm L2 with the item's sign/mantissa tiles and bit range (the tile
+    // index bounds it; clamped to the slab) while the tables are built.
+    // Measured on the Llama-3-8B forward of linears: +3 % tokens/s, the gain
+    // coming from its launches of under one wave; a full 1024-slab launch
+    // loses ~3 % to the extra L2 requests.
+    {
+      const uint8_t* smp = p + kHdr + uint64_t(it.tile0) * 256;
+      const uint64_t smn = uint64_t(it.ntiles) * 256;
+      for (uint64_t off = uint64_t(t) * 128; off < smn; off += uint64_t(GT) * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(smp + off));
+      const uint32_t* tix = a.tidx + a.tbase[it.slab];
+      const uint64_t nbb = sd.size - kHdr - count;
+      const uint64_t pb0 = tix[it.tile0] >> 3, pb1 = min(uint64_t(tix[it.tile0 + it.ntiles] + 7) >> 3, nbb);
+      const uint8_t* bp = p + kHdr + count;
+      for (uint64_t off = pb0 + uint64_t(t) * 128; off < pb1; off += uint64_t(GT) * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(bp + off));
+    }
     if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       __syncthreads();
