@@ -529,17 +529,17 @@ def run_config4_decode(args):
     specs = config4_specs(world, rank, dev)
     payload, info, comp, raw = device_archive(specs, 2, dev, stream, 0.78)
     build_s = time.perf_counter() - t0
-    # one plan per 4 layers (embed and lm_head with the first and last): a
-    # launch of ~10 waves keeps each plan's tail short; within a plan the
-    # longest slabs start first
-    groups, cur, nl = [], [], 0
+    # plans of whole layers holding ~6 GB of output each (4 layers on one GPU,
+    # more when the rows are sharded; embed and lm_head join the first and
+    # last): a launch of many waves keeps each plan's tail short; within a
+    # plan the longest slabs start first
+    groups, cur, cur_bytes = [], [], 0
     for t in info:
         cur.append(t)
-        if t["name"].endswith("post_attention_layernorm.weight"):
-            nl += 1
-            if nl % 4 == 0:
-                groups.append(cur)
-                cur = []
+        cur_bytes += t["rows"] * t["cols"] * 2
+        if t["name"].endswith("post_attention_layernorm.weight") and cur_bytes >= (6 << 30):
+            groups.append(cur)
+            cur, cur_bytes = [], 0
     if cur:
         groups.append(cur)
     plans, spans, max_out = [], [], 0
@@ -600,7 +600,7 @@ def run_config4_decode(args):
                               frac=round((raw + comp) / (ms / 1e3) / 1e9 / peak, 4), peak_source=peak_src),
                 launches_per_step=sum(pl.launches() for pl in plans), plans=len(plans),
                 bit_exact_tensors=len(check), status_errors=bad, build_s=round(build_s, 1),
-                note="output buffer reused per 4-layer plan; inputs larger than L2")
+                note="output buffer reused per plan of ~6 GB output; inputs larger than L2")
     if rank == 0:
         print(json.dumps(line), flush=True)
     for pl in plans:
