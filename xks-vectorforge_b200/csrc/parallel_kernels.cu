@@ -6,18 +6,27 @@
 //
 // B200 design: one warp per slab, one lane per substream (the format's up to
 // 32 independently coded substreams are a warp's worth of independent work);
-// many slabs in flight per SM.  Every per-lane event in the inner loop runs at
+// many slabs in flight per SM.  Every per-lane step of the inner loop runs at
 // a cadence shared by all lanes, so the warp never serialises on one lane:
-//   * each lane builds its own canonical tables: a 2^PK-entry first level for
-//     codes of length <= PK, a second level for lengths PK+1..PK+K2 under the
-//     first NE escape prefixes, and a compact list for lengths up to PK+PNL.
-//     Tables are lane-minor ([entry][lane]) so lookups never share a bank
-//     beyond lane pairs;
-//   * a lane's exponent bits are staged in a 4-slot shared ring by 16-byte
-//     cp.async copies issued once per 16 codes, and read through a 64-bit
-//     register window refilled from the ring once per 4 codes without a
-//     data-dependent branch;
-//   * sign/mantissa bytes arrive 16 at a time through a 3-deep register ring;
+//   * each lane builds its own canonical tables: a 2^PK-entry first level of
+//     32-bit entries for codes of length <= PK, a 16-bit second level for
+//     lengths PK+1..PK+K2 under the first NE escape prefixes, and a compact
+//     list for lengths up to PK+PNL.  Tables are lane-minor ([entry][lane]):
+//     a first-level lookup touches only the lane's own bank;
+//   * a lane's exponent bits live in a 16-word ring in shared memory laid out
+//     [word][lane], so every lane reads only its own bank.  Words arrive as
+//     aligned 32-byte global loads (sm_100 256-bit loads: a warp-wide load of
+//     32 separate streams costs one L1 wavefront per lane, so wider loads move
+//     more bytes per wavefront) held ahead in registers and are byte-swapped
+//     once when they enter the ring;
+//   * codes are decoded four at a time from one 32-bit snapshot of the ring
+//     at the lane's bit position (two shared loads and a funnel shift): four
+//     table lookups each followed by a one-instruction shift.  One check per
+//     block -- total length <= 32 and a non-zero last entry -- proves that
+//     every code of the block was read from real bits and found in the
+//     tables (an entry of 0 consumes no bits, so an unresolved code zeroes
+//     the block's last entry); otherwise the block is redone code by code;
+//   * sign/mantissa bytes arrive 16 at a time through a shared cp.async ring;
 //   * 16 decoded BF16 words (one tile row) leave as one 32-byte store (two
 //     16-byte stores when the output is only 16-byte aligned), un-tiled on the
 //     fly, for 16-row slabs with cols % 16 == 0; other shapes use an
@@ -25,34 +34,48 @@
 // A substream whose codebook the compact tables cannot hold (a length above
 // PK+PNL or more than PLONG long codes, e.g. near-uniform exponents) is decoded
 // afterwards by lane 0 with the bit-serial canonical decoder.
+// A slab's setup is a chain of dependent loads (container header, substream
+// table, substream headers, length tables); while one slab's tables are built
+// the warp already reads its next slab's substream table and prefetches that
+// slab's substream headers and length tables into L2.
+#include <atomic>
+
 #include "kernels.h"
 #include "xksv_device.cuh"
 
 namespace xksv {
 namespace {
 
-constexpr int PK = 7;      // first-level table bits
-constexpr int K2 = 5;      // second level covers lengths PK+1 .. PK+K2
-constexpr int NE = 2;      // escape prefixes with a second-level table
-constexpr int PNL = 16;    // long lengths held per lane: PK+1 .. PK+PNL
-constexpr int PLONG = 32;  // long symbols held per lane
-constexpr int RING = 4;    // 16-byte bit-stream slots per lane
-constexpr int SMR = 4;     // 16-byte sign/mantissa slots per lane
-constexpr int PWARPS = 2;  // slabs (warps) per CTA: small CTAs free their tables sooner
-constexpr int PMAXB = 8;   // GEMM columns per pass
+constexpr int PK = 6;       // first-level table bits
+constexpr int K2 = 4;       // second level covers lengths PK+1 .. PK+K2
+constexpr int NE = 2;       // escape prefixes with a second-level table
+constexpr int NROW2 = (NE << K2) + 1;  // second-level rows (the last is all zero)
+constexpr int PNL = 16;     // long lengths held per lane: PK+1 .. PK+PNL
+constexpr int PLONG = 32;   // long symbols held per lane
+constexpr int BR = 16;      // bit-ring words per lane (power of two)
+constexpr uint32_t kRingLow = 8;  // unread ring words kept at each 16-code group
+constexpr int kSaveChunk = 4;     // first ring row holding length chunks saved by the table build
+constexpr int SMR = 4;      // 16-byte sign/mantissa slots per lane
+constexpr int PWARPS = 2;   // slabs (warps) per CTA: small CTAs free their tables sooner
+constexpr int PMAXB = 8;    // GEMM columns per pass
 
-// One warp's tables, lane-minor so that lane l always touches bank l/2.
+// One warp's tables, lane-minor so that lane l always touches bank l (32-bit
+// first level, bit ring) or bank l/2 (16-bit second level, mostly its shared
+// all-zero row).
 struct WarpTabs {
-  uint16_t lut[1 << PK][32];      // exponent << 7 | length; 0 = no code of length <= PK
-  uint16_t lut2[(NE << K2) + 1][32];  // second level: 12-bit prefix - (L << K2); last row 0
-  uint16_t cnt[PNL][32];          // number of codes of length PK+1+j
-  uint8_t lsym[PLONG][32];        // long-code symbols, canonical (length, symbol) order
+  uint32_t lut[1 << PK][32];     // exponent << 7 | length; 0 = no code of length <= PK
+  uint16_t lut2[NROW2][32];      // second level: (PK+K2)-bit prefix - (L << K2); last row 0
+  uint8_t cnt[PNL][32];          // number of codes of length PK+1+j (<= PLONG)
+  uint8_t lsym[PLONG][32];       // long-code symbols, canonical (length, symbol) order
   union {
-    uint8_t lpos[PNL][32];        // fill cursor per long length (table build only)
-    uint4 ring[RING][32];         // staged exponent-bit chunks (little-endian bytes)
+    uint8_t lpos[PNL][32];       // fill cursor per long length (table build only)
+    uint32_t ring[BR][32];       // exponent bits, big-endian words, word w at [w % BR]
   };
-  uint4 smring[SMR][32];          // staged sign/mantissa chunks
+  uint4 smring[SMR][32];         // staged sign/mantissa chunks
 };
+static_assert(sizeof(WarpTabs) % 16 == 0, "warp tables keep 16-byte alignment");
+static_assert(kRingLow + 8 <= BR, "a staged chunk fits whenever maintain() adds one");
+static_assert(kSaveChunk * 128 >= PNL * 32, "saved length chunks do not overlap lpos");
 // decode: the warps' tables; GEMM adds [16][PMAXB] row accumulators per warp
 constexpr size_t kSmemTabs = PWARPS * sizeof(WarpTabs);
 constexpr size_t kSmemBytes[2] = {kSmemTabs, kSmemTabs + PWARPS * 16 * PMAXB * sizeof(float)};
@@ -76,64 +99,81 @@ struct Seg {
   uint64_t ebytes;
 };
 
-__device__ __forceinline__ uint32_t byte_of(const uint4& v, int b) {
-  const uint32_t w = b < 4 ? v.x : b < 8 ? v.y : b < 12 ? v.z : v.w;
-  return (w >> (8 * (b & 3))) & 255u;
-}
-
 // Builds the lane's tables.  Returns 0 when built, 1 when the codebook needs
 // the generic decoder, -1 when the lengths are oversubscribed (the canonical
-// assignment of src/codec.cpp:11-29 fails exactly then).
+// assignment of src/codec.cpp:11-29 fails exactly then).  The 256 length
+// bytes arrive through 17 aligned 16-byte loads issued together (one memory
+// round trip instead of a short stream of dependent ones) and only their
+// non-zero bytes are visited (a slab's exponents use a dozen or so symbols); the first three
+// non-zero chunks are kept in the lane's column of the bit ring (rows
+// kSaveChunk.., clear of lpos) for the fill pass.  Short-length counters and
+// fill cursors are 8-bit fields of two registers (lengths 1-4 | 5-PK); a field
+// that wraps (256 codes of one length) shows as a count mismatch.
 __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uint32_t& F,
                                  int& maxlen, uint32_t& Lout) {
-  uint64_t c_lo = 0, c_hi = 0;  // 16-bit counters: lengths 1-4 | 5-PK
-  uint32_t nlong = 0;
+  static_assert(PK == 6, "packed counters cover lengths 1-4 and 5-6");
+  uint32_t c14 = 0, c56 = 0, nshort = 0, nlong = 0;
   bool generic = false;
-  maxlen = 0;
+  uint32_t mx = 0;
 #pragma unroll
   for (int j = 0; j < PNL; ++j) W.cnt[j][lane] = 0;
-  uint32_t nz = 0;  // chunks holding a non-zero length
-  for (int g = 0; g < 16; g += 4) {
-    uint4 vv[4];
+  uint32_t nz = 0;      // chunks holding a non-zero length
+  uint32_t nsaved = 0;  // non-zero chunks kept in the ring rows
+  ByteReader16 rd;
+  rd.init(lens, lens + 256);
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const uint4 v = rd.take();
+    if ((v.x | v.y | v.z | v.w) == 0) continue;
+    nz |= 1u << c16;
+    if (nsaved < 3) {
+      const int r = kSaveChunk + 4 * int(nsaved);
+      W.ring[r][lane] = v.x;
+      W.ring[r + 1][lane] = v.y;
+      W.ring[r + 2][lane] = v.z;
+      W.ring[r + 3][lane] = v.w;
+      ++nsaved;
+    }
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) vv[k] = ld16_any(lens + 16 * (g + k));
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint4 v = vv[k];
-      if ((v.x | v.y | v.z | v.w) == 0) continue;
-      nz |= 1u << (g + k);
-#pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        const uint32_t l = byte_of(v, b);
-        if (!l) continue;
-        maxlen = max(maxlen, int(l));
-        if (l <= 4)
-          c_lo += 1ull << (16 * (l - 1));
-        else if (l <= PK)
-          c_hi += 1ull << (16 * (l - 5));
-        else if (l <= PK + PNL) {
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w = wv[q];
+      while (w) {
+        const uint32_t sh = uint32_t(__ffs(w) - 1) & ~7u;
+        const uint32_t l = (w >> sh) & 255u;
+        w &= ~(255u << sh);
+        mx = max(mx, l);
+        if (l <= PK) {
+          ++nshort;
+          if (l <= 4)
+            c14 += 1u << (8 * (l - 1));
+          else
+            c56 += 1u << (8 * (l - 5));
+        } else if (l <= PK + PNL) {
+          // a u8 counter: more than PLONG long codes send the lane to the
+          // generic decoder, before any count is used
           W.cnt[l - PK - 1][lane] += 1;
           ++nlong;
-        } else
+        } else {
           generic = true;
+        }
       }
     }
   }
+  maxlen = int(mx);
   if (generic || nlong > PLONG) return 1;
-  // first-level start row per short length; Kraft check
-  uint64_t s_lo = 0, s_hi = 0;
-  uint32_t L = 0;
+  // first-level start row per short length (8-bit fields); Kraft check
+  uint32_t s14 = 0, s56 = 0, L = 0, tot = 0;
 #pragma unroll
   for (int l = 1; l <= PK; ++l) {
-    const uint32_t c = l <= 4 ? uint32_t(c_lo >> (16 * (l - 1))) & 0xFFFFu
-                              : uint32_t(c_hi >> (16 * (l - 5))) & 0xFFFFu;
+    const uint32_t c = (l <= 4 ? c14 >> (8 * (l - 1)) : c56 >> (8 * (l - 5))) & 255u;
     if (l <= 4)
-      s_lo |= uint64_t(L) << (16 * (l - 1));
+      s14 |= (L & 255u) << (8 * (l - 1));
     else
-      s_hi |= uint64_t(L) << (16 * (l - 5));
+      s56 |= (L & 255u) << (8 * (l - 5));
     L += c << (PK - l);
+    tot += c;
   }
-  if (L > (1u << PK)) return -1;
+  if (tot != nshort || L > (1u << PK)) return -1;
   uint64_t used = L;
   uint32_t pos = 0;
   for (int l = PK + 1; l <= maxlen; ++l) {
@@ -144,32 +184,42 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
   }
   if (maxlen > PK && used > (1ull << maxlen)) return -1;
   F = L << 1;
-  // fill, re-reading only the non-zero chunks
+  // fill from the saved chunks (re-reading any beyond the first three)
+  uint32_t k = 0;
   while (nz) {
     const int c16 = __ffs(nz) - 1;
     nz &= nz - 1;
-    const uint4 v = ld16_any(lens + 16 * c16);
+    uint4 v;
+    if (k < 3) {
+      const int r = kSaveChunk + 4 * int(k);
+      v = make_uint4(W.ring[r][lane], W.ring[r + 1][lane], W.ring[r + 2][lane], W.ring[r + 3][lane]);
+    } else {
+      v = ld16_any(lens + 16 * c16);
+    }
+    ++k;
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int b = 0; b < 16; ++b) {
-      const uint32_t l = byte_of(v, b);
-      if (!l) continue;
-      const uint32_t s = uint32_t(c16 * 16 + b);
-      if (l <= PK) {
-        uint32_t st;
-        if (l <= 4) {
-          st = uint32_t(s_lo >> (16 * (l - 1))) & 0xFFFFu;
-          s_lo += uint64_t(1u << (PK - l)) << (16 * (l - 1));
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w = wv[q];
+      while (w) {
+        const uint32_t sh = uint32_t(__ffs(w) - 1) & ~7u;
+        const uint32_t l = (w >> sh) & 255u;
+        w &= ~(255u << sh);
+        const uint32_t sym = uint32_t(c16 * 16 + q * 4) + (sh >> 3);
+        if (l <= PK) {
+          const bool lo = l <= 4;
+          const uint32_t fs = 8 * (lo ? l - 1 : l - 5);
+          const uint32_t run = 1u << (PK - l);
+          const uint32_t st = ((lo ? s14 : s56) >> fs) & 255u;
+          s14 += lo ? run << fs : 0u;
+          s56 += lo ? 0u : run << fs;
+          const uint32_t e = (sym << 7) | l;
+          for (uint32_t r = 0; r < run; ++r) W.lut[st + r][lane] = e;
         } else {
-          st = uint32_t(s_hi >> (16 * (l - 5))) & 0xFFFFu;
-          s_hi += uint64_t(1u << (PK - l)) << (16 * (l - 5));
+          const int j = int(l) - PK - 1;
+          W.lsym[W.lpos[j][lane]][lane] = uint8_t(sym);
+          W.lpos[j][lane] += 1;
         }
-        const uint16_t e = uint16_t((s << 7) | l);
-        const uint32_t run = 1u << (PK - l);
-        for (uint32_t k = 0; k < run; ++k) W.lut[st + k][lane] = e;
-      } else {
-        const int j = int(l) - PK - 1;
-        W.lsym[W.lpos[j][lane]][lane] = uint8_t(s);
-        W.lpos[j][lane] += 1;
       }
     }
   }
@@ -177,22 +227,18 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
   for (uint32_t z = L; z < (1u << PK); ++z) W.lut[z][lane] = 0;
   // second level: codes of length PK+1..PK+K2 whose (PK+K2)-bit prefixes fall
   // in the first NE escape prefixes
-  for (int z = 0; z <= (NE << K2); ++z) W.lut2[z][lane] = 0;
-  if (NE == 0) {
-    Lout = L;
-    return 0;
-  }
+  for (int z = 0; z < NROW2; ++z) W.lut2[z][lane] = 0;
   uint32_t cf = F, idx = 0;
   const uint32_t base = L << K2;
   for (int l = PK + 1; l <= maxlen && l <= PK + K2; ++l) {
     const uint32_t c = W.cnt[l - PK - 1][lane];
-    for (uint32_t k = 0; k < c; ++k) {
-      const uint32_t code = cf + k;
+    for (uint32_t q = 0; q < c; ++q) {
+      const uint32_t code = cf + q;
       const uint32_t run = 1u << (PK + K2 - l);
       const uint32_t st = (code << (PK + K2 - l)) - base;
       if (st + run <= uint32_t(NE << K2)) {
-        const uint16_t e = uint16_t((uint32_t(W.lsym[idx + k][lane]) << 7) | uint32_t(l));
-        for (uint32_t q = 0; q < run; ++q) W.lut2[st + q][lane] = e;
+        const uint16_t e = uint16_t((uint32_t(W.lsym[idx + q][lane]) << 7) | uint32_t(l));
+        for (uint32_t r = 0; r < run; ++r) W.lut2[st + r][lane] = e;
       }
     }
     idx += c;
@@ -202,7 +248,8 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
   return 0;
 }
 
-// Entry for a code longer than PK bits: exponent << 7 | length, or 0.
+// Entry for a code longer than PK bits at the top of w: exponent << 7 |
+// length, or 0.
 __device__ __noinline__ uint32_t long_entry(uint32_t w, const WarpTabs& W, int lane, uint32_t F,
                                             int maxlen) {
   uint32_t cf = F, idx = 0;
@@ -216,92 +263,85 @@ __device__ __noinline__ uint32_t long_entry(uint32_t w, const WarpTabs& W, int l
   return 0;
 }
 
-// A lane's exponent bits: 16-byte chunks staged by cp.async into the lane's
-// RING slots (fw = words fetched, rw = words consumed), read through a 96-bit
-// window w0:w1:w2 holding nb valid bits (MSB first).  One refill per four
-// codes keeps nb >= 65, so four codes of up to PK+K2 bits need no check.
-struct LaneBits {
-  const uint4* src;   // next chunk to fetch
-  const uint4* last;  // last chunk holding stream bytes (fetches are clamped to it)
-  uint32_t fw, rw, rw0, skipb;
-  uint32_t w0, w1, w2;
-  int nb;
+// 32 bytes at a 32-byte aligned address (one sm_100 256-bit load).
+struct Chunk32 {
+  uint4 a, b;
+};
+__device__ __forceinline__ Chunk32 ldg32(const void* p) {
+  Chunk32 c;
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(c.a.x), "=r"(c.a.y), "=r"(c.a.z), "=r"(c.a.w), "=r"(c.b.x), "=r"(c.b.y), "=r"(c.b.z),
+                 "=r"(c.b.w)
+               : "l"(p));
+  return c;
+}
 
-  __device__ __forceinline__ void fetch(WarpTabs& W, int lane) {
-    const uint4* q = src <= last ? src : last;
-    cp_async16(&W.ring[(fw >> 2) & (RING - 1)][lane], q);
+// A lane's exponent bit stream.  Word w (counted from the 32-byte aligned
+// chunk holding the stream's first byte) sits big-endian in ring[w % BR]; fw
+// words have entered the ring and the next aligned chunk (`stage`) is already
+// loaded into registers.  `pos` counts bits from that aligned start, so the
+// stream's own bits begin at pos0 = 8 * (start & 31).  Chunk loads are clamped
+// to the last chunk holding stream bytes: only a corrupt stream reads past its
+// end, and the final bit count rejects it.
+struct LaneStream {
+  const Chunk32* src;   // next chunk to load
+  const Chunk32* last;  // last chunk holding stream bytes
+  Chunk32 c0;           // first chunk (loaded before the table build)
+  Chunk32 stage;        // next chunk, loaded, not yet in the ring
+  uint32_t fw, pos, pos0;
+
+  __device__ __forceinline__ Chunk32 fetch() {
+    const Chunk32* q = src <= last ? src : last;
     ++src;
-    fw += 4;
+    return ldg32(q);
   }
-  __device__ __forceinline__ uint32_t word(const WarpTabs& W, int lane, uint32_t k) const {
-    return bswap32(reinterpret_cast<const uint32_t*>(&W.ring[(k >> 2) & (RING - 1)][lane])[k & 3]);
-  }
-  __device__ __forceinline__ void init(WarpTabs& W, int lane, const uint8_t* base, uint64_t nbytes) {
+  // Issues the first loads; the ring is written by init_ring() once the
+  // table build no longer needs the memory it shares.
+  __device__ __forceinline__ void start(const uint8_t* base, uint64_t nbytes) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(base);
-    src = reinterpret_cast<const uint4*>(a & ~uintptr_t(15));
-    last = reinterpret_cast<const uint4*>((a + (nbytes ? nbytes - 1 : 0)) & ~uintptr_t(15));
+    src = reinterpret_cast<const Chunk32*>(a & ~uintptr_t(31));
+    last = reinterpret_cast<const Chunk32*>((a + (nbytes ? nbytes - 1 : 0)) & ~uintptr_t(31));
+    pos0 = pos = uint32_t(a & 31) * 8;
+    c0 = fetch();
+    stage = fetch();
+  }
+  __device__ __forceinline__ void put(WarpTabs& W, int lane, const Chunk32& c) {
+    W.ring[(fw + 0) & (BR - 1)][lane] = bswap32(c.a.x);
+    W.ring[(fw + 1) & (BR - 1)][lane] = bswap32(c.a.y);
+    W.ring[(fw + 2) & (BR - 1)][lane] = bswap32(c.a.z);
+    W.ring[(fw + 3) & (BR - 1)][lane] = bswap32(c.a.w);
+    W.ring[(fw + 4) & (BR - 1)][lane] = bswap32(c.b.x);
+    W.ring[(fw + 5) & (BR - 1)][lane] = bswap32(c.b.y);
+    W.ring[(fw + 6) & (BR - 1)][lane] = bswap32(c.b.z);
+    W.ring[(fw + 7) & (BR - 1)][lane] = bswap32(c.b.w);
+    fw += 8;
+  }
+  __device__ __forceinline__ void init_ring(WarpTabs& W, int lane) {
     fw = 0;
-    for (int k = 0; k < RING; ++k) fetch(W, lane);
-    cp_async_commit();
-    cp_async_wait_all();
-    rw0 = rw = uint32_t(a & 15) >> 2;
-    skipb = uint32_t(a & 3) * 8;
-    w0 = word(W, lane, rw);
-    w1 = word(W, lane, rw + 1);
-    w2 = word(W, lane, rw + 2);
-    rw += 3;
-    w0 = __funnelshift_l(w1, w0, skipb);
-    w1 = __funnelshift_l(w2, w1, skipb);
-    w2 = __funnelshift_l(0u, w2, skipb);
-    nb = 96 - int(skipb);
+    put(W, lane, c0);
   }
-  // Once per 16 codes (every lane at the same point): keep >= 8 unread words
-  // staged, and make sure every staged word this stretch may read has landed.
+  // Moves the staged chunk into the ring and loads the next one.
+  __device__ __forceinline__ void advance(WarpTabs& W, int lane) {
+    put(W, lane, stage);
+    stage = fetch();
+  }
+  // Keeps at least kRingLow unread words in the ring: four checked blocks
+  // (<= 32 bits each) and the last snapshot's second word need five; a chunk
+  // enters only when it fits (fw - word <= BR - 8), so the chunk staged here
+  // was loaded several groups earlier.
   __device__ __forceinline__ void maintain(WarpTabs& W, int lane) {
-    int nf = 0;
-    while (fw - rw <= uint32_t(4 * RING - 4)) {
-      fetch(W, lane);
-      ++nf;
-    }
-    cp_async_commit();
-    if (nf <= 1 && fw - rw >= uint32_t(4 * RING - 4))
-      cp_async_wait_1();
-    else
-      cp_async_wait_all();
+    while (fw - (pos >> 5) < kRingLow) advance(W, lane);
   }
-  // Inserts the next word at bit nb when nb <= 64, without a data-dependent
-  // branch (needs nb >= 1).
-  __device__ __forceinline__ void refill(const WarpTabs& W, int lane) {
-    const bool need = nb <= 64;
-    const uint32_t wd = word(W, lane, rw);  // unconditional load of a ring slot, then a select
-    const uint32_t t = need ? wd : 0u;
-    const bool low = nb < 32;  // lands in w0:w1, else in w1:w2
-    const uint32_t k = uint32_t(low ? nb : nb - 32);
-    const uint32_t head = __funnelshift_rc(t, 0u, k), tail = __funnelshift_rc(0u, t, k);
-    w0 |= low ? head : 0u;
-    w1 |= low ? tail : head;
-    w2 |= low ? 0u : tail;
-    nb += need ? 32 : 0;
-    rw += need ? 1u : 0u;
-  }
-  __device__ __forceinline__ void skip(uint32_t n) {  // n: low 5 bits used
-    w0 = __funnelshift_l(w1, w0, n);
-    w1 = __funnelshift_l(w2, w1, n);
-    w2 = __funnelshift_l(0u, w2, n);
-    nb -= int(n & 31u);
-  }
-  __device__ __forceinline__ void shift(uint32_t n) {  // skip without updating nb
-    w0 = __funnelshift_l(w1, w0, n);
-    w1 = __funnelshift_l(w2, w1, n);
-    w2 = __funnelshift_l(0u, w2, n);
-  }
-  __device__ __forceinline__ uint64_t consumed() const {
-    return uint64_t(rw - rw0) * 32 - uint64_t(nb) - skipb;
+  // The 32 bits at pos.
+  __device__ __forceinline__ uint32_t snap(const WarpTabs& W, int lane) const {
+    const uint32_t j = pos >> 5;
+    const uint32_t a = W.ring[j & (BR - 1)][lane], b = W.ring[(j + 1) & (BR - 1)][lane];
+    return __funnelshift_l(b, a, pos);
   }
 };
 
 // A lane's sign/mantissa bytes for 16-code groups: aligned 16-byte chunks
-// staged by cp.async two groups ahead, realigned when a group is consumed.
+// staged by cp.async three groups ahead, realigned when a group is consumed.
 struct LaneSm {
   const uint4* src;
   const uint4* last;
@@ -322,8 +362,8 @@ struct LaneSm {
     fetch(W, lane, 1);
     fetch(W, lane, 2);
   }
-  // Called in step with LaneBits::maintain (same commit group): stages the
-  // chunk three ahead of the group about to be consumed.
+  // Stages the chunk three ahead of the group about to be consumed (its slot
+  // held the chunk the previous group read first).
   __device__ __forceinline__ void stage(WarpTabs& W, int lane) { fetch(W, lane, g + 3); }
   __device__ __forceinline__ uint4 take(const WarpTabs& W, int lane) {
     const uint4 r0 = W.smring[g & (SMR - 1)][lane];
@@ -341,81 +381,65 @@ struct LaneSm {
   }
 };
 
+__device__ __forceinline__ void cp_async_wait_2() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
+
 struct LaneCode {
-  uint32_t F;  // first code of length PK+1
-  uint32_t L;  // first escape prefix (PK-bit units)
+  uint32_t F;   // first code of length PK+1
+  uint32_t L2;  // first escape prefix << K2 (second-level index origin)
   int maxlen;
 };
 
-// Codes the two table levels do not hold (longer than PK+K2 bits, or beyond
-// the covered escape prefixes): the compact list, then a top-up of the window
-// and the ring so the rest of the group still has its bits.
-__device__ __forceinline__ void top_up(LaneBits& b, WarpTabs& W, int lane) {
-  if (b.nb < 65) {
-    if (b.rw + 1 >= b.fw) {
-      b.fetch(W, lane);
-      cp_async_commit();
-    }
-    if (b.rw + 4 >= b.fw) cp_async_wait_all();
-    b.refill(W, lane);
-  }
-}
-
-__device__ __forceinline__ uint32_t rare_entry(LaneBits& b, WarpTabs& W, int lane,
-                                            const LaneCode& lc, bool& bad) {
-  top_up(b, W, lane);  // >= 33 bits: a whole long code (<= PK+PNL bits) is in w0
-  uint32_t e = long_entry(b.w0, W, lane, lc.F, lc.maxlen);
-  if ((e & 31u) == 0) bad = true;
-  b.skip(e);
-  top_up(b, W, lane);
-  return e;
-}
-
-// Table lookup of the code at the window head: exponent << 7 | length, or 0
+// Table lookup of the code at the top of w: exponent << 7 | length, or 0
 // when neither level holds it.  No branch: a prefix outside the second level
 // reads its all-zero last row, and a short code (first level) always has a
 // prefix below the escape rows, so at most one level is non-zero.
-__device__ __forceinline__ uint32_t lookup(const LaneBits& b, const WarpTabs& W, int lane,
-                                          uint32_t L5) {
-  const uint32_t h = b.w0;
-  const uint32_t e1 = W.lut[h >> (32 - PK)][lane];
-  const uint32_t i2 = min((h >> (32 - PK - K2)) - L5, uint32_t(NE << K2));
+__device__ __forceinline__ uint32_t lookup(uint32_t w, const WarpTabs& W, int lane, uint32_t L2) {
+  const uint32_t e1 = W.lut[w >> (32 - PK)][lane];
+  // min(prefix - L2, NE << K2) in one add-min (DPX) instruction
+  const uint32_t i2 = __viaddmin_u32(w >> (32 - PK - K2), 0u - L2, uint32_t(NE << K2));
   return e1 | uint32_t(W.lut2[i2][lane]);
 }
 
-// One code with the rare path.
-__device__ __forceinline__ uint32_t dec(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
-                                       bool& bad) {
-  const uint32_t e = lookup(b, W, lane, lc.L << K2);
-  if (e == 0) return rare_entry(b, W, lane, lc, bad);
-  b.skip(e);
+// One code at pos, with the compact long-code list behind the tables and a
+// ring top-up first (any code the lane can hold has <= PK+PNL <= 32 bits).
+__device__ __forceinline__ uint32_t dec_one(LaneStream& b, WarpTabs& W, int lane, const LaneCode& lc,
+                                            bool& bad) {
+  if (b.fw - (b.pos >> 5) < 2u) b.advance(W, lane);  // the ring keeps >= 2 unread words
+  const uint32_t w = b.snap(W, lane);
+  uint32_t e = lookup(w, W, lane, lc.L2);
+  if (e == 0) {
+    e = long_entry(w, W, lane, lc.F, lc.maxlen);
+    if ((e & 31u) == 0) bad = true;
+  }
+  b.pos += e & 31u;
   return e;
 }
 
-// Four codes from a window holding >= 4*(PK+K2) bits, without a branch in the
-// common case.  A code neither level holds has entry 0, which skips no bits,
-// so the rest of the block looks up the same code and is 0 too: e3 == 0 tells
-// that the window stopped at such a code, and the block finishes code by code
-// from there.
-__device__ __forceinline__ void dec4(LaneBits& b, WarpTabs& W, int lane, const LaneCode& lc,
-                                     bool& bad, uint32_t& e0, uint32_t& e1, uint32_t& e2,
-                                     uint32_t& e3) {
-  const uint32_t L5 = lc.L << K2;
-  e0 = lookup(b, W, lane, L5);
-  b.shift(e0);
-  e1 = lookup(b, W, lane, L5);
-  b.shift(e1);
-  e2 = lookup(b, W, lane, L5);
-  b.shift(e2);
-  e3 = lookup(b, W, lane, L5);
-  b.shift(e3);
+// Four codes from one 32-bit snapshot.  A code k read from bits past the
+// snapshot (its start s_k plus its length above 32) makes the block's total
+// exceed 32; a code it decodes with s_k + length <= 32 used only real bits and
+// is the true code (prefix property).  So total <= 32 and a non-zero last
+// entry prove the whole block; anything else is redone code by code.
+__device__ __forceinline__ void dec4(LaneStream& b, WarpTabs& W, int lane, const LaneCode& lc, bool& bad,
+                                     uint32_t& e0, uint32_t& e1, uint32_t& e2, uint32_t& e3) {
+  uint32_t w = b.snap(W, lane);
+  e0 = lookup(w, W, lane, lc.L2);
+  w = __funnelshift_l(0u, w, e0);  // w << (length & 31)
+  e1 = lookup(w, W, lane, lc.L2);
+  w = __funnelshift_l(0u, w, e1);
+  e2 = lookup(w, W, lane, lc.L2);
+  w = __funnelshift_l(0u, w, e2);
+  e3 = lookup(w, W, lane, lc.L2);
   // lengths sit in bits 0-4 above zero bits 5-6, so one sum carries all four
-  b.nb -= int((e0 + e1 + e2 + e3) & 127u);
-  if (e3 == 0) {
-    if (e0 == 0) e0 = dec(b, W, lane, lc, bad);
-    if (e1 == 0) e1 = dec(b, W, lane, lc, bad);
-    if (e2 == 0) e2 = dec(b, W, lane, lc, bad);
-    e3 = dec(b, W, lane, lc, bad);
+  const uint32_t s = (e0 + e1 + e2 + e3) & 127u;
+  if (s > 32u || e3 == 0) {
+    e0 = dec_one(b, W, lane, lc, bad);
+    e1 = dec_one(b, W, lane, lc, bad);
+    e2 = dec_one(b, W, lane, lc, bad);
+    e3 = dec_one(b, W, lane, lc, bad);
+    b.maintain(W, lane);
+  } else {
+    b.pos += s;
   }
 }
 
@@ -441,30 +465,26 @@ __device__ __forceinline__ void emit_one(const Out& o, uint32_t p, uint32_t word
   }
 }
 
-// Decodes one substream.  `nice`: 16-row slab, cols % 16 == 0 and (decode)
-// 16-byte aligned output; whole tile rows then leave as two 16-byte stores.
+// Decodes one substream.  `rows16`: 16-row slab, cols % 16 == 0, the
+// substream starts on a tile row and (decode) the output is 16-byte aligned;
+// whole tile rows then leave as 32-byte stores.  The caller has started `b`
+// and `smr` and put the first words into the ring.
 template <int MODE>
-__device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCode& lc,
-                               bool nice, const Out& o, bool& bad) {
-  const bool rows16 = nice && (s.start & 15) == 0;
-  LaneSm smr;
-  if (rows16) smr.init(W, lane, s.sm, s.sm + s.count);
-  LaneBits b;
-  b.init(W, lane, s.bits, s.ebytes);  // its commit/wait also covers the first sm chunks
-  uint32_t i = 0, p = s.start;
-  while (i < s.count) {
-    if (rows16) smr.stage(W, lane);
-    b.maintain(W, lane);
-    const uint32_t n = min(16u, s.count - i);
-    if (rows16 && n == 16) {
+__device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCode& lc, bool rows16,
+                               LaneStream& b, LaneSm& smr, const Out& o, bool& bad) {
+  uint32_t i = 0;
+  if (rows16) {
+    const uint32_t ng = s.count >> 4;
+    uint32_t p = s.start;
+    for (uint32_t g = 0; g < ng; ++g, p += 16) {
+      smr.stage(W, lane);
+      cp_async_commit();
+      b.maintain(W, lane);
+      cp_async_wait_2();  // this group's two chunks were committed two groups ago
       const uint4 s16 = smr.take(W, lane);
       uint32_t e[16];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        b.refill(W, lane);
-        if (b.nb < 4 * (PK + K2)) b.refill(W, lane);  // rare: four codes of <= PK+K2 bits
-        dec4(b, W, lane, lc, bad, e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]);
-      }
+      for (int k = 0; k < 4; ++k) dec4(b, W, lane, lc, bad, e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]);
       const uint32_t r = (p >> 4) & 15, c = (p >> 8) * 16;
       if (MODE == 0) {
         uint4 v0, v1;
@@ -493,12 +513,12 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
           const float4* xv = reinterpret_cast<const float4*>(o.x + c);
           float acc = 0.f;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 xq = __ldg(xv + q);
-            acc = fmaf(wf[4 * q], xq.x, acc);
-            acc = fmaf(wf[4 * q + 1], xq.y, acc);
-            acc = fmaf(wf[4 * q + 2], xq.z, acc);
-            acc = fmaf(wf[4 * q + 3], xq.w, acc);
+          for (int qq = 0; qq < 4; ++qq) {
+            const float4 xq = __ldg(xv + qq);
+            acc = fmaf(wf[4 * qq], xq.x, acc);
+            acc = fmaf(wf[4 * qq + 1], xq.y, acc);
+            acc = fmaf(wf[4 * qq + 2], xq.z, acc);
+            acc = fmaf(wf[4 * qq + 3], xq.w, acc);
           }
           atomicAdd(&o.ysm[r * PMAXB], acc);
         } else {
@@ -510,19 +530,15 @@ __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCo
           }
         }
       }
-    } else {
-      for (uint32_t k = 0; k < n; ++k) {
-        b.refill(W, lane);
-        if (b.nb < 65) b.refill(W, lane);
-        const uint32_t e = dec(b, W, lane, lc, bad);
-        emit_one<MODE>(o, p + k, merge1(e, __ldg(s.sm + i + k)));
-      }
     }
-    i += n;
-    p += n;
+    i = ng << 4;
+  }
+  for (; i < s.count; ++i) {
+    const uint32_t e = dec_one(b, W, lane, lc, bad);
+    emit_one<MODE>(o, s.start + i, merge1(e, __ldg(s.sm + i)));
   }
   cp_async_wait_all();
-  if (b.consumed() != s.nbits) bad = true;
+  if (uint64_t(b.pos - b.pos0) != s.nbits) bad = true;
 }
 
 // Lane 0 decodes a substream whose codebook needs the generic decoder.
@@ -565,6 +581,10 @@ __device__ bool decode_segment_generic(const Seg& s, GenericTab& G, const Out& o
   return pos == s.nbits;
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ uint64_t warp_incl_scan(uint64_t v, int lane) {
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
@@ -575,7 +595,7 @@ __device__ __forceinline__ uint64_t warp_incl_scan(uint64_t v, int lane) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(PWARPS * 32)
+__global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 7 : 1)
     parallel_slab_kernel(const Slab* __restrict__ slabs, uint32_t nslabs,
                          const uint8_t* __restrict__ payload, uint8_t* __restrict__ out,
                          const float* __restrict__ x, float* __restrict__ y, uint32_t ld,
@@ -589,14 +609,32 @@ __global__ void __launch_bounds__(PWARPS * 32)
     const Slab sd = slabs[si];
     const uint8_t* p = payload + sd.src;
     const uint64_t n = sd.size;
+    // ---- the warp's next slab: its header lines go to L2 now and its
+    // substream table is read here, so that once this slab's tables are built
+    // the next slab's substream headers and length tables can be prefetched
+    // too; its setup then finds every dependent load in L2 ----
+    const uint32_t sn = si + gridDim.x * PWARPS;
+    const uint8_t* np = nullptr;
+    uint64_t nsize = 0, nlen = 0, ntotal = 0;
+    if (sn < nslabs) {
+      const Slab nd = slabs[sn];
+      np = payload + nd.src;
+      nsize = nd.size;
+      ntotal = nd.rows * nd.cols;
+      if (uint64_t(lane) * 128 < (nsize < 288 ? nsize : 288)) prefetch_l2(np + 128 * lane);
+      if (40 + 8 * uint64_t(lane) <= nsize) nlen = ld8_any(np + 32 + 8 * lane, np + nsize);
+    }
     // ---- container header (cuda/parallel.cu:34-36) ----
     bool ok = n >= 32;
     uint64_t rows = 0, cols = 0, chunks = 0;
     if (ok) {
-      ok = ld_le64(p) == 0x0000003250534B58ull;  // "XKSP2\0\0\0"
-      rows = ld_le64(p + 8);
-      cols = ld_le64(p + 16);
-      chunks = ld_le64(p + 24);
+      // header fields through aligned 8-byte loads (the slab may sit at any
+      // byte offset; n >= 32 keeps every read inside the slab's words)
+      const uint8_t* pe = p + n;
+      ok = ld8_any(p, pe) == 0x0000003250534B58ull;  // "XKSP2\0\0\0"
+      rows = ld8_any(p + 8, pe);
+      cols = ld8_any(p + 16, pe);
+      chunks = ld8_any(p + 24, pe);
       ok = ok && rows && rows <= 16 && cols && chunks && chunks <= 32 &&
            cols <= ~0ull / rows && chunks <= rows * cols && rows * cols <= n &&
            rows * cols <= ~0ull / 32 && n >= 32 + 8 * chunks && rows == sd.rows &&
@@ -613,7 +651,7 @@ __global__ void __launch_bounds__(PWARPS * 32)
     // ---- substream table (cuda/parallel.cu:39-51) ----
     const uint32_t total = uint32_t(rows * cols);
     const bool active = uint64_t(lane) < chunks;
-    const uint64_t len = active ? ld_le64(p + 32 + 8 * lane) : 0;
+    const uint64_t len = active ? ld8_any(p + 32 + 8 * lane, p + n) : 0;
     bool lok = !active || (len >= kHdr && len <= n);
     const uint64_t incl = warp_incl_scan(lok ? len : 0, lane);
     const uint64_t base = 32 + 8 * chunks + incl - len;
@@ -622,8 +660,8 @@ __global__ void __launch_bounds__(PWARPS * 32)
       lok = base + len <= n;
       if (lok) {
         const uint8_t* q = p + base;
-        const uint64_t count = ld_le64(q);
-        s.nbits = ld_le64(q + 8);
+        const uint64_t count = ld8_any(q, p + n);
+        s.nbits = ld8_any(q + 8, p + n);
         s.start = uint32_t(uint64_t(total) * uint64_t(lane) / chunks);
         const uint64_t expect = uint64_t(total) * uint64_t(lane + 1) / chunks - s.start;
         s.ebytes = s.nbits / 8 + (s.nbits % 8 != 0);
@@ -639,14 +677,12 @@ __global__ void __launch_bounds__(PWARPS * 32)
       if (lane == 0) atomicOr(status, kStatusHeader);
       continue;
     }
-    // ---- per-lane tables ----
-    LaneCode lc{0, 0, 0};
-    const int tb = active ? build_lane_tables(s.lens, W, lane, lc.F, lc.maxlen, lc.L) : 0;
-    if (__any_sync(0xffffffffu, tb < 0)) {
-      if (lane == 0) atomicOr(status, kStatusCodebook);
+    // bit positions are 32-bit (the slab format bounds them far lower: a
+    // substream's bits fit in its slab, and compiled slabs are <= 1 MiB)
+    if (__any_sync(0xffffffffu, s.nbits >= (1ull << 32) - 256)) {
+      if (lane == 0) atomicOr(status, kStatusInternal);
       continue;
     }
-    __syncwarp();  // every lane's build is done before the bit ring (over lpos) fills
     Out o;
     o.out = reinterpret_cast<uint16_t*>(out + sd.dst);
     o.x = MODE == 1 ? x + sd.xoff * ld : nullptr;
@@ -657,14 +693,52 @@ __global__ void __launch_bounds__(PWARPS * 32)
     o.nb = nb;
     o.xvec = nb == 1 && ld == 1 && (reinterpret_cast<uintptr_t>(o.x) & 15) == 0;
     o.out32 = (reinterpret_cast<uintptr_t>(o.out) & 31) == 0;
+    const bool nice = rows == 16 && (cols & 15) == 0 &&
+                      (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
+    const bool rows16 = nice && (s.start & 15) == 0;
+    // ---- first bit and sign/mantissa loads, overlapping the table build ----
+    LaneStream b;
+    LaneSm smr;
+    if (active) {
+      b.start(s.bits, s.ebytes);
+      if (rows16) smr.init(W, lane, s.sm, s.sm + s.count);
+    }
+    cp_async_commit();
+    // ---- per-lane tables ----
+    LaneCode lc{0, 0, 0};
+    uint32_t L = 0;
+    const int tb = active ? build_lane_tables(s.lens, W, lane, lc.F, lc.maxlen, L) : 0;
+    lc.L2 = L << K2;
+    __syncwarp();
+    if (np) {  // next slab's substream headers and length tables to L2
+      const uint64_t nch = ntotal < 32 ? ntotal : 32;
+      const bool na = uint64_t(lane) < nch;
+      const uint64_t nl = na ? nlen : 0;
+      const uint64_t off = 32 + 8 * nch + warp_incl_scan(nl, lane) - nl;
+      if (na && nl >= kHdr && off <= nsize && kHdr <= nsize - off) {
+        prefetch_l2(np + off);
+        prefetch_l2(np + off + 128);
+        prefetch_l2(np + off + kHdr - 1);
+      }
+    }
+    if (__any_sync(0xffffffffu, tb < 0)) {
+      cp_async_wait_all();
+      __syncwarp();
+      if (lane == 0) atomicOr(status, kStatusCodebook);
+      continue;
+    }
+    __syncwarp();  // every lane's build is done before the bit ring (over lpos) fills
     if (MODE == 1) {
       for (int k = lane; k < 16 * PMAXB; k += 32) ysm[k] = 0.f;
       __syncwarp();
     }
-    const bool nice = rows == 16 && (cols & 15) == 0 &&
-                      (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
     bool bad = false;
-    if (active && tb == 0) decode_segment<MODE>(s, W, lane, lc, nice, o, bad);
+    if (active && tb == 0) {
+      b.init_ring(W, lane);
+      cp_async_wait_all();
+      decode_segment<MODE>(s, W, lane, lc, rows16, b, smr, o, bad);
+    }
+    cp_async_wait_all();
     // ---- substreams that need the generic decoder ----
     uint32_t gmask = __ballot_sync(0xffffffffu, active && tb == 1);
     __syncwarp();
@@ -690,22 +764,25 @@ __global__ void __launch_bounds__(PWARPS * 32)
     if (MODE == 1) {
       __syncwarp();
       for (uint32_t k = lane; k < uint32_t(rows) * nb; k += 32) {
-        const uint32_t r = k / nb, b = k - r * nb;
-        y[(sd.dst + r) * ld + b] = ysm[r * PMAXB + b];
+        const uint32_t r = k / nb, bb = k - r * nb;
+        y[(sd.dst + r) * ld + bb] = ysm[r * PMAXB + bb];
       }
       __syncwarp();
     }
   }
 }
 
+// Dynamic shared memory opt-in, once per device (concurrent first calls both
+// set the same value, which is harmless).
 void set_attr_once() {
-  static int done_mask = 0;
+  static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && ((done_mask >> dev) & 1)) return;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return;
   cudaFuncSetAttribute(parallel_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes[0]));
   cudaFuncSetAttribute(parallel_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes[1]));
-  if (dev < 31) done_mask |= 1 << dev;
+  if (bit) done.fetch_or(bit, std::memory_order_release);
 }
 
 }  // namespace
