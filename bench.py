@@ -184,72 +184,165 @@ def time_steps(fn, steps, stream):
     return start.elapsed_time(stop) / 1e3
 
 
-def cpu_reference_decode(payload, slabs, seconds, threads):
-    """Times the reference CPU codec (oracle/_ref, compiled from the reference
-    sources) -- or the oracle port when that build is absent -- over slabs of
-    the workload on `threads` host threads for about `seconds`.  Returns
-    (GB/s of BF16 out, kind, cores, sample description)."""
+def workload_config(world):
+    """The `config` of the headline line, from the workload's definition alone,
+    so the reference arm (which never builds the GPU archive) prints the same
+    dict as this arm."""
+    tensors = llama_tensors(**CONFIG2)
+    return dict(workload="configs[1]: Llama-1.1B-shaped checkpoint (h2048, 22L, 32/4 heads, FFN 5632, "
+                         "vocab 32000, untied), dfloat11-parallel, whole-checkpoint decode per GPU",
+                codec="bf16-huffman-parallel32", weights="BF16 N(0, 0.02) seed 1, norms 1.0",
+                tensors=len(tensors), out_bytes=sum(r * c * 2 for _, r, c, _ in tensors),
+                l2="inputs (compressed + decoded, ~3.9 GB) larger than L2 (126 MB); no flush",
+                parallelism=f"slab partition, {world} independent GPU(s), no collective")
+
+
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _bf16_rne(x):
+    """float32 numpy array -> BF16 bit patterns (round to nearest even)."""
+    import numpy as np
+    u = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype("<u2")
+
+
+CPU_SAMPLE_FRACTION = 0.1
+
+
+def cpu_sample(threads, fraction=CPU_SAMPLE_FRACTION, sigma=0.02, seed=1):
+    """A stratified sample of the configs[1] checkpoint for the CPU legs: the
+    first `fraction` of every tensor's 16-row slabs (every norm whole), drawn
+    with numpy (seeded per tensor) and encoded by the reference's own encoder
+    (oracle/_ref xksv_pack_parallel; a slab that does not shrink is stored raw,
+    src/compile.cpp:264-273, slab rows as src/compile.cpp:471-479).  Returns
+    (reference library or None, kind, [dict(blob, raw, rows, cols, codec)]).
+    Loads no library of this repository's product."""
+    import numpy as np
     from concurrent.futures import ThreadPoolExecutor
 
     from oracle.oracle import Oracle, Reference
-
     try:
         lib, kind = Reference(), "reference"
-        unpack, unpack_par, free = (lib.lib.xksv_unpack, lib.lib.xksv_unpack_parallel, lib.lib.xksv_free)
     except OSError:
         lib, kind = Oracle(), "port"
-        unpack, unpack_par, free = (lib.lib.oracle_unpack, lib.lib.oracle_unpack_parallel, lib.lib.oracle_free)
-    base = payload.ctypes.data
-    work = [s for s in slabs if s["codec"] != 0]
-
-    def one(s):
-        out, size = ctypes.c_void_p(), ctypes.c_size_t()
-        p = ctypes.c_void_p(base + s["src_offset"])
-        if s["codec"] == 2:
-            rc = unpack_par(p, s["src_size"], ctypes.byref(out), ctypes.byref(size))
+    jobs = []
+    for i, (name, rows, cols, kind_t) in enumerate(llama_tensors(**CONFIG2)):
+        nslab = -(-rows // 16)
+        take = nslab if kind_t == "norm" else max(1, int(nslab * fraction))
+        r = min(rows, take * 16)
+        if kind_t == "norm":
+            w = np.full((r, cols), 0x3F80, dtype="<u2")
         else:
-            rc = unpack(p, s["src_size"], s["rows"], s["cols"], ctypes.byref(out), ctypes.byref(size))
-        if rc:
-            raise RuntimeError("CPU decode failed")
-        free(out)
-        return size.value
+            rng = np.random.default_rng([seed, i])
+            w = _bf16_rne(rng.standard_normal((r, cols), dtype=np.float32) * sigma)
+        for r0 in range(0, r, 16):
+            jobs.append((w[r0:r0 + 16].tobytes(), min(16, r - r0), cols))
 
-    done = 0
-    n = 0
-    t0 = time.perf_counter()
+    def enc(job):
+        raw, rows, cols = job
+        blob = lib.pack_parallel(raw, rows, cols)
+        if len(blob) < len(raw):
+            return dict(blob=blob, raw=raw, rows=rows, cols=cols, codec=2)
+        return dict(blob=raw, raw=raw, rows=rows, cols=cols, codec=0)
+
     with ThreadPoolExecutor(max_workers=threads) as ex:
-        i = 0
-        while i < len(work) and time.perf_counter() - t0 < seconds:
-            batch = work[i:i + 4 * threads]
-            done += sum(ex.map(one, batch))
-            n += len(batch)
-            i += len(batch)
+        slabs = list(ex.map(enc, jobs))
+    return lib, kind, slabs
+
+
+def cpu_decode_rate(lib, slabs, threads, seconds, check=False):
+    """Reference CPU decode (xksv_unpack_parallel; raw slabs are copies) of the
+    sample on `threads` host threads, repeated for at least `seconds` (one
+    pass at least).  With `check`, an untimed pass first compares every
+    decoded slab with its source bytes.  Returns (GB/s of BF16 out, passes,
+    seconds, bytes_match)."""
+    import ctypes
+    from concurrent.futures import ThreadPoolExecutor
+    coded = [s for s in slabs if s["codec"] == 2]
+    bufs = [ctypes.create_string_buffer(s["blob"], len(s["blob"])) for s in coded]
+    unpack = getattr(lib.lib, lib.prefix + "unpack_parallel")
+    free = getattr(lib.lib, lib.prefix + "free")
+
+    def one(k, check=False):
+        out, size = ctypes.c_void_p(), ctypes.c_size_t()
+        if unpack(bufs[k], len(coded[k]["blob"]), ctypes.byref(out), ctypes.byref(size)):
+            raise RuntimeError("reference CPU decode failed")
+        ok = True
+        if check:
+            ok = ctypes.string_at(out, size.value) == coded[k]["raw"]
+        free(out)
+        return size.value, ok
+
+    match = True
+    done, passes = 0, 0
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        if check:
+            match = all(r[1] for r in ex.map(lambda k: one(k, True), range(len(coded))))
+        t0 = time.perf_counter()
+        while passes == 0 or time.perf_counter() - t0 < seconds:
+            done += sum(r[0] for r in ex.map(one, range(len(coded))))
+            passes += 1
     dt = time.perf_counter() - t0
-    return done / dt / 1e9, kind, threads, f"{n} of {len(work)} coded slabs ({done / 1e9:.3f} GB BF16 out) in {dt:.1f} s"
+    return done / dt / 1e9, passes, dt, bool(match)
+
+
+def cpu_baseline(seconds):
+    """The reference's CPU decode of the workload, on the GPU box's host: one
+    thread (how the reference itself decodes: per block in sequence,
+    src/verify.cpp:251-255, python/xksv.py:370) and every host thread (one slab
+    per task).  `value` is the all-thread figure."""
+    threads = host_threads(1)
+    lib, kind, slabs = cpu_sample(threads)
+    out = sum(len(s["raw"]) for s in slabs if s["codec"] == 2)
+    v1, p1, t1, ok1 = cpu_decode_rate(lib, slabs, 1, seconds / 2, check=True)
+    vn, pn, tn, okn = cpu_decode_rate(lib, slabs, threads, seconds / 2)
+    return dict(value=round(vn, 3), unit="GB/s", cores=threads, kind=kind,
+                single_thread=dict(value=round(v1, 3), unit="GB/s", cores=1),
+                cpu_model=cpu_model(), bytes_match=ok1 and okn,
+                sample=(f"{len([s for s in slabs if s['codec'] == 2])} coded slabs ({out / 1e9:.3f} GB BF16 out: "
+                        f"the first {int(CPU_SAMPLE_FRACTION * 100)} % of every tensor's slabs, numpy-drawn, encoded "
+                        f"by the reference encoder), decoded {p1} x on 1 thread in {t1:.1f} s and {pn} x on "
+                        f"{threads} threads in {tn:.1f} s; every slab byte-checked in an untimed pass"))
 
 
 def run_reference(args, rank, world):
-    import numpy as np
-    import torch
+    """The reference arm: the reference's own CPU decode (oracle/_ref, built
+    from its sources) of the headline workload on this box's host threads.
+    It loads no library of this repository's product (no GPU path)."""
     if rank != 0:
         return
-    dev = "cuda:0" if torch.cuda.is_available() else "cpu"
-    tensors = llama_tensors(**CONFIG2)
-    payload, slabs, out_bytes, _ = build_archive(tensors, 2, 0.02, 1, dev, host_threads(1))
     threads = host_threads(1)
+    lib, kind, slabs = cpu_sample(threads)
     vals = []
-    for _ in range(max(1, args.warmup_cpu)):
-        cpu_reference_decode(payload, slabs, 2.0, threads)
+    _, _, _, match = cpu_decode_rate(lib, slabs, threads, 0.0, check=True)  # warm-up, byte-checked
+    for _ in range(max(0, args.warmup_cpu)):
+        cpu_decode_rate(lib, slabs, threads, 0.0)
+    t_all = 0.0
     for _ in range(args.steps):
-        v, kind, cores, sample = cpu_reference_decode(payload, slabs, args.cpu_seconds, threads)
+        v, _, dt, _ = cpu_decode_rate(lib, slabs, threads, 0.0)
         vals.append(v)
+        t_all += dt
     value = statistics.median(vals)
+    coded = [s for s in slabs if s["codec"] == 2]
+    out = sum(len(s["raw"]) for s in coded)
+    sample = (f"{len(coded)} coded slabs ({out / 1e9:.3f} GB BF16 out: the first {int(CPU_SAMPLE_FRACTION * 100)} % "
+              f"of every tensor's slabs, numpy-drawn, encoded by the reference encoder); one decode pass of the "
+              f"sample per step, {args.steps} steps in {t_all:.1f} s; median step")
     line = dict(metric=METRIC, value=round(value, 3), unit="GB/s", impl="reference", n_gpus=world,
-                steps=args.steps, warmup=args.warmup, higher_is_better=True, scaling="weak",
-                vs_baseline=None, dtype="bf16", data="synthetic",
-                config=dict(workload="configs[1]: Llama-1.1B-shaped checkpoint, dfloat11-parallel, whole-checkpoint decode",
-                            out_bytes=out_bytes),
-                cpu_baseline=dict(value=round(value, 3), unit="GB/s", cores=cores, kind=kind, sample=sample),
+                steps=args.steps, warmup=args.warmup, ms_per_step=round(t_all / max(1, args.steps) * 1e3, 3),
+                higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+                data="synthetic: seeded BF16 N(0,0.02) Llama-1.1B-shaped weights, norms 1.0 (no checkpoint download)",
+                config=workload_config(world),
+                cpu_baseline=dict(value=round(value, 3), unit="GB/s", cores=threads, kind=kind, sample=sample,
+                                  cpu_model=cpu_model(), bytes_match=bool(match)),
                 e2e=dict(value=round(value, 3), unit="GB/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
@@ -505,14 +598,8 @@ def config4_specs(world, rank, dev, sigma=0.015, seed=3):
     return out
 
 
-def run_config4_decode(args):
-    """`--case config4-decode`: whole-model decode of the Llama-3-70B-shaped
-    model, `dfloat11-parallel`, row-sharded over the
-    ranks.  The rank's compressed shard (~94 GB / N) is resident; a step
-    decodes every slab once, layer by layer (one plan per layer), into an
-    output buffer reused by every layer (compressed + decoded = 235 GB does
-    not fit one GPU).  Before timing, every decoded tensor is compared bit for
-    bit with its source regenerated from the seed."""
+def _case_setup():
+    """Device, NCCL group (N > 1) and stream of a `--case` run."""
     import torch
     import xksv_gpu
     world, rank, local = _dist_env()
@@ -523,7 +610,30 @@ def run_config4_decode(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device(dev))
     xksv_gpu.load()
-    stream = torch.cuda.Stream(device=dev)
+    return world, rank, dev, torch.cuda.Stream(device=dev)
+
+
+def run_config4_decode(args):
+    """`--case config4-decode`: prints config4_decode()'s line."""
+    world, rank, dev, stream = _case_setup()
+    line = config4_decode(args, dev, stream, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def config4_decode(args, dev, stream, world, rank):
+    """Whole-model decode of the Llama-3-70B-shaped model (BASELINE
+    configs[3]), `dfloat11-parallel`, row-sharded over the ranks (strong
+    scaling: the model is fixed).  The rank's compressed shard (~97 GB / N) is
+    resident; a step decodes every slab once, in plans of ~6 GB of output
+    each, into an output buffer the plans reuse (compressed + decoded = 238 GB
+    does not fit one GPU).  Before timing, every decoded tensor is compared
+    bit for bit with its source regenerated from the seed."""
+    import torch
+    import xksv_gpu
     h = stream.cuda_stream
     t0 = time.perf_counter()
     specs = config4_specs(world, rank, dev)
@@ -592,7 +702,8 @@ def run_config4_decode(args):
     ms = t / args.steps * 1e3
     peak, peak_src = measured_peak()
     line = dict(case="config4-decode", config="configs[3] Llama-3-70B shapes, N(0,0.015) seed 3, dfloat11-parallel, "
-                "rows sharded in whole slabs", n_gpus=world, steps=args.steps, ms_per_step=round(ms, 3),
+                "rows sharded in whole slabs", scaling="strong", n_gpus=world, steps=args.steps,
+                ms_per_step=round(ms, 3),
                 per_rank_out_bytes=raw, per_rank_compressed_bytes=comp,
                 value=round(world * raw / (ms / 1e3) / 1e9, 1), unit="GB/s BF16 out (all ranks)",
                 per_gpu_out_gbs=round(raw / (ms / 1e3) / 1e9, 1),
@@ -601,12 +712,11 @@ def run_config4_decode(args):
                 launches_per_step=sum(pl.launches() for pl in plans), plans=len(plans),
                 bit_exact_tensors=len(check), status_errors=bad, build_s=round(build_s, 1),
                 note="output buffer reused per plan of ~6 GB output; inputs larger than L2")
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     for pl in plans:
         pl.close()
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    del payload, out
+    torch.cuda.empty_cache()
+    return line
 
 
 def run_config4_gemv(args):
@@ -712,23 +822,25 @@ def run_config4_gemv(args):
 
 
 def run_config5(args):
-    """`--case config5`: the adversarial exponent mix of BASELINE configs[4]:
-    64 tensors of 8192x8192 BF16 from seed 4 -- 32 Student-t(3) x 0.02, 16
-    N(0, 1e-4), 16 uniform 16-bit patterns (raw-fallback slabs) -- encoded on
-    the GPU in both codecs and decoded whole (one plan per codec), bit-exact
-    against the source; tensors split over the ranks (tensor i on rank
-    i % N)."""
+    """`--case config5`: prints config5()'s line."""
+    world, rank, dev, stream = _case_setup()
+    line = config5(args, dev, stream, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def config5(args, dev, stream, world, rank):
+    """The adversarial exponent mix of BASELINE configs[4]: 64 tensors of
+    8192x8192 BF16 from seed 4 -- 32 Student-t(3) x 0.02, 16 N(0, 1e-4), 16
+    uniform 16-bit patterns (raw-fallback slabs) -- encoded on the GPU in both
+    codecs and decoded whole (one plan per codec), bit-exact against the
+    source; tensors split over the ranks (tensor i on rank i % N: strong
+    scaling)."""
     import torch
     import xksv_gpu
-    world, rank, local = _dist_env()
-    torch.cuda.set_device(local)
-    dev = f"cuda:{local}"
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device(dev))
-    xksv_gpu.load()
-    stream = torch.cuda.Stream(device=dev)
     h = stream.cuda_stream
     n = 8192
     torch.manual_seed(4)
@@ -793,12 +905,11 @@ def run_config5(args):
         del payload, out
         torch.cuda.empty_cache()
     line = dict(case="config5", config="configs[4] 64 x 8192x8192 BF16, seed 4: 32 Student-t(3)*0.02, "
-                "16 N(0,1e-4), 16 uniform 16-bit", n_gpus=world, per_rank_out_bytes=raw_bytes,
-                unit="GB/s BF16 out (all ranks)", **results)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+                "16 N(0,1e-4), 16 uniform 16-bit", scaling="strong", n_gpus=world, steps=args.steps,
+                per_rank_out_bytes=raw_bytes, unit="GB/s BF16 out (all ranks)", **results)
+    del srcs
+    torch.cuda.empty_cache()
+    return line
 
 
 def run_runtime(args):
@@ -1026,10 +1137,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU baseline leg: seconds of reference decode (half on 1 thread, half on all)")
     ap.add_argument("--warmup-cpu", type=int, default=0)
     ap.add_argument("--gemv-steps", type=int, default=20)
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[3] and configs[4] keys")
     ap.add_argument("--batch", type=int, default=1, help="batch columns of X in gemv- cases")
     ap.add_argument("--case", default=None,
                     help="CODEC:ROWSxCOLS:SLABS small decode workload (profiling), e.g. parallel:16x2048:2048; "
@@ -1225,10 +1338,28 @@ def main():
         except Exception as ex:  # reported, never silently replaced
             gemv = dict(error=f"{type(ex).__name__}: {ex}")
 
+    # the other BASELINE configs measured in the same run (their own roofline
+    # and bit-exact checks): configs[3] whole-model decode, configs[4] mix
+    del d_payload, h_payload
+    if "d_out" in locals():
+        del d_out
+    torch.cuda.empty_cache()
+    c4 = c5 = None
+    if not args.no_configs:
+        try:
+            c4 = config4_decode(args, dev, stream, world, rank)
+        except Exception as ex:  # reported, never silently replaced
+            c4 = dict(error=f"{type(ex).__name__}: {ex}")
+        torch.cuda.empty_cache()
+        try:
+            c5 = config5(args, dev, stream, world, rank)
+        except Exception as ex:  # reported, never silently replaced
+            c5 = dict(error=f"{type(ex).__name__}: {ex}")
+        torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1:
-        v, kind, cores, sample = cpu_reference_decode(payload, slabs, args.cpu_seconds, host_threads(1))
-        cpu = dict(value=round(v, 3), unit="GB/s", cores=cores, kind=kind, sample=sample)
+        cpu = cpu_baseline(args.cpu_seconds)
 
     clocks = clk.summary()
     if world > 1:
@@ -1245,11 +1376,10 @@ def main():
             warmup=args.warmup, ms_per_step=round(t / args.steps * 1e3, 4), higher_is_better=True,
             scaling="weak", vs_baseline=None, dtype="bf16",
             data="synthetic: seeded BF16 N(0,0.02) Llama-1.1B-shaped weights, norms 1.0 (no checkpoint download)",
-            config=dict(workload="configs[1]: Llama-1.1B-shaped checkpoint (h2048, 22L, 32/4 heads, FFN 5632, vocab 32000, untied), dfloat11-parallel, whole-checkpoint decode per GPU",
-                        codec="bf16-huffman-parallel32", slabs=len(slabs), parallel_slabs=n_par,
-                        raw_slabs=n_raw, compressed_bytes=comp_bytes, out_bytes=out_bytes,
-                        l2="inputs (%.2f GB) larger than L2 (126 MB); no flush" % ((comp_bytes + out_bytes) / 1e9),
-                        parallelism=f"slab partition, {world} independent GPU(s), no collective"),
+            config=workload_config(world),
+            archive=dict(slabs=len(slabs), parallel_slabs=n_par, raw_slabs=n_raw, compressed_bytes=comp_bytes,
+                         out_bytes=out_bytes, encoder="host (xksv_host_pack_tensor, byte-identical to the "
+                                                      "reference encoder)"),
             roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s",
                           frac=round(achieved / peak, 4), traffic=traffic,
                           kernel="parallel_slab_kernel<0> (decode)", peak_source=peak_src,
@@ -1261,7 +1391,7 @@ def main():
                      path="pinned host payload -> xksv_plan_decode_host (8 copy pieces overlapped with "
                           "their slabs' decode) -> xksv_plan_status"),
             clocks=clocks, gpu_launches=launches, sha256_verify=sha, gpu_encoder=enc, fused_gemv=gemv,
-            tp_fused_gemv=tp)
+            tp_fused_gemv=tp, config4_decode=c4, config5=c5)
         print(json.dumps(line), flush=True)
     plan.close()
     par_plan.close()

@@ -8,11 +8,11 @@
 // 32 independently coded substreams are a warp's worth of independent work);
 // many slabs in flight per SM.  Every per-lane step of the inner loop runs at
 // a cadence shared by all lanes, so the warp never serialises on one lane:
-//   * each lane builds its own canonical tables: a 2^PK-entry first level of
-//     32-bit entries for codes of length <= PK, a 16-bit second level for
-//     lengths PK+1..PK+K2 under the first NE escape prefixes, and a compact
-//     list for lengths up to PK+PNL.  Tables are lane-minor ([entry][lane]):
-//     a first-level lookup touches only the lane's own bank;
+//   * each lane builds its own canonical tables: a 2^PK-entry first level for
+//     codes of length <= PK, a second level for lengths PK+1..PK+K2 under the
+//     first NE escape prefixes (12-bit codes: the long tails of large slabs
+//     and heavy-tailed weights stay on the fast path), and a compact list for
+//     lengths up to PK+PNL.  Tables are lane-minor ([entry][lane]);
 //   * a lane's exponent bits live in a 16-word ring in shared memory laid out
 //     [word][lane], so every lane reads only its own bank.  Words arrive as
 //     aligned 32-byte global loads (sm_100 256-bit loads: a warp-wide load of
@@ -26,7 +26,8 @@
 //     every code of the block was read from real bits and found in the
 //     tables (an entry of 0 consumes no bits, so an unresolved code zeroes
 //     the block's last entry); otherwise the block is redone code by code;
-//   * sign/mantissa bytes arrive 16 at a time through a shared cp.async ring;
+//   * sign/mantissa bytes arrive 16 at a time through a shared cp.async ring
+//     (asynchronous copies: nothing waits on a register load);
 //   * 16 decoded BF16 words (one tile row) leave as one 32-byte store (two
 //     16-byte stores when the output is only 16-byte aligned), un-tiled on the
 //     fly, for 16-row slabs with cols % 16 == 0; other shapes use an
@@ -47,11 +48,11 @@ namespace xksv {
 namespace {
 
 constexpr int PK = 6;       // first-level table bits
-constexpr int K2 = 4;       // second level covers lengths PK+1 .. PK+K2
+constexpr int K2 = 5;       // second level covers lengths PK+1 .. PK+K2
 constexpr int NE = 2;       // escape prefixes with a second-level table
 constexpr int NROW2 = (NE << K2) + 1;  // second-level rows (the last is all zero)
 constexpr int PNL = 16;     // long lengths held per lane: PK+1 .. PK+PNL
-constexpr int PLONG = 32;   // long symbols held per lane
+constexpr int PLONG = 16;   // long symbols held per lane
 constexpr int BR = 16;      // bit-ring words per lane (power of two)
 constexpr uint32_t kRingLow = 8;  // unread ring words kept at each 16-code group
 constexpr int kSaveChunk = 4;     // first ring row holding length chunks saved by the table build
@@ -59,11 +60,10 @@ constexpr int SMR = 4;      // 16-byte sign/mantissa slots per lane
 constexpr int PWARPS = 2;   // slabs (warps) per CTA: small CTAs free their tables sooner
 constexpr int PMAXB = 8;    // GEMM columns per pass
 
-// One warp's tables, lane-minor so that lane l always touches bank l (32-bit
-// first level, bit ring) or bank l/2 (16-bit second level, mostly its shared
-// all-zero row).
+// One warp's tables, lane-minor so that lane l always touches bank l/2
+// (16-bit tables) or bank l (the bit ring).
 struct WarpTabs {
-  uint32_t lut[1 << PK][32];     // exponent << 7 | length; 0 = no code of length <= PK
+  uint16_t lut[1 << PK][32];     // exponent << 7 | length; 0 = no code of length <= PK
   uint16_t lut2[NROW2][32];      // second level: (PK+K2)-bit prefix - (L << K2); last row 0
   uint8_t cnt[PNL][32];          // number of codes of length PK+1+j (<= PLONG)
   uint8_t lsym[PLONG][32];       // long-code symbols, canonical (length, symbol) order
@@ -213,7 +213,7 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
           const uint32_t st = ((lo ? s14 : s56) >> fs) & 255u;
           s14 += lo ? run << fs : 0u;
           s56 += lo ? 0u : run << fs;
-          const uint32_t e = (sym << 7) | l;
+          const uint16_t e = uint16_t((sym << 7) | l);
           for (uint32_t r = 0; r < run; ++r) W.lut[st + r][lane] = e;
         } else {
           const int j = int(l) - PK - 1;
@@ -225,9 +225,8 @@ __device__ int build_lane_tables(const uint8_t* lens, WarpTabs& W, int lane, uin
   }
   // rows past the short codes: prefixes of long codes or unused code space
   for (uint32_t z = L; z < (1u << PK); ++z) W.lut[z][lane] = 0;
-  // second level: codes of length PK+1..PK+K2 whose (PK+K2)-bit prefixes fall
-  // in the first NE escape prefixes
-  for (int z = 0; z < NROW2; ++z) W.lut2[z][lane] = 0;
+  // second level (zeroed by the whole warp before the build): codes of length
+  // PK+1..PK+K2 whose (PK+K2)-bit prefixes fall in the first NE escape prefixes
   uint32_t cf = F, idx = 0;
   const uint32_t base = L << K2;
   for (int l = PK + 1; l <= maxlen && l <= PK + K2; ++l) {
@@ -305,15 +304,19 @@ struct LaneStream {
     c0 = fetch();
     stage = fetch();
   }
+  // fw is always a multiple of 8 (chunks of 8 words from word 0), so a chunk
+  // fills ring rows (fw % BR) .. +7 from one base address.
   __device__ __forceinline__ void put(WarpTabs& W, int lane, const Chunk32& c) {
-    W.ring[(fw + 0) & (BR - 1)][lane] = bswap32(c.a.x);
-    W.ring[(fw + 1) & (BR - 1)][lane] = bswap32(c.a.y);
-    W.ring[(fw + 2) & (BR - 1)][lane] = bswap32(c.a.z);
-    W.ring[(fw + 3) & (BR - 1)][lane] = bswap32(c.a.w);
-    W.ring[(fw + 4) & (BR - 1)][lane] = bswap32(c.b.x);
-    W.ring[(fw + 5) & (BR - 1)][lane] = bswap32(c.b.y);
-    W.ring[(fw + 6) & (BR - 1)][lane] = bswap32(c.b.z);
-    W.ring[(fw + 7) & (BR - 1)][lane] = bswap32(c.b.w);
+    static_assert(BR == 16, "a chunk fills one half of the ring");
+    uint32_t* r = &W.ring[fw & 8][lane];
+    r[0 * 32] = bswap32(c.a.x);
+    r[1 * 32] = bswap32(c.a.y);
+    r[2 * 32] = bswap32(c.a.z);
+    r[3 * 32] = bswap32(c.a.w);
+    r[4 * 32] = bswap32(c.b.x);
+    r[5 * 32] = bswap32(c.b.y);
+    r[6 * 32] = bswap32(c.b.z);
+    r[7 * 32] = bswap32(c.b.w);
     fw += 8;
   }
   __device__ __forceinline__ void init_ring(WarpTabs& W, int lane) {
@@ -468,7 +471,8 @@ __device__ __forceinline__ void emit_one(const Out& o, uint32_t p, uint32_t word
 // Decodes one substream.  `rows16`: 16-row slab, cols % 16 == 0, the
 // substream starts on a tile row and (decode) the output is 16-byte aligned;
 // whole tile rows then leave as 32-byte stores.  The caller has started `b`
-// and `smr` and put the first words into the ring.
+// and `smr` (sign/mantissa bytes, 16 per group) and put the first words into
+// the ring.
 template <int MODE>
 __device__ void decode_segment(const Seg& s, WarpTabs& W, int lane, const LaneCode& lc, bool rows16,
                                LaneStream& b, LaneSm& smr, const Out& o, bool& bad) {
@@ -595,7 +599,7 @@ __device__ __forceinline__ uint64_t warp_incl_scan(uint64_t v, int lane) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 7 : 1)
+__global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 8 : 1)
     parallel_slab_kernel(const Slab* __restrict__ slabs, uint32_t nslabs,
                          const uint8_t* __restrict__ payload, uint8_t* __restrict__ out,
                          const float* __restrict__ x, float* __restrict__ y, uint32_t ld,
@@ -705,6 +709,13 @@ __global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 7 : 1)
     }
     cp_async_commit();
     // ---- per-lane tables ----
+    // the second-level table starts all zero: 16-byte stores by the warp
+    {
+      static_assert(sizeof(WarpTabs::lut2) % 16 == 0 && offsetof(WarpTabs, lut2) % 16 == 0, "lut2 as uint4");
+      uint4* z = reinterpret_cast<uint4*>(&W.lut2[0][0]);
+      for (uint32_t k = lane; k < sizeof(WarpTabs::lut2) / 16; k += 32) z[k] = make_uint4(0, 0, 0, 0);
+      __syncwarp();
+    }
     LaneCode lc{0, 0, 0};
     uint32_t L = 0;
     const int tb = active ? build_lane_tables(s.lens, W, lane, lc.F, lc.maxlen, L) : 0;
