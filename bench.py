@@ -390,13 +390,13 @@ def fused_gemv(args, dev, stream, threads):
     # one-time tile index of the resident weights (xksv_plan_index)
     t_idx = time.perf_counter()
     for pl in plans:
-        if pl.index(d_payload.data_ptr(), h):
+        if pl.index(d_payload, h):
             raise RuntimeError("xksv_plan_index failed")
     index_s = time.perf_counter() - t_idx
 
     def forward():
         for pl in plans:
-            pl.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 1, h)
+            pl.gemm(d_payload, x, y, 1, h)
 
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -420,7 +420,7 @@ def fused_gemv(args, dev, stream, threads):
     t0 = name_to["model.layers.0.mlp.down_proj.weight"]
     dplan = xksv_gpu.Plan(slabs[t0["first"]:t0["first"] + t0["n"]])
     wdec = torch.empty(t0["rows"] * t0["cols"] * 2 + t0["dst"], dtype=torch.uint8, device=dev)
-    dplan.decode(d_payload.data_ptr(), wdec.data_ptr(), h)
+    dplan.decode(d_payload, wdec, h)
     bad += dplan.status(h)
     W = wdec[t0["dst"]:].view(torch.bfloat16).view(t0["rows"], t0["cols"]).float()
     # down_proj is the 4th group of layer 0: its x and y offsets
@@ -483,14 +483,14 @@ def run_case(args):
         nb = args.batch
         x = torch.randn(cols, nb, device=dev)
         y = torch.empty(nslabs * rows, nb, device=dev)
-        if plan.index(d_payload.data_ptr(), h):
+        if plan.index(d_payload, h):
             raise RuntimeError("xksv_plan_index failed")
-        fn = lambda: plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), nb, h)
+        fn = lambda: plan.gemm(d_payload, x, y, nb, h)
     else:
         d_out = torch.empty(out, dtype=torch.uint8, device=dev)
-        if indexed and plan.index(d_payload.data_ptr(), h):
+        if indexed and plan.index(d_payload, h):
             raise RuntimeError("xksv_plan_index failed")
-        fn = lambda: plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+        fn = lambda: plan.decode(d_payload, d_out, h)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             fn()
@@ -670,7 +670,7 @@ def config4_decode(args, dev, stream, world, rank):
 
     def step():
         for pl in plans:
-            pl.decode(payload.data_ptr(), out.data_ptr(), h)
+            pl.decode(payload, out, h)
 
     # bit-exact check of every tensor against its regenerated source
     check = config4_specs(world, rank, dev)
@@ -678,7 +678,7 @@ def config4_decode(args, dev, stream, world, rank):
     mismatches = 0
     with torch.cuda.stream(stream):
         for pl, span in zip(plans, spans):
-            pl.decode(payload.data_ptr(), out.data_ptr(), h)
+            pl.decode(payload, out, h)
             if pl.status(h):
                 raise RuntimeError("decode reported a slab error")
             for name, off, n in span:
@@ -759,7 +759,7 @@ def run_config4_gemv(args):
             plans.append(xksv_gpu.Plan(entries))
     t_idx = time.perf_counter()
     for pl in plans:
-        if pl.index(payload.data_ptr(), h):
+        if pl.index(payload, h):
             raise RuntimeError("xksv_plan_index failed")
     index_s = time.perf_counter() - t_idx
     # batch >= 4 runs on the tensor cores after decoding each plan's weights
@@ -779,7 +779,7 @@ def run_config4_gemv(args):
 
         def forward():
             for pl in plans:
-                pl.gemm(payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch, h)
+                pl.gemm(payload, x, y, batch, h)
         with torch.cuda.stream(stream):
             forward()  # first call: the tensor-core path allocates its X^T buffers
         assert all(pl.status(h) == 0 for pl in plans)
@@ -798,7 +798,7 @@ def run_config4_gemv(args):
         td = by[members[0]]
         dplan = xksv_gpu.Plan(td["slabs"])
         w = torch.empty(td["rows"] * td["cols"] * 2, dtype=torch.uint8, device=dev)
-        dplan.decode(payload.data_ptr(), w.data_ptr(), h)
+        dplan.decode(payload, w, h)
         assert dplan.status(h) == 0
         dplan.close()
         W = w.view(torch.bfloat16).view(td["rows"], td["cols"]).float()
@@ -878,18 +878,18 @@ def config5(args, dev, stream, world, rank):
         plan = xksv_gpu.Plan(entries)
         out = torch.empty(base, dtype=torch.uint8, device=dev)
         with torch.cuda.stream(stream):
-            plan.decode(payload.data_ptr(), out.data_ptr(), h)
+            plan.decode(payload, out, h)
         if plan.status(h):
             raise RuntimeError("decode reported a slab error")
         exact = all(torch.equal(out[k * n * n * 2:(k + 1) * n * n * 2].view(torch.int16),
                                 s.view(torch.int16).reshape(-1)) for k, s in enumerate(srcs))
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
-                plan.decode(payload.data_ptr(), out.data_ptr(), h)
+                plan.decode(payload, out, h)
             stream.synchronize()
             if world > 1:
                 torch.distributed.barrier()
-            t = time_steps(lambda: plan.decode(payload.data_ptr(), out.data_ptr(), h), args.steps, stream)
+            t = time_steps(lambda: plan.decode(payload, out, h), args.steps, stream)
         t = _max_over_ranks(t, world, dev)
         ms = t / args.steps * 1e3
         kinds = {}
@@ -1058,7 +1058,7 @@ def tp_gemv(args, dev, stream, threads, rank, world):
                     entries.append(e)
                 yl += t["rows"]
             plan = xksv_gpu.Plan(entries)
-            if plan.index(d_payload.data_ptr(), stream.cuda_stream):
+            if plan.index(d_payload, stream.cuda_stream):
                 raise RuntimeError("xksv_plan_index failed")
             groups.append(dict(plan=plan, rows=yl, y=torch.empty(yl, device=dev),
                                yfull=torch.empty(world * yl, device=dev)))
@@ -1068,7 +1068,7 @@ def tp_gemv(args, dev, stream, threads, rank, world):
 
     def forward():
         for g in groups:
-            comm.gemm(g["plan"], d_payload.data_ptr(), x.data_ptr(), g["y"].data_ptr(), g["rows"],
+            comm.gemm(g["plan"], d_payload, x, g["y"].data_ptr(), g["rows"],
                       g["yfull"].data_ptr(), 1, h)
 
     with torch.cuda.stream(stream):
@@ -1095,7 +1095,7 @@ def tp_gemv(args, dev, stream, threads, rank, world):
 
     def forward_fused():
         for g in groups:
-            g["fused_y"] = fused.gemm(g["plan"], d_payload.data_ptr(), x.data_ptr(), g["rows"], 1, h)
+            g["fused_y"] = fused.gemm(g["plan"], d_payload, x, g["rows"], 1, h)
 
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -1112,7 +1112,7 @@ def tp_gemv(args, dev, stream, threads, rank, world):
     ms_f = float(tt.item()) / args.gemv_steps * 1e3
     # same gathered rows as the NCCL path (last group, this rank's block)
     chk = torch.empty(world * g0["rows"], device=dev)
-    fused.gemm(g0["plan"], d_payload.data_ptr(), x.data_ptr(), g0["rows"], 1, h, chk.data_ptr())
+    fused.gemm(g0["plan"], d_payload, x, g0["rows"], 1, h, chk)
     stream.synchronize()
     fused_match = bool(torch.allclose(chk, g0["yfull"], rtol=1e-5, atol=1e-6))
     torch.cuda.synchronize()
@@ -1194,7 +1194,7 @@ def main():
     h = stream.cuda_stream
 
     def step():
-        plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
+        plan.decode(d_payload, d_out, h)
 
     # correctness of the decoded checkpoint: every slab's bytes against the
     # BF16 source regenerated with the same seed
@@ -1235,8 +1235,8 @@ def main():
     # dominant kernel alone (the parallel-codec decode), for the roofline
     with torch.cuda.stream(stream):
         for _ in range(3):
-            par_plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
-    tk = time_steps(lambda: par_plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h), args.steps, stream)
+            par_plan.decode(d_payload, d_out, h)
+    tk = time_steps(lambda: par_plan.decode(d_payload, d_out, h), args.steps, stream)
     assert par_plan.status(h) == 0
     kdur = tk / args.steps
     peak, peak_src = measured_peak()
@@ -1255,9 +1255,9 @@ def main():
     import hashlib
     d_dig = torch.zeros(32 * len(slabs), dtype=torch.uint8, device=dev)
     with torch.cuda.stream(stream):
-        plan.decode(d_payload.data_ptr(), d_out.data_ptr(), h)
-        plan.sha256(d_out.data_ptr(), d_dig.data_ptr(), h)
-        ts = time_steps(lambda: plan.sha256(d_out.data_ptr(), d_dig.data_ptr(), h), 3, stream)
+        plan.decode(d_payload, d_out, h)
+        plan.sha256(d_out, d_dig, h)
+        ts = time_steps(lambda: plan.sha256(d_out, d_dig, h), 3, stream)
     assert plan.status(h) == 0
     dig = d_dig.cpu().numpy().tobytes()
     sha_ok = True
@@ -1286,7 +1286,7 @@ def main():
         hp, hs = xksv_gpu.host_pack_tensor(hw.ctypes.data, hw.nbytes, er, ec, 2, threads=threads)
         dpay = torch.empty(nbytes_e, dtype=torch.uint8, device=dev)
         cp = xksv_gpu.Plan([dict(src_offset=0, src_size=nbytes_e, rows=1, cols=1, dst_offset=0, codec=0)])
-        cp.decode(dptr, dpay.data_ptr(), h)
+        cp.decode(dptr, dpay, h, payload_bytes=nbytes_e)
         same = cp.status(h) == 0 and sl_e == hs and bool(np.array_equal(dpay.cpu().numpy(), hp))
         cp.close()
         xksv_gpu.free_device(dptr)
@@ -1306,7 +1306,7 @@ def main():
     def e2e_step():
         # xksv_plan_decode_host: the payload crosses PCIe in pieces while the
         # slabs of the pieces already landed decode
-        plan.decode_host(h_payload.data_ptr(), payload.nbytes, d_payload.data_ptr(), d_out.data_ptr(), h)
+        plan.decode_host(h_payload.data_ptr(), payload.nbytes, d_payload, d_out, h)
         if plan.status(h):
             raise RuntimeError("decode error")
 

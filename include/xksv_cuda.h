@@ -80,16 +80,24 @@ typedef struct xksv_slab {
 typedef struct xksv_plan xksv_plan;
 
 /* Validates the host table, copies it to the current device and groups it by
- * codec.  Returns 0 and a plan, or 1. */
+ * codec.  Returns 0 and a plan, or 1.  The plan records the extents its
+ * table needs: payload bytes (largest src_offset + src_size), decoded bytes
+ * (largest dst_offset + rows * cols * 2, or + src_size for raw blocks), X rows
+ * (largest x_offset + cols) and Y rows (largest dst_offset + rows).  Every call
+ * below is given the size of each device buffer it reads or writes and
+ * returns 1 without launching anything when a slab lies outside one: a bad
+ * table entry never reaches a kernel as an out-of-bounds access. */
 int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** plan);
 void xksv_plan_destroy(xksv_plan* plan);
 
-/* Enqueues decode of every slab of the plan from d_payload (device) into
- * d_out (device) on `stream` (a cudaStream_t; NULL = legacy default stream).
- * Returns 1 for launch errors and, without launching, when d_out or a coded
- * slab's dst_offset is odd (BF16 words need 2-byte alignment); stream errors
- * are found by xksv_plan_status(). */
-int xksv_plan_decode(const xksv_plan* plan, const void* d_payload, void* d_out, void* stream);
+/* Enqueues decode of every slab of the plan from d_payload (device,
+ * payload_size bytes) into d_out (device, out_size bytes) on `stream` (a
+ * cudaStream_t; NULL = legacy default stream).  Returns 1 for launch errors
+ * and, without launching, when a slab lies outside either buffer or when
+ * d_out or a coded slab's dst_offset is odd (BF16 words need 2-byte
+ * alignment); stream errors are found by xksv_plan_status(). */
+int xksv_plan_decode(const xksv_plan* plan, const void* d_payload, size_t payload_size, void* d_out,
+                     size_t out_size, void* stream);
 
 /* The same decode from a HOST payload (pinned memory for overlap): the first
  * payload_size bytes at h_payload are copied into d_payload (device, at least
@@ -98,17 +106,18 @@ int xksv_plan_decode(const xksv_plan* plan, const void* d_payload, void* d_out, 
  * overlap.  The copies wait for work already enqueued on `stream`.  Needs
  * each codec's slabs in increasing payload order (an archive's block order;
  * otherwise, and for a plan indexed on d_payload, it copies once and then
- * decodes).  Returns 1 as xksv_plan_decode does, and when a slab lies past
- * payload_size.  No reference counterpart (the reference stages one slab per
- * blocking call, cuda/decode.cu:47-83). */
+ * decodes).  Returns 1 as xksv_plan_decode does (a slab past payload_size or
+ * past out_size included).  No reference counterpart (the reference stages
+ * one slab per blocking call, cuda/decode.cu:47-83). */
 int xksv_plan_decode_host(const xksv_plan* plan, const void* h_payload, size_t payload_size,
-                          void* d_payload, void* d_out, void* stream);
+                          void* d_payload, void* d_out, size_t out_size, void* stream);
 
 /* Enqueues Y[dst_offset + r, b] = sum_c W[r, c] * X[x_offset + c, b] for every
- * slab, X FP32 row-major [*, batch] and Y FP32 row-major [*, batch] (rows of
- * Y not covered by a slab are left untouched). */
-int xksv_plan_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y,
-                   size_t batch, void* stream);
+ * slab, X FP32 row-major [x_rows, batch] and Y FP32 row-major [y_rows, batch]
+ * (rows of Y not covered by a slab are left untouched).  Returns 1 without
+ * launching when a slab lies outside the payload, X or Y. */
+int xksv_plan_gemm(const xksv_plan* plan, const void* d_payload, size_t payload_size, const float* d_x,
+                   size_t x_rows, float* d_y, size_t y_rows, size_t batch, void* stream);
 
 /* The tensor-core path (batch >= 4) decodes the plan's weights into a BF16
  * scratch before its GEMM; by default each plan allocates its own on first
@@ -142,7 +151,7 @@ int xksv_plan_launches(const xksv_plan* plan);
  * the side, the slab format is unchanged.  Synchronises `stream`; 0 on
  * success, 1 on a bad slab or CUDA error (no index is kept then).  Calls on
  * one plan must not overlap. */
-int xksv_plan_index(xksv_plan* plan, const void* d_payload, void* stream);
+int xksv_plan_index(xksv_plan* plan, const void* d_payload, size_t payload_size, void* stream);
 
 
 /* ---------------- Part 3: archive-side encoder (host CPU) --------------- */
@@ -187,17 +196,21 @@ void xksv_cuda_free(void* d_ptr);
  * device-wide synchronisation.  Decodes the n slabs of `slabs` (host array,
  * same fields as for xksv_plan_create) from d_payload into d_out (both device
  * buffers owned by the caller) on `stream`, then waits for the stream and
- * returns 0 on success, 1 on a bad table entry, a launch error or a slab that
- * fails to decode, and 2 when n exceeds XKSV_NOALLOC_MAX_SLABS.
+ * returns 0 on success, 1 on a bad table entry (a slab outside the
+ * payload_size bytes at d_payload or the out_size bytes at d_out included,
+ * found before any launch), a launch error or a slab that fails to decode,
+ * and 2 when n exceeds XKSV_NOALLOC_MAX_SLABS.
  * Besides the caller's buffers it uses only a fixed scratch array compiled
  * into the library (the slab table and a status word, about 192 KiB on every
  * GPU that loads the library, kept until the process exits).  The first call
- * on a device looks that array up (cudaGetSymbolAddress): make it before any
- * stream capture.  All calls share the array: calls that overlap on the GPU
- * race, so issue them one at a time. */
+ * on a device looks that array up (cudaGetSymbolAddress) and keeps its
+ * address: make it before any stream capture, and make no call on a device
+ * after a cudaDeviceReset of it (the address is stale then).  All calls
+ * share the array: calls that overlap on the GPU race, so issue them one at
+ * a time. */
 #define XKSV_NOALLOC_MAX_SLABS 4096
-int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload,
-                             void* d_out, void* stream);
+int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload, size_t payload_size,
+                             void* d_out, size_t out_size, void* stream);
 
 /* Fused variant: no separate collective.  The indexed GEMV kernel writes its
  * output rows into this rank's block of its own gathered buffer; the grid's
@@ -220,13 +233,16 @@ int xksv_tp_fused_create(int nranks, int rank, size_t max_rows_shard, size_t max
 int xksv_tp_fused_open(xksv_tp_fused* ctx, const void* handles);
 /* Enqueues the fused GEMV/GEMM (batch <= max_batch) of this rank's plan,
  * which must hold only 16-row serial-codec slabs with a tile index for
- * d_payload (xksv_plan_index).  The gathered Y [nranks * rows_shard, batch]
- * (rank order) is copied to d_y_full when it is not NULL, and its address in
- * the context's buffers is stored to *d_gathered when that is not NULL.
+ * d_payload (xksv_plan_index) and write no row at or past rows_shard.  X is
+ * FP32 [x_rows, batch].  The gathered Y [nranks * rows_shard, batch] (rank
+ * order) is copied to d_y_full when it is not NULL, and its address in the
+ * context's buffers is stored to *d_gathered when that is not NULL.
  * Collective: every rank makes the same calls in the same order.  1 for bad
- * arguments or launch errors. */
-int xksv_tp_fused_gemm(xksv_tp_fused* ctx, const xksv_plan* plan, const void* d_payload, const float* d_x,
-                       size_t rows_shard, size_t batch, float* d_y_full, float** d_gathered, void* stream);
+ * arguments (a slab outside the payload, X or the rank's rows included) or
+ * launch errors. */
+int xksv_tp_fused_gemm(xksv_tp_fused* ctx, const xksv_plan* plan, const void* d_payload, size_t payload_size,
+                       const float* d_x, size_t x_rows, size_t rows_shard, size_t batch, float* d_y_full,
+                       float** d_gathered, void* stream);
 void xksv_tp_fused_destroy(xksv_tp_fused* ctx);
 
 /* ---------------- Part 6: SHA-256 of decoded bytes on the GPU ----------- */
@@ -243,9 +259,9 @@ void xksv_tp_fused_destroy(xksv_tp_fused* ctx);
 int xksv_cuda_sha256(const uint64_t* ranges, size_t n, const void* d_base, void* d_digests, void* stream);
 
 /* Digest i (slab order of xksv_plan_create) = SHA-256 of slab i's decoded
- * bytes in d_out: [dst_offset, dst_offset + rows * cols * 2), or src_size
- * bytes for a raw slab. */
-int xksv_plan_sha256(const xksv_plan* plan, const void* d_out, void* d_digests, void* stream);
+ * bytes in d_out (out_size bytes): [dst_offset, dst_offset + rows * cols * 2),
+ * or src_size bytes for a raw slab. */
+int xksv_plan_sha256(const xksv_plan* plan, const void* d_out, size_t out_size, void* d_digests, void* stream);
 
 /* ---------------- Part 5: tensor-parallel fused GEMV / GEMM ------------- */
 /* One process per GPU; each rank's plan holds the slabs of its own rows
@@ -265,12 +281,14 @@ int xksv_tp_comm_create(const void* id, int nranks, int rank, void** comm);
 void xksv_tp_comm_destroy(void* comm);
 
 /* Enqueues on `stream`: d_y_shard[rows_shard, batch] = W_shard X (the fused
- * plan GEMM), then one all-gather of every rank's shard into
- * d_y_full[nranks * rows_shard, batch] (rank order = row order; all ranks
- * pass the same rows_shard).  Returns 1 only for launch errors; slab errors
- * are read with xksv_plan_status. */
-int xksv_tp_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y_shard,
-                 size_t rows_shard, float* d_y_full, size_t batch, void* comm, void* stream);
+ * plan GEMM, X FP32 [x_rows, batch]), then one all-gather of every rank's
+ * shard into d_y_full[nranks * rows_shard, batch] (rank order = row order;
+ * all ranks pass the same rows_shard).  Returns 1 for launch errors and,
+ * without launching, for a slab outside the payload, X or the shard's rows;
+ * slab errors are read with xksv_plan_status. */
+int xksv_tp_gemm(const xksv_plan* plan, const void* d_payload, size_t payload_size, const float* d_x,
+                 size_t x_rows, float* d_y_shard, size_t rows_shard, float* d_y_full, size_t batch, void* comm,
+                 void* stream);
 
 #ifdef __cplusplus
 }

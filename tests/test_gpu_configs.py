@@ -55,18 +55,18 @@ def test_config4_slabs(xg, codec):
     d_payload = torch.from_numpy(payload).cuda()
     out = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     plan = xg.Plan(dec)
-    plan.decode(d_payload.data_ptr(), out.data_ptr())
+    plan.decode(d_payload, out)
     assert plan.status() == 0
     assert out.cpu().numpy().tobytes() == b"".join(m.tobytes() for m in mats)
     plan.close()
     gp = xg.Plan(gemv)
     if codec == 1:
-        assert gp.index(d_payload.data_ptr()) == 0
+        assert gp.index(d_payload) == 0
     W = [torch.from_numpy(bf16_to_f32(m)).cuda() for m in mats]
     for batch in (1, 4, 8, 16):
         x = torch.randn(ncols, batch, device="cuda")
         y = torch.full((nrows, batch), float("nan"), device="cuda")
-        gp.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+        gp.gemm(d_payload, x, y, batch)
         assert gp.status() == 0
         xr = x.to(torch.bfloat16).float() if batch >= TC_MIN_BATCH and gp.scratch_bytes() else x
         ro = co = 0
@@ -89,9 +89,9 @@ def test_config5_mix(xg, codec):
     d_payload = torch.from_numpy(payload).cuda()
     out = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     plan = xg.Plan(dec)
-    plan.decode(d_payload.data_ptr(), out.data_ptr())
+    plan.decode(d_payload, out)
     dig = torch.empty(32 * len(dec), dtype=torch.uint8, device="cuda")
-    plan.sha256(out.data_ptr(), dig.data_ptr())
+    plan.sha256(out, dig)
     assert plan.status() == 0
     src = b"".join(m.tobytes() for m in mats)
     assert out.cpu().numpy().tobytes() == src

@@ -40,7 +40,7 @@ def test_gpu_encoder_matches_host(xg, codec, shape, kind):
         # the device payload, copied out with a one-raw-slab plan (a byte copy)
         buf = torch.empty(n, dtype=torch.uint8, device="cuda")
         cp = xg.Plan([dict(src_offset=0, src_size=n, rows=1, cols=1, dst_offset=0, codec=0)])
-        cp.decode(dptr, buf.data_ptr())
+        cp.decode(dptr, buf, payload_bytes=n)
         assert cp.status() == 0
         cp.close()
         got = buf.cpu().numpy()
@@ -48,7 +48,7 @@ def test_gpu_encoder_matches_host(xg, codec, shape, kind):
         # round trip: decode the GPU payload with a plan
         out = torch.empty(rows * cols * 2 + 64, dtype=torch.uint8, device="cuda")
         pl = xg.Plan(slabs)
-        pl.decode(dptr, out.data_ptr())
+        pl.decode(dptr, out, payload_bytes=n)
         assert pl.status() == 0
         assert out[64:].cpu().numpy().tobytes() == w.tobytes()
         pl.close()

@@ -53,7 +53,7 @@ def test_plan_decode_mixed(xg):
     total = sum(len(r) for r in raws)
     d_out = torch.full((total + 64,), 0xCD, dtype=torch.uint8, device="cuda")
     plan = xg.Plan(entries)
-    plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+    plan.decode(d_payload, d_out)
     assert plan.status() == 0
     got = d_out.cpu().numpy().tobytes()
     for e, raw in zip(entries, raws):
@@ -75,11 +75,11 @@ def test_plan_reports_corrupt_slab(xg):
     d_payload = torch.frombuffer(bad, dtype=torch.uint8).cuda()
     d_out = torch.zeros(sum(len(r) for r in raws), dtype=torch.uint8, device="cuda")
     plan = xg.Plan(entries)
-    plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+    plan.decode(d_payload, d_out)
     assert plan.status() == 1
     # the status word is cleared after being read
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
-    plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+    plan.decode(d_payload, d_out)
     assert plan.status() == 0
 
 
@@ -109,7 +109,7 @@ def test_plan_gemm_multi_tensor(xg, batch):
     y = torch.full((yrow, batch), float("nan"), device="cuda")
     d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
     plan = xg.Plan(entries)
-    plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+    plan.gemm(d_payload, x, y, batch)
     assert plan.status() == 0
     xo = yo = 0
     # from TC_MIN_BATCH the plan runs on the tensor cores with X rounded to BF16
@@ -141,12 +141,12 @@ def test_misaligned_outputs_are_refused(xg):
     d_payload = torch.frombuffer(bytearray(blob), dtype=torch.uint8).cuda()
     odd = xg.Plan([dict(src_offset=0, src_size=len(blob), rows=16, cols=256, dst_offset=3, codec=1)])
     with pytest.raises(RuntimeError):
-        odd.decode(d_payload.data_ptr(), d_out.data_ptr())
+        odd.decode(d_payload, d_out)
     odd.close()
     ok = xg.Plan([dict(src_offset=0, src_size=len(blob), rows=16, cols=256, dst_offset=0, codec=1)])
     with pytest.raises(RuntimeError):
-        ok.decode(d_payload.data_ptr(), d_out.data_ptr() + 1)
-    ok.decode(d_payload.data_ptr(), d_out.data_ptr())
+        ok.decode(d_payload, d_out.data_ptr() + 1, out_bytes=d_out.numel() - 1)
+    ok.decode(d_payload, d_out)
     assert ok.status() == 0
     assert d_out[:len(raw)].cpu().numpy().tobytes() == raw
     ok.close()
@@ -173,7 +173,7 @@ def test_plan_decode_host_matches_device_decode(xg, order):
     plan = xg.Plan(entries)
     for _ in range(2):  # the second call reuses the plan's copy stream and events
         d_out.fill_(0xCD)
-        plan.decode_host(h_payload.data_ptr(), len(payload), d_payload.data_ptr(), d_out.data_ptr())
+        plan.decode_host(h_payload.data_ptr(), len(payload), d_payload, d_out)
         assert plan.status() == 0
         got = d_out.cpu().numpy().tobytes()
         for e, raw in zip(entries, raws):
@@ -181,5 +181,5 @@ def test_plan_decode_host_matches_device_decode(xg, order):
     assert plan.launches() >= (4 if order == "archive" else 1)
     short = max(e["src_offset"] + e["src_size"] for e in entries) - 1
     assert xg.load().xksv_plan_decode_host(plan.handle, h_payload.data_ptr(), short, d_payload.data_ptr(),
-                                           d_out.data_ptr(), None) == 1
+                                           d_out.data_ptr(), d_out.numel(), None) == 1
     plan.close()

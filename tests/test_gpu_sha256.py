@@ -66,9 +66,9 @@ def test_plan_sha256_matches_golden_and_hashlib(xg):
     d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
     d_out = torch.zeros(out + 8, dtype=torch.uint8, device="cuda")
     plan = xg.Plan(entries)
-    plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+    plan.decode(d_payload, d_out)
     dig = torch.zeros(32 * len(entries), dtype=torch.uint8, device="cuda")
-    plan.sha256(d_out.data_ptr(), dig.data_ptr())
+    plan.sha256(d_out, dig)
     assert plan.status() == 0
     got = dig.cpu().numpy().tobytes()
     for i, w in enumerate(want):
@@ -94,9 +94,9 @@ def test_plan_sha256_raw_and_tensor(xg):
     d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
     d_out = torch.zeros(48 * 2048, dtype=torch.uint8, device="cuda")
     plan = xg.Plan(entries)
-    plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+    plan.decode(d_payload, d_out)
     dig = torch.zeros(32 * 3, dtype=torch.uint8, device="cuda")
-    plan.sha256(d_out.data_ptr(), dig.data_ptr())
+    plan.sha256(d_out, dig)
     assert plan.status() == 0
     got = dig.cpu().numpy().tobytes()
     for i, raw in enumerate(raws):

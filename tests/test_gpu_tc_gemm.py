@@ -69,7 +69,7 @@ def test_tc_gemm_mixed_codecs(xg, batch):
     plan = xg.Plan(entries)
     for _ in range(2):
         y = torch.full((yn, batch), float("nan"), device="cuda")
-        plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+        plan.gemm(d_payload, x, y, batch)
         assert plan.status() == 0
         check(ws, x, y)
     plan.close()
@@ -86,7 +86,7 @@ def test_tc_gemm_llama_shapes(xg):
     x = torch.randn(xn, 16, device="cuda")
     y = torch.empty(yn, 16, device="cuda")
     plan = xg.Plan(entries)
-    plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 16)
+    plan.gemm(d_payload, x, y, 16)
     assert plan.status() == 0
     check(ws, x, y)
     plan.close()
@@ -103,7 +103,7 @@ def test_tc_gemm_reports_corrupt_slab(xg):
     x = torch.randn(xn, 16, device="cuda")
     y = torch.empty(yn, 16, device="cuda")
     plan = xg.Plan(entries)
-    plan.gemm(d_bad.data_ptr(), x.data_ptr(), y.data_ptr(), 16)
+    plan.gemm(d_bad, x, y, 16)
     assert plan.status() == 1
     plan.close()
 
@@ -131,8 +131,8 @@ def test_tc_gemm_shared_scratch_and_x_base(xg, batch):
         p.set_scratch(scratch.data_ptr(), need)
     for _ in range(2):
         y = torch.full((yn, batch), float("nan"), device="cuda")
-        p1.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
-        p2.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+        p1.gemm(d_payload, x, y, batch)
+        p2.gemm(d_payload, x, y, batch)
         assert p1.status() == 0 and p2.status() == 0
         check(ws, x, y)
     p1.close()

@@ -69,10 +69,10 @@ def test_indexed_gemm_matches_fp32(xg, kind, batch):
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
     x = torch.randn(xn, batch, device="cuda")
     plan = xg.Plan(entries)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     for rep in range(2):  # the split-slab counters must be back at zero
         y = torch.full((yn, batch), float("nan"), device="cuda")
-        plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), batch)
+        plan.gemm(d_payload, x, y, batch)
         assert plan.status() == 0
         check(ws, mats, x, y, 1e-5, plan)
     if batch < TC_MIN_BATCH:
@@ -88,11 +88,11 @@ def test_indexed_gemm_is_deterministic(xg):
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
     x = torch.randn(xn, 1, device="cuda")
     plan = xg.Plan(entries)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     outs = []
     for _ in range(3):
         y = torch.empty(yn, 1, device="cuda")
-        plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 1)
+        plan.gemm(d_payload, x, y, 1)
         assert plan.status() == 0
         outs.append(y.cpu())
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
@@ -124,9 +124,9 @@ def test_index_multi_round_dense_tiles(xg):
     d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
     x = torch.randn(xoff, 1, device="cuda")
     plan = xg.Plan(entries)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     y = torch.empty(yrow, 1, device="cuda")
-    plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 1)
+    plan.gemm(d_payload, x, y, 1)
     assert plan.status() == 0
     check(ws, mats, x, y, 1e-5)
     plan.close()
@@ -143,14 +143,14 @@ def test_index_mixed_plan_and_fallbacks(xg):
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
     x = torch.randn(xn, 2, device="cuda")
     plan = xg.Plan(entries)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     y = torch.full((yn, 2), float("nan"), device="cuda")
-    plan.gemm(d_payload.data_ptr(), x.data_ptr(), y.data_ptr(), 2)
+    plan.gemm(d_payload, x, y, 2)
     assert plan.status() == 0
     check(ws, mats, x, y, 1e-5)
     copy = d_payload.clone()
     y2 = torch.full((yn, 2), float("nan"), device="cuda")
-    plan.gemm(copy.data_ptr(), x.data_ptr(), y2.data_ptr(), 2)
+    plan.gemm(copy, x, y2, 2)
     assert plan.status() == 0
     check(ws, mats, x, y2, 1e-5)
     plan.close()
@@ -169,13 +169,13 @@ def test_index_rejects_corrupt_slab(xg):
         oracle.unpack(bytes(bad[o:o + e["src_size"]]), 16, 1024)
     d_bad = torch.frombuffer(bad, dtype=torch.uint8).cuda()
     plan = xg.Plan(entries)
-    assert plan.index(d_bad.data_ptr()) == 1
+    assert plan.index(d_bad) == 1
     assert plan.status() == 0  # the index call reports and clears its own error
     d_good = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
-    assert plan.index(d_good.data_ptr()) == 0
+    assert plan.index(d_good) == 0
     x = torch.randn(xn, 1, device="cuda")
     y = torch.empty(yn, 1, device="cuda")
-    plan.gemm(d_good.data_ptr(), x.data_ptr(), y.data_ptr(), 1)
+    plan.gemm(d_good, x, y, 1)
     assert plan.status() == 0
     check(ws, mats, x, y, 1e-5)
     plan.close()
@@ -207,10 +207,10 @@ def test_indexed_decode_bit_exact(xg, kind):
         out += len(raw) + (2 if i % 2 else 16)
     d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
     plan = xg.Plan(entries)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     for rep in range(2):
         d_out = torch.full((out + 16,), 0xAB, dtype=torch.uint8, device="cuda")
-        plan.decode(d_payload.data_ptr(), d_out.data_ptr())
+        plan.decode(d_payload, d_out)
         assert plan.status() == 0
         got = d_out.cpu().numpy().tobytes()
         for e, raw in zip(entries, raws):

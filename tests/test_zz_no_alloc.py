@@ -47,12 +47,13 @@ def test_noalloc_matches_plan_decode_twice():
         d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
         want = torch.full((out_bytes,), 0x5A, dtype=torch.uint8, device="cuda")
         plan = xksv_gpu.Plan(entries)
-        plan.decode(d_payload.data_ptr(), want.data_ptr(), stream)
+        plan.decode(d_payload, want, stream)
         assert plan.status(stream) == 0
         plan.close()
         got = torch.full((out_bytes,), 0xA5, dtype=torch.uint8, device="cuda")
         table, n = xksv_gpu.slab_table(entries)
-        assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), got.data_ptr(), stream) == 0
+        assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), d_payload.numel(), got.data_ptr(),
+                                            got.numel(), stream) == 0
         assert torch.equal(got, want)
 
 
@@ -66,9 +67,12 @@ def test_noalloc_reports_bad_slab_and_limit():
     d_payload = torch.frombuffer(bad, dtype=torch.uint8).cuda()
     out = torch.empty(out_bytes, dtype=torch.uint8, device="cuda")
     table, n = xksv_gpu.slab_table(entries)
-    assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), out.data_ptr(), stream) == 1
+    assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), d_payload.numel(), out.data_ptr(),
+                                        out.numel(), stream) == 1
     # the status word is cleared by the next call
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
-    assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), out.data_ptr(), stream) == 0
+    assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), d_payload.numel(), out.data_ptr(),
+                                        out.numel(), stream) == 0
     big, nbig = xksv_gpu.slab_table([entries[0]] * (xksv_gpu.NOALLOC_MAX_SLABS + 1))
-    assert lib.xksv_cuda_decode_noalloc(big, nbig, d_payload.data_ptr(), out.data_ptr(), stream) == 2
+    assert lib.xksv_cuda_decode_noalloc(big, nbig, d_payload.data_ptr(), d_payload.numel(), out.data_ptr(),
+                                        out.numel(), stream) == 2

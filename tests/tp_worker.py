@@ -116,11 +116,11 @@ def gpu_tp_check(rank, world, port, out):
     batch = 3
     x = torch.from_numpy(np.random.default_rng(5).standard_normal((xn, batch)).astype(np.float32)).cuda()
     plan = xksv_gpu.Plan(local, lib)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     y_shard = torch.zeros(pad, batch, device="cuda")
     y_full = torch.full((world * pad, batch), float("nan"), device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    comm.gemm(plan, d_payload.data_ptr(), x.data_ptr(), y_shard.data_ptr(), pad, y_full.data_ptr(),
+    comm.gemm(plan, d_payload, x, y_shard, pad, y_full,
               batch, stream)
     assert plan.status(stream) == 0
     torch.cuda.synchronize()
@@ -163,7 +163,7 @@ def gpu_tp_fused_check(rank, world, port, out):
     idx = torch.from_numpy(xksv_gpu.gathered_to_full(None, world, all_runs, pad)).cuda()
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
     plan = xksv_gpu.Plan(local, lib)
-    assert plan.index(d_payload.data_ptr()) == 0
+    assert plan.index(d_payload) == 0
     fused = xksv_gpu.TPFused(rank, world, pad, 4, lib)
     stream = torch.cuda.current_stream().cuda_stream
     errs = []
@@ -171,7 +171,7 @@ def gpu_tp_fused_check(rank, world, port, out):
         xs = np.random.default_rng(call).standard_normal((xn, batch)).astype(np.float32)
         x = torch.from_numpy(xs).cuda()
         y_full = torch.full((world * pad, batch), float("nan"), device="cuda")
-        fused.gemm(plan, d_payload.data_ptr(), x.data_ptr(), pad, batch, stream, y_full.data_ptr())
+        fused.gemm(plan, d_payload, x, pad, batch, stream, y_full)
         assert plan.status(stream) == 0
         full = y_full[idx].cpu().numpy()
         ref = np.concatenate([bf16_to_f32(w) @ xs[o:o + w.shape[1]]

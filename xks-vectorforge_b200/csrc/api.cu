@@ -176,7 +176,11 @@ struct xksv_plan {
   uint32_t n_ser = 0, n_par = 0, n_raw = 0;
   bool raw_gemm_ok = true;
   bool odd_dst = false;  // a coded slab with an odd byte offset: decode refused
-  uint64_t max_batch_rows = 0;
+  // buffer extents the slab table needs, checked against the sizes every call
+  // is given before anything is launched: payload bytes (max src end),
+  // decoded bytes (max dst end, decode and SHA-256), X rows (max x_offset +
+  // cols) and Y rows (max dst_offset + rows) of GEMV/GEMM
+  uint64_t need_payload = 0, need_out = 0, need_x_rows = 0, need_y_rows = 0;
   int* d_status = nullptr;
   int* h_status = nullptr;
   int grid_ser = 148, grid_par = 148, grid_raw = 148;
@@ -343,9 +347,24 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   *out = nullptr;
   std::vector<Slab> ser, par, raw;
   bool raw_gemm_ok = true, odd_dst = false;
+  uint64_t need_payload = 0, need_out = 0, need_x = 0, need_y = 0;
   for (size_t i = 0; i < n; ++i) {
     const xksv_slab& s = slabs[i];
     if (s.flags || s.src_offset > kMax - s.src_size) return 1;
+    need_payload = std::max(need_payload, s.src_offset + s.src_size);
+    // the bytes a decode of this slab writes at dst_offset, and the X / Y
+    // rows a GEMV/GEMM reads and writes (raw decode-only slabs: src_size
+    // bytes, no rows); an extent that does not fit in 64 bits is refused
+    const bool shaped = s.rows && s.cols && s.cols <= kMax / 2 / s.rows;
+    if ((s.rows || s.cols) && !shaped) return 1;
+    const uint64_t dec = s.codec == XKSV_CODEC_RAW ? s.src_size : s.rows * s.cols * 2;
+    if (s.dst_offset > kMax - dec) return 1;
+    need_out = std::max(need_out, s.dst_offset + dec);
+    if (shaped) {
+      if (s.x_offset > kMax - s.cols || s.dst_offset > kMax - s.rows) return 1;
+      need_x = std::max(need_x, s.x_offset + s.cols);
+      need_y = std::max(need_y, s.dst_offset + s.rows);
+    }
     // decode writes BF16 words: an odd byte offset would be a misaligned store
     if (s.codec != XKSV_CODEC_RAW && (s.dst_offset & 1)) odd_dst = true;
     Slab d{s.src_offset, s.src_size, s.rows, s.cols, s.dst_offset, s.x_offset};
@@ -385,6 +404,10 @@ int xksv_plan_create(const xksv_slab* slabs, size_t n, xksv_plan** out) {
   p->n_raw = uint32_t(raw.size());
   p->raw_gemm_ok = raw_gemm_ok;
   p->odd_dst = odd_dst;
+  p->need_payload = need_payload;
+  p->need_out = need_out;
+  p->need_x_rows = need_x;
+  p->need_y_rows = need_y;
   std::vector<Slab> all;
   all.reserve(n);
   all.insert(all.end(), ser.begin(), ser.end());
@@ -474,9 +497,11 @@ cudaError_t tile_decode(xksv_plan* p, const xksv::Slab* slabs, const uint8_t* pa
 }
 }  // namespace
 
-int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, void* d_out, void* stream) {
+int xksv_plan_decode(const xksv_plan* pc, const void* d_payload, size_t payload_size, void* d_out,
+                     size_t out_size, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
   if (!p || !d_payload || !d_out || p->odd_dst || misaligned(d_out, 2)) return 1;
+  if (p->need_payload > payload_size || p->need_out > out_size) return 1;  // a slab outside a buffer
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint8_t* pay = static_cast<const uint8_t*>(d_payload);
   uint8_t* out = static_cast<uint8_t*>(d_out);
@@ -522,9 +547,10 @@ uint64_t chunk_end(uint64_t end, int c) {  // end * (c + 1) / kHostChunks withou
 }  // namespace
 
 int xksv_plan_decode_host(const xksv_plan* pc, const void* h_payload, size_t payload_size, void* d_payload,
-                          void* d_out, void* stream) {
+                          void* d_out, size_t out_size, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
   if (!p || !h_payload || !d_payload || !d_out || p->odd_dst || misaligned(d_out, 2)) return 1;
+  if (p->need_payload > payload_size || p->need_out > out_size) return 1;  // a slab outside a buffer
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const auto& hs = p->h_slabs;
   uint64_t end = 0;
@@ -542,7 +568,7 @@ int xksv_plan_decode_host(const xksv_plan* pc, const void* h_payload, size_t pay
       ordered = hs[i].src + hs[i].size >= hs[i - 1].src + hs[i - 1].size;
   if (!ordered) {
     if (end && cudaMemcpyAsync(d_payload, h_payload, end, cudaMemcpyHostToDevice, st) != cudaSuccess) return 1;
-    return xksv_plan_decode(p, d_payload, d_out, stream);
+    return xksv_plan_decode(p, d_payload, payload_size, d_out, out_size, stream);
   }
   if (!p->copy_st && cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking) != cudaSuccess) return 1;
   for (cudaEvent_t& ev : p->chunk_ev)
@@ -591,12 +617,13 @@ int xksv_plan_decode_host(const xksv_plan* pc, const void* h_payload, size_t pay
   return e == cudaSuccess ? 0 : 1;
 }
 
-int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, const float* d_x, float* d_y,
-                   size_t batch, void* stream) {
+int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, size_t payload_size, const float* d_x,
+                   size_t x_rows, float* d_y, size_t y_rows, size_t batch, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
   if (!p || !d_payload || !d_x || !d_y || !batch || batch > std::numeric_limits<uint32_t>::max() ||
       misaligned(d_x, 4) || misaligned(d_y, 4))
     return 1;
+  if (p->need_payload > payload_size || p->need_x_rows > x_rows || p->need_y_rows > y_rows) return 1;
   if (p->n_raw && !p->raw_gemm_ok) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint8_t* pay = static_cast<const uint8_t*>(d_payload);
@@ -742,8 +769,8 @@ int xksv_cuda_sha256(const uint64_t* ranges, size_t n, const void* d_base, void*
   return e == cudaSuccess && f == cudaSuccess && g == cudaSuccess ? 0 : 1;
 }
 
-int xksv_plan_sha256(const xksv_plan* p, const void* d_out, void* d_digests, void* stream) {
-  if (!p || !d_out || !d_digests) return 1;
+int xksv_plan_sha256(const xksv_plan* p, const void* d_out, size_t out_size, void* d_digests, void* stream) {
+  if (!p || !d_out || !d_digests || p->need_out > out_size) return 1;
   const uint32_t n = p->n_ser + p->n_par + p->n_raw;
   return launch_sha256(p->d_hash_ranges, n, static_cast<const uint8_t*>(d_out), static_cast<uint8_t*>(d_digests),
                        static_cast<cudaStream_t>(stream)) == cudaSuccess
@@ -751,8 +778,8 @@ int xksv_plan_sha256(const xksv_plan* p, const void* d_out, void* d_digests, voi
              : 1;
 }
 
-int xksv_plan_index(xksv_plan* p, const void* d_payload, void* stream) {
-  if (!p || !d_payload) return 1;
+int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, void* stream) {
+  if (!p || !d_payload || p->need_payload > payload_size) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaStreamSynchronize(st) != cudaSuccess) return 1;
   free_index(p);
@@ -885,12 +912,17 @@ int xksv_tp_fused_open(xksv_tp_fused* c, const void* handles) {
   return ok ? 0 : 1;
 }
 
-int xksv_tp_fused_gemm(xksv_tp_fused* c, const xksv_plan* pc, const void* d_payload, const float* d_x,
-                       size_t rows_shard, size_t batch, float* d_y_full, float** d_gathered, void* stream) {
+int xksv_tp_fused_gemm(xksv_tp_fused* c, const xksv_plan* pc, const void* d_payload, size_t payload_size,
+                       const float* d_x, size_t x_rows, size_t rows_shard, size_t batch, float* d_y_full,
+                       float** d_gathered, void* stream) {
   auto* p = const_cast<xksv_plan*>(pc);
   if (!c || !p || !d_payload || !d_x || !c->d_peer_flags || !batch || batch > c->max_batch ||
       rows_shard > c->max_rows || misaligned(d_x, 4) || misaligned(d_y_full, 4))
     return 1;
+  // the epilogue stores row r of this rank's block at rank * rows_shard + r of
+  // every gathered buffer: a plan row past rows_shard would land in the next
+  // rank's block or past the buffer, onto the flags
+  if (p->need_y_rows > rows_shard || p->need_payload > payload_size || p->need_x_rows > x_rows) return 1;
   // every slab must be on the indexed tile path for this payload
   const uint32_t n = p->n_ser + p->n_par + p->n_raw;
   if (!p->d_tidx || d_payload != p->indexed_payload || p->n_ser_idx != n || !p->n_items) return 1;

@@ -11,9 +11,12 @@
 // on a device and kept until the process exits.
 //
 // The first call on each device looks up that array's device address with
-// cudaGetSymbolAddress (with the device current) and caches it; make that
-// first call before any stream capture.  Every call shares the one array and
-// overwrites it, so calls that overlap on the GPU (different streams, or
+// cudaGetSymbolAddress (with the device current) and caches it for the life
+// of the process; make that first call before any stream capture.  A
+// cudaDeviceReset unloads the library's device code with the array, so the
+// cached address is stale afterwards: a process that resets a device must
+// not call this entry point on it again.  Every call shares the one array
+// and overwrites it, so calls that overlap on the GPU (different streams, or
 // other host threads) race on it: issue them one after another.
 #include <mutex>
 
@@ -39,8 +42,9 @@ int g_noalloc_status_host = 0;
 }  // namespace xksv
 
 extern "C" int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const void* d_payload,
-                                        void* d_out, void* stream) {
+                                        size_t payload_size, void* d_out, size_t out_size, void* stream) {
   using namespace xksv;
+  constexpr uint64_t kMax = ~uint64_t(0);
   if (n > size_t(XKSV_NOALLOC_MAX_SLABS)) return 2;  // beyond the scratch array
   if ((n && !slabs) || !d_payload || !d_out || (reinterpret_cast<uintptr_t>(d_out) & 1)) return 1;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
@@ -63,6 +67,11 @@ extern "C" int xksv_cuda_decode_noalloc(const xksv_slab* slabs, size_t n, const 
     if (s.codec == XKSV_CODEC_TILE16 && (!s.rows || !s.cols || s.src_size < kHdr)) return 1;
     if (s.codec == XKSV_CODEC_PARALLEL32 && (!s.rows || s.rows > 16 || !s.cols || s.src_size < 32))
       return 1;
+    // every slab inside the caller's buffers, checked before any launch
+    if (s.src_offset > kMax - s.src_size || s.src_offset + s.src_size > payload_size) return 1;
+    if (s.codec != XKSV_CODEC_RAW && s.cols > kMax / 2 / s.rows) return 1;
+    const uint64_t dec = s.codec == XKSV_CODEC_RAW ? s.src_size : s.rows * s.cols * 2;
+    if (s.dst_offset > kMax - dec || s.dst_offset + dec > out_size) return 1;
     ++counts[s.codec == XKSV_CODEC_TILE16 ? 0 : s.codec == XKSV_CODEC_PARALLEL32 ? 1 : 2];
   }
   uint32_t pos[3] = {0, counts[0], counts[0] + counts[1]};

@@ -28,6 +28,8 @@
 // shared copy, refilled once per four codes.  Tables: 2^SK-entry single-code
 // table, 2^CK-entry count table, canonical limits up to 32 bits and a
 // bit-serial decoder beyond (the format allows lengths up to 255).
+#include <atomic>
+
 #include "kernels.h"
 #include "xksv_device.cuh"
 
@@ -983,11 +985,14 @@ __global__ void tp_wait_kernel(const uint32_t* flags, uint32_t world, const uint
   __threadfence_system();
 }
 
+// Dynamic shared memory opt-in, once per device (concurrent first calls both
+// set the same values, which is harmless).
 void serial_set_attr() {
-  static int done_mask = 0;
+  static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && ((done_mask >> dev) & 1)) return;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return;
   cudaFuncSetAttribute(serial_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
@@ -995,7 +1000,7 @@ void serial_set_attr() {
   cudaFuncSetAttribute(serial_tile_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   cudaFuncSetAttribute(serial_tile_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   cudaFuncSetAttribute(serial_tile_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
-  if (dev < 31) done_mask |= 1 << dev;
+  if (bit) done.fetch_or(bit, std::memory_order_release);
 }
 
 }  // namespace

@@ -75,11 +75,13 @@ void xksv_tp_comm_destroy(void* comm) {
   if (comm && n.ok) n.comm_destroy(static_cast<ncclComm_t>(comm));
 }
 
-int xksv_tp_gemm(const xksv_plan* plan, const void* d_payload, const float* d_x, float* d_y_shard,
-                 size_t rows_shard, float* d_y_full, size_t batch, void* comm, void* stream) {
+int xksv_tp_gemm(const xksv_plan* plan, const void* d_payload, size_t payload_size, const float* d_x,
+                 size_t x_rows, float* d_y_shard, size_t rows_shard, float* d_y_full, size_t batch, void* comm,
+                 void* stream) {
   const NcclApi& n = nccl();
   if (!plan || !d_y_shard || !d_y_full || !comm || !batch || !n.ok) return 1;
-  if (rows_shard && xksv_plan_gemm(plan, d_payload, d_x, d_y_shard, batch, stream)) return 1;
+  // the shard's rows bound the plan's output rows (checked by the GEMM)
+  if (xksv_plan_gemm(plan, d_payload, payload_size, d_x, x_rows, d_y_shard, rows_shard, batch, stream)) return 1;
   return n.all_gather(d_y_shard, d_y_full, rows_shard * batch, ncclFloat32,
                       static_cast<ncclComm_t>(comm), static_cast<cudaStream_t>(stream)) == ncclSuccess
              ? 0

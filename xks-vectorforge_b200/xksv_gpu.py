@@ -38,20 +38,22 @@ _SIGS = {
     "xksv_plan_create": ([ctypes.POINTER(Slab), ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)],
                          ctypes.c_int),
     "xksv_plan_destroy": ([ctypes.c_void_p], None),
-    "xksv_plan_decode": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
-                         ctypes.c_int),
+    "xksv_plan_decode": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                          ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_decode_host": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
-                               ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
-    "xksv_plan_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                        ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+                               ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                        ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                        ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_status": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_scratch_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
     "xksv_plan_set_scratch": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
-    "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_cuda_sha256": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_void_p,
                           ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
-    "xksv_plan_sha256": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_sha256": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                          ctypes.c_void_p], ctypes.c_int),
     "xksv_cuda_pack_tensor": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int,
                                ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
                                ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_void_p),
@@ -60,17 +62,18 @@ _SIGS = {
     "xksv_tp_fused_create": ([ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t,
                               ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p], ctypes.c_int),
     "xksv_tp_fused_open": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
-    "xksv_tp_fused_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                            ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
-                            ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p], ctypes.c_int),
+    "xksv_tp_fused_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                            ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p],
+                           ctypes.c_int),
     "xksv_tp_fused_destroy": ([ctypes.c_void_p], None),
     "xksv_tp_unique_id": ([ctypes.c_void_p], ctypes.c_int),
     "xksv_tp_comm_create": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                              ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "xksv_tp_comm_destroy": ([ctypes.c_void_p], None),
-    "xksv_tp_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+    "xksv_tp_gemm": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
                       ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
-                      ctypes.c_void_p], ctypes.c_int),
+                      ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_host_pack": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                         ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
                         ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
@@ -81,7 +84,8 @@ _SIGS = {
                                ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_size_t)],
                               ctypes.c_int),
     "xksv_cuda_decode_noalloc": ([ctypes.POINTER(Slab), ctypes.c_size_t, ctypes.c_void_p,
-                                  ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+                                  ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                                  ctypes.c_void_p], ctypes.c_int),
 }
 
 NOALLOC_MAX_SLABS = 4096
@@ -203,8 +207,33 @@ def free_device(d_ptr, lib=None):
     (lib or load()).xksv_cuda_free(d_ptr)
 
 
+def dev_buffer(buf, nbytes=None, what="buffer"):
+    """(address, byte size) of a device buffer given to a plan call: a torch
+    tensor (its own size, or `nbytes` when that is smaller) or an integer
+    device address with its byte size.  The library refuses a call whose
+    slabs fall outside the sizes it is given."""
+    if hasattr(buf, "data_ptr"):
+        n = buf.numel() * buf.element_size()
+        return buf.data_ptr(), n if nbytes is None else min(int(nbytes), n)
+    if nbytes is None:
+        raise TypeError(f"{what}: an integer device address needs its byte size")
+    return int(buf), int(nbytes)
+
+
+def _rows(buf, nrows, batch, what):
+    """(address, rows) of an FP32 [rows, batch] matrix (tensor or address)."""
+    if hasattr(buf, "data_ptr"):
+        n = buf.numel() * buf.element_size() // (4 * max(1, batch))
+        return buf.data_ptr(), n if nrows is None else min(int(nrows), n)
+    if nrows is None:
+        raise TypeError(f"{what}: an integer device address needs its row count")
+    return int(buf), int(nrows)
+
+
 class Plan:
-    """A device-resident plan over one payload buffer (see include/xksv_cuda.h)."""
+    """A device-resident plan over one payload buffer (see include/xksv_cuda.h).
+    Device buffers are torch tensors (their sizes bound the call) or integer
+    addresses with explicit sizes (payload_bytes, out_bytes, x_rows, y_rows)."""
 
     def __init__(self, entries, lib=None):
         self.lib = lib or load()
@@ -215,27 +244,39 @@ class Plan:
         self.handle = h
         self.n = n
 
-    def decode(self, d_payload, d_out, stream=0):
-        if self.lib.xksv_plan_decode(self.handle, d_payload, d_out, stream):
-            raise RuntimeError("xksv_plan_decode launch failed")
+    def decode(self, d_payload, d_out, stream=0, payload_bytes=None, out_bytes=None):
+        pay, npay = dev_buffer(d_payload, payload_bytes, "payload")
+        out, nout = dev_buffer(d_out, out_bytes, "output")
+        if self.lib.xksv_plan_decode(self.handle, pay, npay, out, nout, stream):
+            raise RuntimeError("xksv_plan_decode refused the call or failed to launch")
 
-    def decode_host(self, h_payload, size, d_payload, d_out, stream=0):
-        """Host payload -> d_payload -> decode, copy and decode overlapped
-        (xksv_plan_decode_host)."""
-        if self.lib.xksv_plan_decode_host(self.handle, h_payload, size, d_payload, d_out, stream):
-            raise RuntimeError("xksv_plan_decode_host failed")
+    def decode_host(self, h_payload, size, d_payload, d_out, stream=0, out_bytes=None):
+        """Host payload (`size` bytes at host address h_payload) -> d_payload
+        -> decode, copy and decode overlapped (xksv_plan_decode_host)."""
+        pay, npay = dev_buffer(d_payload, None if hasattr(d_payload, "data_ptr") else size, "payload")
+        out, nout = dev_buffer(d_out, out_bytes, "output")
+        if npay < size:
+            raise ValueError("device payload buffer smaller than the host payload")
+        if self.lib.xksv_plan_decode_host(self.handle, h_payload, size, pay, out, nout, stream):
+            raise RuntimeError("xksv_plan_decode_host refused the call or failed")
 
-    def gemm(self, d_payload, d_x, d_y, batch, stream=0):
-        if self.lib.xksv_plan_gemm(self.handle, d_payload, d_x, d_y, batch, stream):
-            raise RuntimeError("xksv_plan_gemm launch failed")
+    def gemm(self, d_payload, d_x, d_y, batch, stream=0, payload_bytes=None, x_rows=None, y_rows=None):
+        pay, npay = dev_buffer(d_payload, payload_bytes, "payload")
+        x, nx = _rows(d_x, x_rows, batch, "x")
+        y, ny = _rows(d_y, y_rows, batch, "y")
+        if self.lib.xksv_plan_gemm(self.handle, pay, npay, x, nx, y, ny, batch, stream):
+            raise RuntimeError("xksv_plan_gemm refused the call or failed to launch")
 
-    def index(self, d_payload, stream=0):
+    def index(self, d_payload, stream=0, payload_bytes=None):
         """Builds the tile index (xksv_plan_index); returns 0, or 1 on a bad slab."""
-        return self.lib.xksv_plan_index(self.handle, d_payload, stream)
+        pay, npay = dev_buffer(d_payload, payload_bytes, "payload")
+        return self.lib.xksv_plan_index(self.handle, pay, npay, stream)
 
-    def sha256(self, d_out, d_digests, stream=0):
+    def sha256(self, d_out, d_digests, stream=0, out_bytes=None):
         """Enqueues the SHA-256 of every slab's decoded bytes (xksv_plan_sha256)."""
-        if self.lib.xksv_plan_sha256(self.handle, d_out, d_digests, stream):
+        out, nout = dev_buffer(d_out, out_bytes, "output")
+        dig = d_digests.data_ptr() if hasattr(d_digests, "data_ptr") else d_digests
+        if self.lib.xksv_plan_sha256(self.handle, out, nout, dig, stream):
             raise RuntimeError("xksv_plan_sha256 failed")
 
     def scratch_bytes(self):
@@ -339,9 +380,13 @@ class TPComm:
         self.handle = h
         self.rank, self.world = rank, world
 
-    def gemm(self, plan, d_payload, d_x, d_y_shard, rows_shard, d_y_full, batch, stream=0):
-        if self.lib.xksv_tp_gemm(plan.handle, d_payload, d_x, d_y_shard, rows_shard, d_y_full,
-                                 batch, self.handle, stream):
+    def gemm(self, plan, d_payload, d_x, d_y_shard, rows_shard, d_y_full, batch, stream=0,
+             payload_bytes=None, x_rows=None):
+        pay, npay = dev_buffer(d_payload, payload_bytes, "payload")
+        x, nx = _rows(d_x, x_rows, batch, "x")
+        ys = d_y_shard.data_ptr() if hasattr(d_y_shard, "data_ptr") else d_y_shard
+        yf = d_y_full.data_ptr() if hasattr(d_y_full, "data_ptr") else d_y_full
+        if self.lib.xksv_tp_gemm(plan.handle, pay, npay, x, nx, ys, rows_shard, yf, batch, self.handle, stream):
             raise RuntimeError("xksv_tp_gemm failed")
 
     def close(self):
@@ -386,12 +431,16 @@ class TPFused:
             raise RuntimeError("xksv_tp_fused_open failed")
         dist.barrier()
 
-    def gemm(self, plan, d_payload, d_x, rows_shard, batch, stream=0, d_y_full=None):
+    def gemm(self, plan, d_payload, d_x, rows_shard, batch, stream=0, d_y_full=None, payload_bytes=None,
+             x_rows=None):
         """Enqueues the fused call (and a copy of the gathered Y to d_y_full
         when given); returns the device address of the gathered Y."""
+        pay, npay = dev_buffer(d_payload, payload_bytes, "payload")
+        x, nx = _rows(d_x, x_rows, batch, "x")
+        yf = d_y_full.data_ptr() if hasattr(d_y_full, "data_ptr") else d_y_full
         y = ctypes.c_void_p()
-        if self.lib.xksv_tp_fused_gemm(self.handle, plan.handle, d_payload, d_x, rows_shard, batch,
-                                       d_y_full, ctypes.byref(y), stream):
+        if self.lib.xksv_tp_fused_gemm(self.handle, plan.handle, pay, npay, x, nx, rows_shard, batch,
+                                       yf, ctypes.byref(y), stream):
             raise RuntimeError("xksv_tp_fused_gemm failed")
         return y.value
 

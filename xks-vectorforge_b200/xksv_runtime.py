@@ -372,7 +372,7 @@ class ResidentArchive:
         if plan is None:
             return
         try:
-            plan.decode(self.payload_ptr, out.data_ptr(), stream)
+            plan.decode(self.payload, out, stream)
             if plan.status(stream):
                 fail(f"GPU block decode failed: {names[0] if len(names) == 1 else 'archive'}")
         finally:
@@ -509,7 +509,7 @@ class FusedWeight:
         self.rows, self.cols = t["shape"]
         self.plan = xksv_gpu.Plan(gemm_entries(t), lib=archive.lib)
         with torch.cuda.device(archive.device):
-            if self.plan.index(archive.payload_ptr, archive._stream()):
+            if self.plan.index(archive.payload, archive._stream()):
                 fail(f"fused GEMV failed: {self.name}")
         # batch >= TC_MIN_BATCH decodes the weight into a BF16 scratch for the tensor
         # cores: borrow the archive's shared one instead of keeping a
@@ -539,7 +539,7 @@ class FusedWeight:
         else:           # the ABI takes X [cols, batch] and returns Y [rows, batch]
             xt = xb.t().float().contiguous()
             y = torch.empty(self.rows, batch, device=x.device, dtype=torch.float32)
-        self.plan.gemm(self.archive.payload_ptr, xt.data_ptr(), y.data_ptr(), batch, stream)
+        self.plan.gemm(self.archive.payload, xt, y, batch, stream)
         if not self.archive.verified and self.plan.status(stream):
             fail(f"fused GEMV failed: {self.name}")
         out = y if batch == 1 else y.t()

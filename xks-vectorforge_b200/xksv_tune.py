@@ -71,14 +71,14 @@ class GpuTuner:
             plan = xksv_gpu.Plan(entries, lib=self.lib)
             stream = torch.cuda.current_stream(self.device)
             try:
-                plan.decode(payload.data_ptr(), out.data_ptr(), stream.cuda_stream)
+                plan.decode(payload, out, stream.cuda_stream)
                 if plan.status(stream.cuda_stream):
                     raise ValueError("GPU autotuning decode failed")
                 samples = []
                 for _ in range(self.repeats):
                     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     a.record(stream)
-                    plan.decode(payload.data_ptr(), out.data_ptr(), stream.cuda_stream)
+                    plan.decode(payload, out, stream.cuda_stream)
                     b.record(stream)
                     b.synchronize()
                     samples.append(a.elapsed_time(b) / 1e3 / n)
