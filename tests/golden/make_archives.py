@@ -40,7 +40,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("XKSV_REFERENCE", "/root/reference"))
+# the reference tree: $XKSV_REFERENCE, else a directory named "reference"
+# beside this repository's root
+REF = Path(os.environ.get("XKSV_REFERENCE", ROOT.parent / "reference"))
 
 LLAMA_CONFIG = {
     "architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": 64,

@@ -63,3 +63,68 @@ def test_checkpoint_rejects_gaps(tmp_path):
     p.write_bytes(p.read_bytes() + b"\0")
     with pytest.raises(rt.ArchiveError, match="unreferenced data"):
         xc.checkpoint(src)
+
+
+def _raw_safetensors(path, header, data=b""):
+    hb = json.dumps(header).encode() if not isinstance(header, bytes) else header
+    path.write_bytes(len(hb).to_bytes(8, "little") + hb + data)
+
+
+@pytest.mark.parametrize("header,data,msg", [
+    (b'{"a": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}, "a": {}}', b"\0\0", "duplicate JSON key: a"),
+    (b'{"a": {"dtype": "BF16", "shape": [NaN], "data_offsets": [0, 2]}}', b"\0\0", "invalid JSON number"),
+    ({"a": {"dtype": "Q8", "shape": [1], "data_offsets": [0, 1]}}, b"\0", "unsupported dtype Q8 for a"),
+    ({"a": {"dtype": "BF16", "shape": [-1], "data_offsets": [0, 2]}}, b"\0\0", "invalid shape: a"),
+    ({"a": {"dtype": "BF16", "shape": [2], "data_offsets": [0]}}, b"\0" * 4, "invalid offsets: a"),
+    ({"a": {"dtype": "BF16", "shape": [2], "data_offsets": [0, 2]}}, b"\0" * 2, "invalid tensor extent: a"),
+    ({"a": {"dtype": "BF16", "shape": [2], "data_offsets": [0, 4]},
+      "b": {"dtype": "BF16", "shape": [2], "data_offsets": [2, 6]}}, b"\0" * 6, "overlapping or noncontiguous"),
+    ({"a": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}}, b"\0" * 4, "unreferenced data"),
+    ([1, 2], b"", "invalid Safetensors header"),
+    ({"a": 7}, b"", "invalid descriptor: a"),
+])
+def test_checkpoint_header_checks(tmp_path, header, data, msg):
+    """The Safetensors front end refuses malformed headers with the reference
+    compiler's messages (python/xksv.py:30-40, 83-135)."""
+    f = tmp_path / "m.safetensors"
+    _raw_safetensors(f, header, data)
+    with pytest.raises(rt.ArchiveError, match=msg):
+        xc.checkpoint(f)
+
+
+def test_checkpoint_header_length_and_shard_index(tmp_path):
+    f = tmp_path / "t.safetensors"
+    f.write_bytes((1 << 40).to_bytes(8, "little"))
+    with pytest.raises(rt.ArchiveError, match="invalid header length"):
+        xc.checkpoint(f)
+    d = tmp_path / "sharded"
+    d.mkdir()
+    _raw_safetensors(d / "a.safetensors", {"x": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}}, b"\0\0")
+    (d / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {"x": "../a.safetensors"}}))
+    with pytest.raises(rt.ArchiveError, match="invalid shard index"):
+        xc.checkpoint(d)
+    (d / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {"y": "a.safetensors"}}))
+    with pytest.raises(rt.ArchiveError, match="shard index does not match"):
+        xc.checkpoint(d)
+    (d / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {"x": "a.safetensors"}}))
+    (shard,) = xc.checkpoint(d)
+    assert [t["name"] for t in shard["tensors"]] == ["x"]
+
+
+@pytest.mark.parametrize("name,role", [
+    ("model.embed_tokens.weight", "token_embedding"),
+    ("lm_head.weight", "language_model_head"),
+    ("model.visual.blocks.0.attn.qkv.weight", "vision_component"),
+    ("model.layers.0.linear_attn.conv1d.weight", "deltanet_convolution"),
+    ("model.layers.0.linear_attn.in_proj_qkvz.weight", "deltanet_input_projection"),
+    ("model.layers.0.linear_attn.out_proj.weight", "deltanet_output_projection"),
+    ("model.layers.0.linear_attn.A_log", "deltanet_state_parameter"),
+    ("model.layers.0.self_attn.q_proj.weight", "attention_parameter"),
+    ("model.layers.0.mlp.experts.3.down_proj.weight", "moe_expert"),
+    ("model.layers.0.mlp.router.weight", "moe_router"),
+    ("model.layers.0.mlp.gate_proj.weight", "feed_forward_parameter"),
+    ("model.layers.0.input_layernorm.weight", "normalization_parameter"),
+    ("rotary.inv_freq", "other"),
+])
+def test_tensor_role_labels(name, role):
+    assert xc.tensor_role(name) == role

@@ -34,48 +34,63 @@ ASSET_NAMES = ("config.json", "generation_config.json", "tokenizer.json", "token
 CODEC_NAMES = {"dfloat11": "bf16-huffman-tile16", "dfloat11-parallel": "bf16-huffman-parallel32"}
 
 
-def parse_json(data):
-    """Strict JSON: duplicate keys and NaN/Infinity rejected (python/xksv.py:30-40)."""
-    def pairs(items):
-        out = {}
-        for k, v in items:
-            if k in out:
-                fail(f"duplicate JSON key: {k}")
-            out[k] = v
-        return out
+class _StrictObjects:
+    """object_pairs_hook / parse_constant of a JSON reader that refuses what
+    Python's default reader lets through silently: a repeated key (the last
+    one would win) and the NaN / Infinity literals.  The messages are the
+    ones the reference compiler prints (python/xksv.py:30-40)."""
 
-    def bad_constant(_):
+    @staticmethod
+    def build(items):
+        obj = dict(items)
+        if len(obj) != len(items):
+            seen = set()
+            for key, _ in items:
+                if key in seen:
+                    fail(f"duplicate JSON key: {key}")
+                seen.add(key)
+        return obj
+
+    @staticmethod
+    def constant(_literal):
         fail("invalid JSON number")
-    return json.loads(data, object_pairs_hook=pairs, parse_constant=bad_constant)
+
+
+def parse_json(data):
+    """Strict JSON (bytes or str): repeated keys and NaN/Infinity rejected."""
+    return json.loads(data, object_pairs_hook=_StrictObjects.build, parse_constant=_StrictObjects.constant)
+
+
+# The index's role label of a tensor: the first rule whose substrings occur in
+# the tensor name decides.  The labels and their precedence are part of the
+# archive format (the reference's index lists them, python/xksv.py:43-57).
+_ROLE_RULES = (
+    (("embed_tokens", "word_embeddings"), "token_embedding"),
+    (("lm_head", "output_projection"), "language_model_head"),
+    (("visual", "vision"), "vision_component"),
+    (("linear_attn",), "deltanet"),
+    (("self_attn", ".attention."), "attention_parameter"),
+    (("expert",), "moe_expert"),
+    (("router",), "moe_router"),
+    ((".mlp.", ".feed_forward."), "feed_forward_parameter"),
+    (("norm",), "normalization_parameter"),
+)
+# linear-attention (DeltaNet) tensors are labelled by their part
+_DELTANET_RULES = (
+    (("conv",), "deltanet_convolution"),
+    (("in_proj",), "deltanet_input_projection"),
+    (("out_proj",), "deltanet_output_projection"),
+)
+
+
+def _first_rule(name, rules, default):
+    return next((role for keys, role in rules if any(k in name for k in keys)), default)
 
 
 def tensor_role(name):
-    """The index's role label of a tensor name (python/xksv.py:43-57)."""
-    if "embed_tokens" in name or "word_embeddings" in name:
-        return "token_embedding"
-    if "lm_head" in name or "output_projection" in name:
-        return "language_model_head"
-    if "visual" in name or "vision" in name:
-        return "vision_component"
-    if "linear_attn" in name:
-        if "conv" in name:
-            return "deltanet_convolution"
-        if "in_proj" in name:
-            return "deltanet_input_projection"
-        if "out_proj" in name:
-            return "deltanet_output_projection"
-        return "deltanet_state_parameter"
-    if "self_attn" in name or ".attention." in name:
-        return "attention_parameter"
-    if "expert" in name:
-        return "moe_expert"
-    if "router" in name:
-        return "moe_router"
-    if ".mlp." in name or ".feed_forward." in name:
-        return "feed_forward_parameter"
-    if "norm" in name:
-        return "normalization_parameter"
-    return "other"
+    """The index's role label of a tensor name."""
+    role = _first_rule(name, _ROLE_RULES, "other")
+    return _first_rule(name, _DELTANET_RULES, "deltanet_state_parameter") if role == "deltanet" else role
 
 
 def contiguous_strides(shape):
@@ -86,81 +101,99 @@ def contiguous_strides(shape):
     return list(reversed(out))
 
 
+def _shard_files(path):
+    """The checkpoint's shard files, and the shard index's tensor -> file map
+    when a directory has a model.safetensors.index.json (else None)."""
+    if not path.is_dir():
+        return [path], None
+    index_file = path / "model.safetensors.index.json"
+    if not index_file.is_file():
+        return sorted(path.glob("*.safetensors")), None
+    weight_map = parse_json(index_file.read_bytes()).get("weight_map")
+    plain_file = lambda v: isinstance(v, str) and Path(v).name == v and v.endswith(".safetensors")
+    if not isinstance(weight_map, dict) or not all(plain_file(v) for v in weight_map.values()):
+        fail("invalid shard index")
+    return [path / name for name in sorted(set(weight_map.values()))], weight_map
+
+
+def _shard_header(file):
+    """(header bytes, data section bytes) of one Safetensors file: a u64
+    little-endian header length, the JSON header, then the data."""
+    if not file.is_file() or file.suffix != ".safetensors":
+        fail(f"not a Safetensors file: {file}")
+    total = file.stat().st_size
+    with file.open("rb") as f:
+        head = f.read(8)
+        if len(head) < 8:
+            fail(f"truncated header: {file}")
+        (hlen,) = struct.unpack("<Q", head)
+        if hlen > min(MAX_HEADER, total - 8):
+            fail(f"invalid header length: {file}")
+        return f.read(hlen), total - 8 - hlen
+
+
+def _tensor_record(name, desc, data_bytes):
+    """One header entry, validated: a known dtype, a shape of non-negative
+    ints, [start, end) data offsets inside the data section whose length is
+    exactly the shape's element count times the dtype's size."""
+    if not isinstance(desc, dict):
+        fail(f"invalid descriptor: {name}")
+    dtype, shape, offsets = desc.get("dtype"), desc.get("shape"), desc.get("data_offsets")
+    if dtype not in DTYPE_SIZES:
+        fail(f"unsupported dtype {dtype} for {name}")
+    if not isinstance(shape, list) or not all(type(d) is int and d >= 0 for d in shape):
+        fail(f"invalid shape: {name}")
+    if not (isinstance(offsets, list) and len(offsets) == 2 and all(type(o) is int for o in offsets)):
+        fail(f"invalid offsets: {name}")
+    start, end = offsets
+    want = int(np.prod(shape, dtype=object)) * DTYPE_SIZES[dtype]
+    if not 0 <= start <= end <= data_bytes or end - start != want:
+        fail(f"invalid tensor extent: {name}")
+    return dict(name=name, dtype=dtype, shape=shape, strides=contiguous_strides(shape),
+                role=tensor_role(name), start=start, size=end - start)
+
+
+def _check_tiling(file, tensors, data_bytes):
+    """The non-empty tensors cover the data section back to back: no gap,
+    no overlap, nothing after the last one."""
+    expect = 0
+    for t in sorted((t for t in tensors if t["size"]), key=lambda t: t["start"]):
+        if t["start"] != expect:
+            fail(f"overlapping or noncontiguous tensors in {file}")
+        expect = t["start"] + t["size"]
+    if expect != data_bytes:
+        fail(f"unreferenced data in {file}")
+
+
 def checkpoint(path):
     """Shards of a Safetensors checkpoint (a file, or a directory with an
-    optional model.safetensors.index.json) with the reference's checks
-    (python/xksv.py:83-135): known dtypes, extents matching shapes, tensors
-    tiling the data section exactly."""
-    path = Path(path)
-    index_path = path / "model.safetensors.index.json" if path.is_dir() else None
-    mapping = None
-    if index_path and index_path.is_file():
-        mapping = parse_json(index_path.read_bytes()).get("weight_map")
-        if not isinstance(mapping, dict) or any(not isinstance(v, str) or Path(v).name != v
-                                                or not v.endswith(".safetensors") for v in mapping.values()):
-            fail("invalid shard index")
-        files = [path / name for name in sorted(set(mapping.values()))]
-    else:
-        files = sorted(path.glob("*.safetensors")) if path.is_dir() else [path]
+    optional model.safetensors.index.json), every header entry validated and
+    each shard's data section tiled exactly by its tensors; tensors listed in
+    data order.  Error messages are the reference compiler's
+    (python/xksv.py:83-135)."""
+    files, weight_map = _shard_files(Path(path))
     if not files:
         fail("no Safetensors shards found")
-    shards, names = [], set()
+    shards, seen = [], set()
     for file in files:
-        if not file.is_file() or file.suffix != ".safetensors":
-            fail(f"not a Safetensors file: {file}")
-        size = file.stat().st_size
-        with file.open("rb") as f:
-            prefix = f.read(8)
-            if len(prefix) != 8:
-                fail(f"truncated header: {file}")
-            hlen = struct.unpack("<Q", prefix)[0]
-            if hlen > MAX_HEADER or hlen > size - 8:
-                fail(f"invalid header length: {file}")
-            header = f.read(hlen)
-        j = parse_json(header)
-        if not isinstance(j, dict):
+        header, data_bytes = _shard_header(file)
+        entries = parse_json(header)
+        if not isinstance(entries, dict):
             fail("invalid Safetensors header")
-        tensors, ranges = [], []
-        for name, desc in j.items():
+        tensors = []
+        for name, desc in entries.items():
             if name == "__metadata__":
                 continue
-            if name in names:
+            if name in seen:
                 fail(f"duplicate tensor: {name}")
-            names.add(name)
-            if not isinstance(desc, dict):
-                fail(f"invalid descriptor: {name}")
-            dtype, shape, offsets = desc.get("dtype"), desc.get("shape"), desc.get("data_offsets")
-            if dtype not in DTYPE_SIZES:
-                fail(f"unsupported dtype {dtype} for {name}")
-            if not isinstance(shape, list) or any(type(x) is not int or x < 0 for x in shape):
-                fail(f"invalid shape: {name}")
-            if not isinstance(offsets, list) or len(offsets) != 2 or any(type(x) is not int for x in offsets):
-                fail(f"invalid offsets: {name}")
-            start, end = offsets
-            num = 1
-            for dim in shape:
-                num *= dim
-            if start < 0 or end < start or end > size - 8 - hlen or end - start != num * DTYPE_SIZES[dtype]:
-                fail(f"invalid tensor extent: {name}")
-            tensors.append(dict(name=name, dtype=dtype, shape=shape, strides=contiguous_strides(shape),
-                                role=tensor_role(name), start=start, size=end - start))
-            if end > start:
-                ranges.append((start, end))
-        ranges.sort()
-        cursor = 0
-        for start, end in ranges:
-            if start != cursor:
-                fail(f"overlapping or noncontiguous tensors in {file}")
-            cursor = end
-        if cursor != size - 8 - hlen:
-            fail(f"unreferenced data in {file}")
-        tensors.sort(key=lambda x: x["start"])
+            seen.add(name)
+            tensors.append(_tensor_record(name, desc, data_bytes))
+        _check_tiling(file, tensors, data_bytes)
+        tensors.sort(key=lambda t: t["start"])
         shards.append(dict(name=file.name, path=str(file), header=base64.b64encode(header).decode("ascii"),
-                           header_size=hlen, tensors=tensors))
-    if mapping is not None:
-        actual = {t["name"]: s["name"] for s in shards for t in s["tensors"]}
-        if mapping != actual:
-            fail("shard index does not match discovered tensor names and files")
+                           header_size=len(header), tensors=tensors))
+    if weight_map is not None and weight_map != {t["name"]: s["name"] for s in shards for t in s["tensors"]}:
+        fail("shard index does not match discovered tensor names and files")
     return shards
 
 
