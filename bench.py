@@ -485,6 +485,8 @@ def run_case(args):
         y = torch.empty(nslabs * rows, nb, device=dev)
         if plan.index(d_payload, h):
             raise RuntimeError("xksv_plan_index failed")
+        plan.set_gemm_route({"auto": xksv_gpu.GEMM_AUTO, "scratch": xksv_gpu.GEMM_SCRATCH,
+                             "fused": xksv_gpu.GEMM_FUSED}[args.route])
         fn = lambda: plan.gemm(d_payload, x, y, nb, h)
     else:
         d_out = torch.empty(out, dtype=torch.uint8, device=dev)
@@ -506,7 +508,7 @@ def run_case(args):
                 ms_per_launch=round(ms, 5))
     if gemv:
         idx = nslabs * (cols // 16 + 1) * 4
-        line.update(batch=args.batch, launches=launches,
+        line.update(batch=args.batch, launches=launches, route=args.route,
                     tflops=round(2 * (out / 2) * args.batch / ms / 1e9, 2),
                     gweights_per_s=round(out / 2 / ms / 1e6, 1),
                     traffic_gbs=round((len(payload) + idx) / ms / 1e6, 1), index_bytes=idx)
@@ -1144,6 +1146,8 @@ def main():
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the configs[3] and configs[4] keys")
     ap.add_argument("--batch", type=int, default=1, help="batch columns of X in gemv- cases")
+    ap.add_argument("--route", default="auto", choices=("auto", "scratch", "fused"),
+                    help="tensor-core GEMM route of gemv- cases at batch >= 4 (xksv_plan_set_gemm_route)")
     ap.add_argument("--case", default=None,
                     help="CODEC:ROWSxCOLS:SLABS small decode workload (profiling), e.g. parallel:16x2048:2048; "
                          "gemv-serial:16x4096:1024 runs the indexed batch-1 GEMV instead")

@@ -131,6 +131,20 @@ int xksv_plan_gemm(const xksv_plan* plan, const void* d_payload, size_t payload_
 size_t xksv_plan_scratch_bytes(const xksv_plan* plan);
 int xksv_plan_set_scratch(xksv_plan* plan, void* d_scratch, size_t bytes);
 
+/* Tensor-core routing of xksv_plan_gemm for 4 <= batch <= 128 on a plan
+ * indexed for the payload (xksv_plan_index) whose slabs are all 16-row
+ * serial-codec slabs: XKSV_GEMM_FUSED decodes each tile row straight into
+ * the shared-memory operand stages of the tensor-core MMAs (one kernel, no
+ * decoded weight written to memory); XKSV_GEMM_SCRATCH decodes into the BF16
+ * scratch and runs the tensor-core GEMM on it (also the route for larger
+ * batches and other plans); XKSV_GEMM_AUTO (the default) picks the fused
+ * kernel wherever it applies.  Returns 1 for an unknown route. */
+enum { XKSV_GEMM_AUTO = 0, XKSV_GEMM_SCRATCH = 1, XKSV_GEMM_FUSED = 2 };
+int xksv_plan_set_gemm_route(xksv_plan* plan, int route);
+/* 1 when the fused route applies to this plan and payload (after
+ * xksv_plan_index), else 0. */
+int xksv_plan_fused_ready(const xksv_plan* plan, const void* d_payload);
+
 /* Synchronises `stream`, returns 0 when no slab reported an error since the
  * last call (then clears the word), else 1. */
 int xksv_plan_status(const xksv_plan* plan, void* stream);

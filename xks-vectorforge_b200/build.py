@@ -15,7 +15,7 @@ ROOT = HERE.parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libxksv_cuda.so"
 SOURCES = ["api.cu", "parallel_kernels.cu", "serial_kernels.cu", "raw_kernels.cu", "pack_host.cpp", "noalloc.cu",
-           "tp.cpp", "tc_gemm.cu", "sha256.cu", "pack_gpu.cu"]
+           "tp.cpp", "tc_gemm.cu", "fused_gemm.cu", "sha256.cu", "pack_gpu.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -9,7 +9,9 @@
 #include <algorithm>
 #include <cstring>
 #include <limits>
+#include <map>
 #include <mutex>
+#include <queue>
 #include <vector>
 
 #include "xksv_cuda.h"
@@ -191,6 +193,7 @@ struct xksv_plan {
   std::vector<xksv::Slab> h_slabs;  // host copy of d_slabs
   const void* indexed_payload = nullptr;
   uint32_t* d_tidx = nullptr;
+  uint32_t* d_tmid = nullptr;  // row-8 offsets of the tiles (fused GEMM work split)
   uint64_t* d_tbase = nullptr;
   xksv::GemvItem* d_items = nullptr;
   uint32_t n_items = 0;
@@ -206,6 +209,15 @@ struct xksv_plan {
   uint8_t* d_scratch = nullptr;
   bool scratch_owned = true;  // false: lent by the caller (xksv_plan_set_scratch)
   void* d_xt = nullptr;  // BF16 X^T [256][x_cols] of X rows from x_base
+  // fused decode -> tensor-core GEMM (xksv_plan_index of an all-serial,
+  // all-indexable plan whose codebooks fit the fused decoder)
+  bool fused_ok = false;
+  int gemm_route = 0;  // XKSV_GEMM_*
+  uint32_t n_fctas = 0;
+  uint32_t* d_fseg0 = nullptr;  // CTA c's segments: d_ftasks[d_fseg0[c] .. d_fseg0[c + 1])
+  xksv::FusedTask* d_ftasks = nullptr;
+  xksv::FusedGroup* d_fgroups = nullptr;
+  uint32_t* d_fmembers = nullptr;
   uint64_t* d_hash_ranges = nullptr;  // per slab in creation order: {dst, decoded bytes}
   // xksv_plan_decode_host: copy stream and per-chunk events (created on first use)
   cudaStream_t copy_st = nullptr;
@@ -215,11 +227,23 @@ struct xksv_plan {
 namespace {
 void free_index(xksv_plan* p) {
   if (p->d_tidx) cudaFree(p->d_tidx);
+  if (p->d_tmid) cudaFree(p->d_tmid);
   if (p->d_tbase) cudaFree(p->d_tbase);
   if (p->d_items) cudaFree(p->d_items);
   if (p->d_partials) cudaFree(p->d_partials);
   if (p->d_counters) cudaFree(p->d_counters);
+  if (p->d_fseg0) cudaFree(p->d_fseg0);
+  if (p->d_ftasks) cudaFree(p->d_ftasks);
+  if (p->d_fgroups) cudaFree(p->d_fgroups);
+  if (p->d_fmembers) cudaFree(p->d_fmembers);
+  p->d_fseg0 = nullptr;
+  p->d_ftasks = nullptr;
+  p->d_fgroups = nullptr;
+  p->d_fmembers = nullptr;
+  p->n_fctas = 0;
+  p->fused_ok = false;
   p->d_tidx = nullptr;
+  p->d_tmid = nullptr;
   p->d_tbase = nullptr;
   p->d_items = nullptr;
   p->d_partials = nullptr;
@@ -277,6 +301,109 @@ bool build_tc_groups(const std::vector<xksv::Slab>& all, std::vector<xksv::TcGro
   }
   groups.push_back(cur);
   return true;
+}
+// Fused-GEMM groups and CTA work: slabs reading the same X columns
+// (x_offset, cols) in groups of up to 32 (one slab per lane).  The work unit
+// is a half tile of a group (8 rows x 16 columns of all its slabs; the same
+// instruction count whatever the group's slab count, since a warp issues for
+// all its lanes).  A CTA's producer warps share each of its segments (one
+// group's run of half tiles), so a CTA's time follows the sum over its
+// segments of the largest warp share plus a start-up per segment (stream
+// starts, length staging, table build: measured about half a unit).  Two
+// schedules are built and the one whose slowest CTA is cheaper is kept:
+//   * by group: every group gets one CTA, then the group whose CTAs carry
+//     the most half tiles gets another, until there are `sms` CTAs;
+//   * equal shares: the groups' units in order cut into `sms` equal ranges,
+//     a range that crosses a group boundary becoming several segments.
+// seg0[c] .. seg0[c + 1] are CTA c's segments.  X columns are relative to
+// x_base.
+void build_fused(const std::vector<xksv::Slab>& all, uint64_t x_base, int sms, uint32_t warps,
+                 std::vector<xksv::FusedGroup>& groups, std::vector<uint32_t>& members,
+                 std::vector<xksv::FusedTask>& segs, std::vector<uint32_t>& seg0) {
+  std::map<std::pair<uint64_t, uint64_t>, std::vector<uint32_t>> by_x;
+  std::vector<std::pair<uint64_t, uint64_t>> order;
+  for (uint32_t i = 0; i < all.size(); ++i) {
+    const auto key = std::make_pair(all[i].xoff, all[i].cols);
+    auto it = by_x.find(key);
+    if (it == by_x.end()) {
+      order.push_back(key);
+      it = by_x.emplace(key, std::vector<uint32_t>()).first;
+    }
+    it->second.push_back(i);
+  }
+  for (const auto& key : order) {
+    const std::vector<uint32_t>& v = by_x[key];
+    for (size_t k = 0; k < v.size(); k += 32) {
+      xksv::FusedGroup g{};
+      g.m0 = uint32_t(members.size());
+      g.nslabs = uint32_t(std::min<size_t>(32, v.size() - k));
+      g.tiles = uint32_t(key.second / 16);
+      g.xoff = key.first - x_base;
+      members.insert(members.end(), v.begin() + k, v.begin() + k + g.nslabs);
+      groups.push_back(g);
+    }
+  }
+  const size_t ng = groups.size();
+  auto units = [&](size_t g) { return 2 * uint64_t(groups[g].tiles); };
+  using Sched = std::pair<std::vector<xksv::FusedTask>, std::vector<uint32_t>>;
+  // cost of a schedule in units: the slowest CTA's segments, each its
+  // largest warp share + a start-up of half a unit
+  auto cost = [&](const Sched& sc) {
+    double worst = 0;
+    for (size_t c = 0; c + 1 < sc.second.size(); ++c) {
+      double t = 0;
+      for (uint32_t i = sc.second[c]; i < sc.second[c + 1]; ++i)
+        t += double((sc.first[i].h1 - sc.first[i].h0 + warps - 1) / warps) + 0.5;
+      worst = std::max(worst, t);
+    }
+    return worst;
+  };
+  Sched by_group, shares;
+  {
+    std::vector<uint32_t> parts(ng, 1);
+    auto load = [&](size_t g) { return (units(g) + parts[g] - 1) / parts[g]; };
+    std::priority_queue<std::pair<uint64_t, size_t>> q;  // (half tiles per CTA, group)
+    for (size_t g = 0; g < ng; ++g) q.emplace(load(g), g);
+    size_t total = ng;
+    while (total < size_t(sms) && !q.empty()) {
+      const size_t g = q.top().second;
+      q.pop();
+      if (parts[g] >= units(g)) continue;  // one half tile per CTA already
+      ++parts[g];
+      ++total;
+      q.emplace(load(g), g);
+    }
+    for (size_t g = 0; g < ng; ++g)
+      for (uint32_t j = 0; j < parts[g]; ++j) {
+        const uint64_t u = units(g);
+        by_group.second.push_back(uint32_t(by_group.first.size()));
+        by_group.first.push_back(xksv::FusedTask{uint32_t(g), uint32_t(u * j / parts[g]), uint32_t(u * (j + 1) / parts[g]), 0});
+      }
+    by_group.second.push_back(uint32_t(by_group.first.size()));
+  }
+  {
+    std::vector<uint64_t> unit0(ng);
+    uint64_t all_units = 0;
+    for (size_t g = 0; g < ng; ++g) {
+      unit0[g] = all_units;
+      all_units += units(g);
+    }
+    const uint64_t nctas = std::min<uint64_t>(uint64_t(std::max(sms, 1)), all_units);
+    size_t g = 0;
+    for (uint64_t c = 0; c < nctas; ++c) {
+      shares.second.push_back(uint32_t(shares.first.size()));
+      const uint64_t u0 = all_units * c / nctas, u1 = all_units * (c + 1) / nctas;
+      while (g < ng && unit0[g] + units(g) <= u0) ++g;
+      for (size_t h = g; h < ng && unit0[h] < u1; ++h) {
+        const uint64_t a = std::max(u0, unit0[h]), b = std::min(u1, unit0[h] + units(h));
+        if (a < b) shares.first.push_back(xksv::FusedTask{uint32_t(h), uint32_t(a - unit0[h]), uint32_t(b - unit0[h]), 0});
+      }
+    }
+    shares.second.push_back(uint32_t(shares.first.size()));
+  }
+  const Sched& best = cost(shares) < cost(by_group) ? shares : by_group;
+  segs = best.first;
+  seg0 = best.second;
 }
 }  // namespace
 
@@ -636,6 +763,32 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, size_t payload_si
   // rounded to BF16 (200 us for any batch <= 256, against 230 us for batch 4
   // on the CUDA cores; the 70B linears: 164 ms against 226 ms at batch 4)
   const bool indexed = p->d_tidx && d_payload == p->indexed_payload;
+  const bool fused = p->fused_ok && indexed && batch >= 4 && batch <= 128 && p->gemm_route != XKSV_GEMM_SCRATCH;
+  if (fused) {
+    // one kernel decodes every tile row into tensor-core operand stages,
+    // after a prep kernel (X^T in BF16, zeroed Y rows) that it overlaps
+    if (!p->d_xt && cudaMalloc(&p->d_xt, 256 * p->x_cols * 2) != cudaSuccess) return 1;
+    FusedArgs f{};
+    f.seg0 = p->d_fseg0;
+    f.tasks = p->d_ftasks;
+    f.groups = p->d_fgroups;
+    f.members = p->d_fmembers;
+    f.slabs = p->d_slabs;
+    f.tbase = p->d_tbase;
+    f.tidx = p->d_tidx;
+    f.tmid = p->d_tmid;
+    f.payload = pay;
+    f.xt = p->d_xt;
+    f.xt_ld = p->x_cols;
+    f.y = d_y;
+    f.ld = ld;
+    f.nb = uint32_t(batch);
+    f.npad = (f.nb + 15) / 16 * 16;
+    f.status = p->d_status;
+    e = launch_fused_gemm(f, p->n_fctas, d_x + p->x_base * ld, p->x_cols, p->d_groups, p->ngroups, st);
+    p->launches = 2;
+    return e == cudaSuccess ? 0 : 1;
+  }
   if (p->tc_ok && batch >= 4) {
     // decode every slab into its BF16 row group, then the tensor-core GEMM,
     // up to 256 batch columns per pass over the same decoded scratch
@@ -724,6 +877,16 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, size_t payload_si
   return e == cudaSuccess ? 0 : 1;
 }
 
+int xksv_plan_set_gemm_route(xksv_plan* p, int route) {
+  if (!p || route < XKSV_GEMM_AUTO || route > XKSV_GEMM_FUSED) return 1;
+  p->gemm_route = route;
+  return 0;
+}
+
+int xksv_plan_fused_ready(const xksv_plan* p, const void* d_payload) {
+  return p && p->fused_ok && p->d_tidx && d_payload == p->indexed_payload ? 1 : 0;
+}
+
 size_t xksv_plan_scratch_bytes(const xksv_plan* p) {
   return p && p->tc_ok ? size_t(std::max<uint64_t>(16, p->scratch_bytes)) : 0;
 }
@@ -778,6 +941,56 @@ int xksv_plan_sha256(const xksv_plan* p, const void* d_out, size_t out_size, voi
              : 1;
 }
 
+// After a successful index: the fused decode -> tensor-core GEMM applies
+// when every slab of the plan is on the tile path, the plan has a
+// tensor-core path and every codebook fits the fused decoder's tables.  Any
+// failure here only leaves the fused route off.
+static void setup_fused(xksv_plan* p, const uint8_t* d_payload, cudaStream_t st) {
+  const uint32_t n = p->n_ser + p->n_par + p->n_raw;
+  if (!p->tc_ok || !n || p->n_ser_idx != n) return;
+  uint8_t* d_ok = nullptr;
+  std::vector<uint8_t> ok(n, 0);
+  bool good = cudaMalloc(&d_ok, n) == cudaSuccess && launch_fused_check(p->d_slabs, n, d_payload, d_ok, st) == cudaSuccess &&
+              cudaMemcpyAsync(ok.data(), d_ok, n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+              cudaStreamSynchronize(st) == cudaSuccess;
+  if (d_ok) cudaFree(d_ok);
+  for (uint32_t i = 0; i < n && good; ++i) good = ok[i] == 1;
+  if (!good) return;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
+  std::vector<FusedGroup> groups;
+  std::vector<uint32_t> members, seg0;
+  std::vector<FusedTask> tasks;
+  build_fused(p->h_slabs, p->x_base, sms, fused_producers(16, nullptr), groups, members, tasks, seg0);
+  good = !tasks.empty() && seg0.size() >= 2 &&
+         cudaMalloc(&p->d_fseg0, seg0.size() * sizeof(uint32_t)) == cudaSuccess &&
+         cudaMemcpyAsync(p->d_fseg0, seg0.data(), seg0.size() * sizeof(uint32_t), cudaMemcpyHostToDevice, st) ==
+             cudaSuccess &&
+         cudaMalloc(&p->d_ftasks, tasks.size() * sizeof(FusedTask)) == cudaSuccess &&
+         cudaMalloc(&p->d_fgroups, groups.size() * sizeof(FusedGroup)) == cudaSuccess &&
+         cudaMalloc(&p->d_fmembers, members.size() * sizeof(uint32_t)) == cudaSuccess &&
+         cudaMemcpyAsync(p->d_ftasks, tasks.data(), tasks.size() * sizeof(FusedTask), cudaMemcpyHostToDevice, st) ==
+             cudaSuccess &&
+         cudaMemcpyAsync(p->d_fgroups, groups.data(), groups.size() * sizeof(FusedGroup), cudaMemcpyHostToDevice,
+                         st) == cudaSuccess &&
+         cudaMemcpyAsync(p->d_fmembers, members.data(), members.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                         st) == cudaSuccess &&
+         cudaStreamSynchronize(st) == cudaSuccess;
+  if (!good) {
+    if (p->d_fseg0) cudaFree(p->d_fseg0);
+    p->d_fseg0 = nullptr;
+    if (p->d_ftasks) cudaFree(p->d_ftasks);
+    if (p->d_fgroups) cudaFree(p->d_fgroups);
+    if (p->d_fmembers) cudaFree(p->d_fmembers);
+    p->d_ftasks = nullptr;
+    p->d_fgroups = nullptr;
+    p->d_fmembers = nullptr;
+    return;
+  }
+  p->n_fctas = uint32_t(seg0.size() - 1);
+  p->fused_ok = true;
+}
+
 int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, void* stream) {
   if (!p || !d_payload || p->need_payload > payload_size) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -810,6 +1023,7 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, vo
   // every copy and fill on the caller's stream, ahead of the index kernel
   // (a non-blocking stream does not wait for the legacy default stream)
   bool ok = cudaMalloc(&p->d_tidx, total * sizeof(uint32_t)) == cudaSuccess &&
+            cudaMalloc(&p->d_tmid, total * sizeof(uint32_t)) == cudaSuccess &&
             cudaMalloc(&p->d_tbase, n * sizeof(uint64_t)) == cudaSuccess &&
             cudaMalloc(&p->d_items, items.size() * sizeof(GemvItem)) == cudaSuccess &&
             cudaMalloc(&p->d_partials, items.size() * 16 * 4 * sizeof(float)) == cudaSuccess &&
@@ -818,9 +1032,10 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, vo
             cudaMemcpyAsync(p->d_items, items.data(), items.size() * sizeof(GemvItem), cudaMemcpyHostToDevice, st) == cudaSuccess &&
             cudaMemsetAsync(p->d_counters, 0, n * sizeof(uint32_t), st) == cudaSuccess &&
             cudaMemsetAsync(p->d_tidx, 0, total * sizeof(uint32_t), st) == cudaSuccess &&
+            cudaMemsetAsync(p->d_tmid, 0, total * sizeof(uint32_t), st) == cudaSuccess &&
             cudaMemsetAsync(p->d_status, 0, sizeof(int), st) == cudaSuccess;
   if (ok)
-    ok = launch_serial_index(p->d_slabs, n, static_cast<const uint8_t*>(d_payload), p->d_tidx,
+    ok = launch_serial_index(p->d_slabs, n, static_cast<const uint8_t*>(d_payload), p->d_tidx, p->d_tmid,
                              p->d_tbase, p->d_status, st) == cudaSuccess;
   if (ok)
     ok = cudaMemcpyAsync(p->h_status, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, st) == cudaSuccess &&
@@ -834,6 +1049,7 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, vo
   }
   p->n_items = uint32_t(items.size());
   p->indexed_payload = d_payload;
+  setup_fused(p, static_cast<const uint8_t*>(d_payload), st);
   return 0;
 }
 

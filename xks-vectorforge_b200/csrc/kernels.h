@@ -32,9 +32,11 @@ cudaError_t launch_raw_gemm(const Slab* slabs, uint32_t n, const uint8_t* payloa
                             cudaStream_t st);
 
 // Tile index of 16-row serial-codec slabs: tidx[tbase[i] + k] = bit offset of
-// tile k's first code in slab i's stream, tidx[tbase[i] + tiles] = bit count.
+// tile k's first code in slab i's stream, tidx[tbase[i] + tiles] = bit count;
+// tmid[tbase[i] + k] = bit offset of tile k's row 8 (its 129th code).
 cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* payload,
-                                uint32_t* tidx, const uint64_t* tbase, int* status, cudaStream_t st);
+                                uint32_t* tidx, uint32_t* tmid, const uint64_t* tbase, int* status,
+                                cudaStream_t st);
 
 struct GemvArgs {
   const GemvItem* items;
@@ -91,6 +93,54 @@ size_t tc_gemm_smem_bytes(uint32_t npad);
 // K is split, then runs the tensor-core GEMM: ngroups * ksplit CTAs.
 cudaError_t launch_tc_gemm(const TcGemmArgs& args, uint32_t ngroups, const float* x, uint64_t x_cols,
                            cudaStream_t st);
+
+// X (FP32, [cols, ld] from column 0 of the pass) to X^T BF16 [npad][xt_ld],
+// zero for batch columns nb <= n < npad; and Y[rows of every group, 0..nb) = 0.
+cudaError_t launch_xt_convert(const float* x, uint32_t ld, uint32_t nb, uint64_t cols, uint32_t npad, void* xt,
+                              uint64_t xt_ld, cudaStream_t st);
+cudaError_t launch_zero_rows(const TcGroup* groups, uint32_t ngroups, float* y, uint32_t ld, uint32_t nb,
+                             cudaStream_t st);
+
+// Fused decode -> tensor-core GEMM of indexed 16-row serial-codec slabs.  A
+// group is up to 32 slabs reading the same X columns; a CTA runs one or more
+// segments, each a range of one group's half tiles (8 rows x 16 columns).
+struct FusedGroup {
+  uint32_t m0;       // first member in the members array (slab indices)
+  uint32_t nslabs;   // <= 32
+  uint32_t tiles;    // cols / 16
+  uint32_t pad;
+  uint64_t xoff;     // X^T column of the group's column 0
+};
+struct FusedTask {  // one segment of a CTA's work
+  uint32_t group, h0, h1, pad;  // half tiles [h0, h1) of the group (half h: rows 8 (h % 2).. of tile h / 2)
+};
+struct FusedArgs {
+  const uint32_t* seg0;  // CTA c runs segments tasks[seg0[c] .. seg0[c + 1])
+  const FusedTask* tasks;
+  const FusedGroup* groups;
+  const uint32_t* members;
+  const Slab* slabs;
+  const uint64_t* tbase;
+  const uint32_t* tidx;
+  const uint32_t* tmid;  // row-8 offsets of the tiles
+  const uint8_t* payload;
+  const void* xt;        // BF16 X^T [npad][xt_ld]
+  uint64_t xt_ld;
+  float* y;              // Y at batch column b0 (row stride ld), rows zeroed
+  uint32_t ld, nb, npad;
+  int* status;
+};
+// Producer warps and dynamic shared memory for a batch pass of npad columns
+// (16 <= npad <= 128, a multiple of 16); 0 producers when it does not fit.
+uint32_t fused_producers(uint32_t npad, size_t* smem_bytes);
+// The codebook of every slab fits the fused decoder's lane tables: ok[i] = 1.
+cudaError_t launch_fused_check(const Slab* slabs, uint32_t n, const uint8_t* payload, uint8_t* ok,
+                               cudaStream_t st);
+// X (FP32 [x_cols, ld] at the pass's first column) to args.xt, zeroed Y rows
+// of `groups`, then `nctas` fused CTAs (args.seg0 has nctas + 1 entries),
+// launched to overlap the prep kernel: two launches.
+cudaError_t launch_fused_gemm(const FusedArgs& args, uint32_t nctas, const float* x, uint64_t x_cols,
+                              const TcGroup* groups, uint32_t ngroups, cudaStream_t st);
 
 // SHA-256 (FIPS 180-4) of n ranges {offset, length} (device array of 2n u64)
 // of d_base; 32-byte big-endian digests to d_digests.

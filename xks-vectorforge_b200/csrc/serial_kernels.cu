@@ -287,6 +287,7 @@ struct SerialArgs {
   int* status;
   uint32_t* tidx;         // MODE 2: tile index (bit offset of each 16x16 tile's first code)
   const uint64_t* tbase;  // MODE 2: first index entry of each slab
+  uint32_t* tmid;         // MODE 2: bit offset of each tile's row 8 (same entry positions)
 };
 
 struct SOut {
@@ -523,14 +524,16 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
       }
       // ---- 5. exact decode straight to the output ----
       if (MODE == 2 && myN) {
-        // tile index: the stream offset of every 256th code (a 16x16 tile start)
+        // tile index: the stream offset of every 256th code (a 16x16 tile
+        // start) and of every tile's 129th code (its row 8)
         SmemWin96 r;
         r.init(S.win, t == 0 ? p0rel : S.endpos[t - 1]);
         bool dead = false;
         uint32_t* ti = a.tidx + a.tbase[si];
+        uint32_t* tm = a.tmid + a.tbase[si];
         const uint32_t gend = base + my_off + myN;
         for (uint32_t g = base + my_off; g < gend; ++g) {
-          if ((g & 255u) == 0) ti[g >> 8] = R0 + r.pos();
+          if ((g & 127u) == 0) ((g & 128u) ? tm : ti)[g >> 8] = R0 + r.pos();
           r.refill();
           code1<7>(S, r, dead);
         }
@@ -1029,10 +1032,10 @@ cudaError_t launch_serial_gemm(const Slab* slabs, uint32_t n, const uint8_t* pay
 }
 
 cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* payload,
-                                uint32_t* tidx, const uint64_t* tbase, int* status, cudaStream_t st) {
+                                uint32_t* tidx, uint32_t* tmid, const uint64_t* tbase, int* status, cudaStream_t st) {
   if (!n) return cudaSuccess;
   serial_set_attr();
-  SerialArgs a{payload, nullptr, nullptr, nullptr, 1, 1, status, tidx, tbase};
+  SerialArgs a{payload, nullptr, nullptr, nullptr, 1, 1, status, tidx, tbase, tmid};
   serial_slab_kernel<2><<<n, ST, sizeof(SerialShared), st>>>(slabs, n, a);
   return cudaGetLastError();
 }

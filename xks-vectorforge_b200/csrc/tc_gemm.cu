@@ -22,6 +22,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace xksv {
 namespace {
@@ -29,88 +30,6 @@ namespace {
 constexpr int TC_THREADS = 128;
 constexpr int TC_KC = 64;              // K per stage (4 MMAs of K = 16)
 constexpr int TC_M = 128;              // rows per MMA tile (TMEM lanes)
-constexpr uint32_t kSpin = 1u << 24;   // bounded mbarrier polls (with back-off)
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-
-// Polls the mbarrier phase with the given parity; false after kSpin polls.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpin; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (i > 64) __nanosleep(64);
-  }
-  return false;
-}
-
-// UMMA shared-memory descriptor, K-major, no swizzle: start, leading (K
-// direction core-matrix) and stride (8-row direction) byte offsets >> 4,
-// descriptor version 1 (sm_100) in bits 46-47, layout type 0 in bits 61-63.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
-         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
-}
-
-// Instruction descriptor, kind::f16: FP32 accumulate (bits 4-5 = 1), A and B
-// BF16 (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 in bits 17-22, M >> 4
-// in bits 24-28.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(uint32_t m, uint32_t n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t idesc, uint32_t accumulate) {
-  const uint32_t z = 0;
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-}
-
-// 16 FP32 accumulator columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 // Byte offset of (row m, 16-byte K chunk c of a 64-wide stage) in a stage
 // buffer holding `rows` rows: K step j = c / 2 occupies rows * 32 bytes; in
@@ -285,12 +204,26 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& args, uint32_t ngroups, const float
   const size_t smem = std::max(tc_gemm_smem_bytes(args.npad), per_sm / (fit + 1) + 1024);
   cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  const uint64_t total = x_cols * args.npad;
-  const int cb = int(std::min<uint64_t>((total + 255) / 256, 4096));
-  xt_convert_kernel<<<cb, 256, 0, st>>>(x, args.ld, args.nb, x_cols, args.npad,
-                                          static_cast<__nv_bfloat16*>(const_cast<void*>(args.xt)), args.xt_ld);
-  if (args.ksplit > 1) zero_rows_kernel<<<std::min<uint32_t>(ngroups, 1024), 256, 0, st>>>(args.groups, ngroups, args.y, args.ld, args.nb);
+  e = launch_xt_convert(x, args.ld, args.nb, x_cols, args.npad, const_cast<void*>(args.xt), args.xt_ld, st);
+  if (e == cudaSuccess && args.ksplit > 1) e = launch_zero_rows(args.groups, ngroups, args.y, args.ld, args.nb, st);
+  if (e != cudaSuccess) return e;
   tc_gemm_kernel<<<ngroups * args.ksplit, TC_THREADS, smem, st>>>(args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_xt_convert(const float* x, uint32_t ld, uint32_t nb, uint64_t cols, uint32_t npad, void* xt,
+                              uint64_t xt_ld, cudaStream_t st) {
+  const uint64_t total = cols * npad;
+  if (!total) return cudaSuccess;
+  const int cb = int(std::min<uint64_t>((total + 255) / 256, 4096));
+  xt_convert_kernel<<<cb, 256, 0, st>>>(x, ld, nb, cols, npad, static_cast<__nv_bfloat16*>(xt), xt_ld);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero_rows(const TcGroup* groups, uint32_t ngroups, float* y, uint32_t ld, uint32_t nb,
+                             cudaStream_t st) {
+  if (!ngroups) return cudaSuccess;
+  zero_rows_kernel<<<std::min<uint32_t>(ngroups, 1024), 256, 0, st>>>(groups, ngroups, y, ld, nb);
   return cudaGetLastError();
 }
 

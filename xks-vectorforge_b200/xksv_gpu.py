@@ -49,6 +49,8 @@ _SIGS = {
     "xksv_plan_scratch_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
     "xksv_plan_set_scratch": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "xksv_plan_launches": ([ctypes.c_void_p], ctypes.c_int),
+    "xksv_plan_set_gemm_route": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
+    "xksv_plan_fused_ready": ([ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "xksv_plan_index": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "xksv_cuda_sha256": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_void_p,
                           ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
@@ -89,6 +91,10 @@ _SIGS = {
 }
 
 NOALLOC_MAX_SLABS = 4096
+# xksv_plan_set_gemm_route
+GEMM_AUTO, GEMM_SCRATCH, GEMM_FUSED = 0, 1, 2
+# the fused decode -> tensor-core GEMM takes batches up to this size
+FUSED_MAX_BATCH = 128
 # xksv_plan_gemm: batches from this size run on the tensor cores (X rounded
 # to BF16) when the plan has a tensor-core path (xksv_plan_scratch_bytes > 0)
 TC_MIN_BATCH = 4
@@ -287,6 +293,17 @@ class Plan:
         """Lends the plan a caller-owned scratch (xksv_plan_set_scratch)."""
         if self.lib.xksv_plan_set_scratch(self.handle, d_scratch, nbytes):
             raise ValueError("scratch too small or misaligned")
+
+    def set_gemm_route(self, route):
+        """GEMM_AUTO, GEMM_SCRATCH or GEMM_FUSED (xksv_plan_set_gemm_route)."""
+        if self.lib.xksv_plan_set_gemm_route(self.handle, int(route)):
+            raise ValueError(f"unknown GEMM route {route}")
+
+    def fused_ready(self, d_payload):
+        """True when the fused decode -> tensor-core GEMM applies to this
+        plan on d_payload (indexed, all 16-row serial slabs)."""
+        pay = d_payload.data_ptr() if hasattr(d_payload, "data_ptr") else d_payload
+        return bool(self.lib.xksv_plan_fused_ready(self.handle, pay))
 
     def status(self, stream=0):
         """0 when no slab reported an error since the last call, else 1."""
