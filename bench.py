@@ -429,17 +429,57 @@ def fused_gemv(args, dev, stream, threads):
     ref = W @ x[xo:xo + t0["cols"]]
     got = y[yo:yo + t0["rows"]]
     rel = float((got - ref).norm() / ref.norm())
+    del graph
+    # batch 16 on the tensor cores: the fused decode -> tcgen05 kernel against
+    # the decode-to-scratch route (one scratch shared by every plan)
+    nb = 16
+    xb = torch.randn(xs, nb, generator=torch.Generator(device=dev).manual_seed(4), device=dev)
+    yb = torch.empty(ys, nb, device=dev)
+    need = max(pl.scratch_bytes() for pl in plans)
+    scratch = torch.empty(need, dtype=torch.uint8, device=dev)
     for pl in plans:
+        pl.set_scratch(scratch.data_ptr(), need)
+    b16 = dict(batch=nb, fused_ready_plans=sum(pl.fused_ready(d_payload) for pl in plans), plans=len(plans))
+    for route, code in (("fused", xksv_gpu.GEMM_FUSED), ("scratch", xksv_gpu.GEMM_SCRATCH)):
+        for pl in plans:
+            pl.set_gemm_route(code)
+
+        def forward_b():
+            for pl in plans:
+                pl.gemm(d_payload, xb, yb, nb, h)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                forward_b()
+        stream.synchronize()
+        bad += sum(pl.status(h) for pl in plans)
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            forward_b()
+        nl = sum(pl.launches() for pl in plans)
+        with torch.cuda.stream(stream):
+            g2.replay()
+            t2 = time_steps(g2.replay, args.gemv_steps, stream)
+        ms2 = t2 / args.gemv_steps * 1e3
+        bad += sum(pl.status(h) for pl in plans)
+        refb = W @ xb[xo:xo + t0["cols"]].to(torch.bfloat16).float()
+        relb = float((yb[yo:yo + t0["rows"]] - refb).norm() / refb.norm())
+        b16[route] = dict(tok_s=round(nb * 1e3 / ms2, 1), ms_per_forward=round(ms2, 3), launches=nl,
+                          hbm_gbs=round(comp_bytes / (ms2 / 1e3) / 1e9, 1), rel_l2_layer0_down=relb)
+        del g2
+    for pl in plans:
+        pl.set_gemm_route(xksv_gpu.GEMM_AUTO)
         pl.close()
     dplan.close()
-    del graph
+    del scratch
     return dict(metric="fused-GEMV tok/s Llama-8B b=1", value=round(1e3 / ms, 2), unit="tok/s",
                 ms_per_token=round(ms, 4), codec="dfloat11", compressed_bytes=comp_bytes,
                 hbm_gbs=round(comp_bytes / (ms / 1e3) / 1e9, 1), launches_per_token=launches,
                 index_build_s=round(index_s, 3),
                 index_bytes=4 * sum(t["n"] * (t["cols"] // 16 + 1) for t in info),
-                rel_l2_layer0_down=rel, status_errors=bad,
-                note="per token: 128 dependent plan launches (qkv, o, gate+up, down per layer) in one CUDA graph; lm_head excluded as in runtime.py:258")
+                rel_l2_layer0_down=rel, status_errors=bad, batch16=b16,
+                note="per token: 128 dependent plan launches (qkv, o, gate+up, down per layer) in one CUDA graph; "
+                     "lm_head excluded as in runtime.py:258; batch16: the same plans at batch 16 on the tensor cores "
+                     "(fused decode->tcgen05 kernel vs decode to a BF16 scratch + tcgen05 GEMM), X rounded to BF16")
 
 
 def run_case(args):
