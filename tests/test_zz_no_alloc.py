@@ -3,7 +3,9 @@ a library allocate device memory (a server that reserved the whole GPU for
 its own allocator, or code that cannot take cudaMalloc's device-wide
 synchronisation).  It must decode exactly what the plan API decodes, on two
 calls in a row (the calls share one scratch array that keeps the previous
-call's contents), and refuse tables larger than its scratch array.
+call's contents), byte for byte equal to the slabs' source words (what the
+oracle's unpack returns for these slabs) and to the plan API's decode, and
+refuse tables larger than its scratch array.
 
 This file is named to be collected last, so a run that stops at the first
 failure has already run every other test."""
@@ -23,7 +25,7 @@ def _archive(seed):
     shapes = [(16, 2048), (16, 512), (1, 2048), (7, 19), (16, 4097), (33, 35)] * 5
     kinds = ["normal002", "student3", "single", "uniform", "normal1e4", "three_exp"] * 5
     payload = bytearray(b"\x00" * 7)
-    entries, out = [], 0
+    entries, out, source = [], 0, bytearray()
     for i, ((rows, cols), kind) in enumerate(zip(shapes, kinds)):
         raw = words_for(kind, rows * cols, rng).astype("<u2").tobytes()
         codec = [1, 2, 0][i % 3]
@@ -34,7 +36,8 @@ def _archive(seed):
                             dst_offset=out, codec=codec))
         payload += blob + b"\x00" * (i % 3)
         out += len(raw)
-    return bytes(payload), entries, out
+        source += raw
+    return bytes(payload), entries, out, bytes(source)
 
 
 def test_noalloc_matches_plan_decode_twice():
@@ -43,7 +46,7 @@ def test_noalloc_matches_plan_decode_twice():
     lib = xksv_gpu.load()
     stream = torch.cuda.current_stream().cuda_stream
     for seed in (11, 12):  # two calls in a row, different slabs each time
-        payload, entries, out_bytes = _archive(seed)
+        payload, entries, out_bytes, source = _archive(seed)
         d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
         want = torch.full((out_bytes,), 0x5A, dtype=torch.uint8, device="cuda")
         plan = xksv_gpu.Plan(entries)
@@ -55,13 +58,14 @@ def test_noalloc_matches_plan_decode_twice():
         assert lib.xksv_cuda_decode_noalloc(table, n, d_payload.data_ptr(), d_payload.numel(), got.data_ptr(),
                                             got.numel(), stream) == 0
         assert torch.equal(got, want)
+        assert got.cpu().numpy().tobytes() == source
 
 
 def test_noalloc_reports_bad_slab_and_limit():
     import xksv_gpu
     lib = xksv_gpu.load()
     stream = torch.cuda.current_stream().cuda_stream
-    payload, entries, out_bytes = _archive(13)
+    payload, entries, out_bytes, _ = _archive(13)
     bad = bytearray(payload)
     bad[entries[0]["src_offset"] + 8] ^= 1  # first slab (serial): bit count off by one
     d_payload = torch.frombuffer(bad, dtype=torch.uint8).cuda()
