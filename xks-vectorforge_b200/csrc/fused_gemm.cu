@@ -51,11 +51,14 @@ namespace {
 using FCfg = ldec::Cfg<6, 5, 2, 26, 32>;
 using ldec::BR;
 using ldec::SMR;
-constexpr int FR = 2;                           // stage slots per producer warp
-constexpr int FMAXP = 16;                       // producer warps at most
+constexpr int FR = 1;                           // stage slots per producer warp
+constexpr int FMAXP = 19;                       // producer warps at most (20 warps: 5 per SM sub-partition keep 96 registers)
 constexpr int FTHREADS = (FMAXP + 1) * 32;      // + the MMA warp
 constexpr uint32_t kStageBytes = 128 * 16 * 2;  // 128 rows x K 16, BF16
 constexpr size_t kSmemLimit = 232448;           // dynamic shared memory per CTA (227 KB)
+constexpr uint32_t kLensPerArea = FR * kStageBytes / 512;  // length chunks (x 32 lanes) per stage area
+constexpr uint32_t kLensAreas = (17 + kLensPerArea - 1) / kLensPerArea;
+constexpr uint32_t kIdleLimit = 1u << 21;       // MMA-thread polls without progress: about a second
 
 struct FusedShared {
   ldec::Tables<FCfg> T;
@@ -64,6 +67,7 @@ struct FusedShared {
   int maxlen[32];
   uint32_t hb[FMAXP + 1];  // producer warp w decodes half tiles [hb[w], hb[w + 1]) of the segment
   uint32_t mc[FMAXP];      // MMA thread: stages of warp w consumed in earlier segments
+  uint32_t mi[FMAXP];      // MMA thread: stages of warp w issued in this segment
   uint64_t full[FMAXP][FR], empty[FMAXP][FR], done;
   uint32_t tmem_base;
   uint32_t qmask;  // accumulators D_q written by some MMA (a one-half-tile task writes two)
@@ -93,6 +97,18 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity
   return false;
 }
 
+// Non-blocking probe of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
@@ -115,9 +131,10 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
   uint8_t* bring = wr + FR * kStageBytes;                            // [2][npad * 32]
   ldec::Ring ring = reinterpret_cast<ldec::Ring>(bring + 2 * npad * 32);
   ldec::SmRing smring = reinterpret_cast<ldec::SmRing>(bring + 2 * npad * 32 + BR * 32 * 4);
-  // a segment's code lengths are staged in the stage areas of warps 1 and 2
-  const uint4* lens_lo = reinterpret_cast<const uint4*>(smem + kHdrBytes + 1 * warp_bytes(npad));
-  const uint4* lens_hi = reinterpret_cast<const uint4*>(smem + kHdrBytes + 2 * warp_bytes(npad));
+  // a segment's code lengths are staged in the stage areas of warps 1, 2, ..
+  // (kLensPerArea chunks of 32 lanes each)
+  uint8_t* const lens_area = smem + kHdrBytes + 1 * warp_bytes(npad);
+  const uint32_t lens_stride = uint32_t(warp_bytes(npad));
   const bool prod = warp < P;
 
   if (warp == P) {
@@ -185,17 +202,14 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
       smr.init(smring, lane, sm + 128 * uint64_t(ha), sm + 128 * uint64_t(hb));
     }
     // the group's code lengths, as the 17 aligned 16-byte chunks that cover
-    // each slab's, into the stage areas of warps 1 (chunks 0-15, [chunk][lane])
-    // and 2 (chunk 16), idle until decoding starts: one memory round trip
-    if ((warp == 1 || warp == 2) && lane < grp.nslabs) {
+    // each slab's, into the stage areas of warps 1, 2, .. ([chunk][lane] in
+    // each), idle until decoding starts: one memory round trip
+    if (warp >= 1 && warp <= kLensAreas && lane < grp.nslabs) {
       const uintptr_t la = reinterpret_cast<uintptr_t>(a.payload + a.slabs[a.members[grp.m0 + lane]].src + 16);
       const uint8_t* c0 = reinterpret_cast<const uint8_t*>(la & ~uintptr_t(15));
-      if (warp == 1) {
-#pragma unroll
-        for (int c = 0; c < 16; ++c) cp_async16(const_cast<uint4*>(lens_lo) + 32 * c + lane, c0 + 16 * c);
-      } else {
-        cp_async16(const_cast<uint4*>(lens_hi) + lane, c0 + 256);
-      }
+      uint8_t* area = lens_area + (warp - 1) * lens_stride;
+      for (uint32_t c = (warp - 1) * kLensPerArea; c < warp * kLensPerArea && c < 17; ++c)
+        cp_async16(area + ((c - (warp - 1) * kLensPerArea) * 32 + lane) * 16, c0 + 16 * c);
     }
     cp_async_commit();
     if (warp == 0) {  // lut2 starts all zero; the lanes' builds share no row of it
@@ -211,7 +225,7 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
       int mx = 0, tb = 0;
       if (lane < grp.nslabs) {
         const uintptr_t la = reinterpret_cast<uintptr_t>(a.payload + a.slabs[a.members[grp.m0 + lane]].src + 16);
-        ldec::SmemLens lens(lens_lo + lane, lens_hi + lane, la);
+        ldec::SmemLens lens(lens_area + lane * 16, lens_stride, kLensPerArea, la);
         tb = ldec::build_tables<FCfg>(lens, S.T, S.lpos, int(lane), F, mx, L);
       }
       S.F[lane] = F;
@@ -286,23 +300,27 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
       }
       if (active && ok && (bad || b.pos - b.pos0 != b1 - b0)) atomicOr(a.status, kStatusStream);
     } else if (warp == P && lane == 0 && go) {
-      // ---- MMA issue: stage m of every warp in warp order, then m + 1.
-      // Stage m of warp w is half tile h = hb[w] + m / 2, rows 4 (m % 2) ..
-      // of it, i.e. tile rows 4 q .. 4 q + 3 with q = 2 (h % 2) + m % 2 ----
+      // ---- MMA issue: every warp's stages in its own order, the warps
+      // served as their stages become ready.  Stage m of warp w is half tile
+      // h = hb[w] + m / 2, rows 4 (m % 2) .. of it, i.e. tile rows 4 q ..
+      // 4 q + 3 with q = 2 (h % 2) + m % 2 ----
       const uint32_t idesc = umma_idesc_bf16(128, npad);
-      uint32_t maxst = 0;
-      for (uint32_t w = 0; w < P; ++w) maxst = max(maxst, 2 * (S.hb[w + 1] - S.hb[w]));
+      uint32_t left = 0;
+      for (uint32_t w = 0; w < P; ++w) {
+        S.mi[w] = 0;
+        left += 2 * (S.hb[w + 1] - S.hb[w]);
+      }
       uint32_t init = 0;  // D_q written once already
       bool ok = true;
-      for (uint32_t m = 0; m < maxst && ok; ++m) {
+      uint32_t idle = 0;
+      while (left && ok) {
+        bool issued = false;
         for (uint32_t w = 0; w < P; ++w) {
+          const uint32_t m = S.mi[w];
           if (m >= 2 * (S.hb[w + 1] - S.hb[w])) continue;
           const uint32_t mg = S.mc[w] + m;  // the warp's stage count over all segments
           const uint32_t slot = mg % FR;
-          if (!mbar_wait_or_abort(smem_addr(&S.full[w][slot]), (mg / FR) & 1, &S.abort_flag)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_test(smem_addr(&S.full[w][slot]), (mg / FR) & 1)) continue;
           tc_fence_after();
           const uint32_t h = S.hb[w] + (m >> 1);
           const uint32_t q = 2 * (h & 1) + (m & 1), tl = (h >> 1) - (S.hb[w] >> 1);
@@ -312,6 +330,16 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
           umma_bf16(tmem + q * npad, ad, bd, idesc, (init >> q) & 1);
           init |= 1u << q;
           umma_commit(smem_addr(&S.empty[w][slot]));
+          S.mi[w] = m + 1;
+          --left;
+          issued = true;
+        }
+        if (issued) {
+          idle = 0;
+        } else if (++idle > kIdleLimit || S.abort_flag) {
+          ok = false;
+        } else if (idle > 32) {
+          __nanosleep(64);
         }
       }
       for (uint32_t w = 0; w < P; ++w) S.mc[w] += 2 * (S.hb[w + 1] - S.hb[w]);

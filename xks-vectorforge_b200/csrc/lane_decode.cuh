@@ -94,17 +94,20 @@ struct GlobalLens {
   }
 };
 
-// From shared memory: the 17 aligned 16-byte chunks that cover the lengths
-// (chunk c of this lane at chunk(c)), realigned by the lengths' offset in
-// their first chunk.
+// From shared memory: the 17 aligned 16-byte chunks that cover the lengths,
+// chunk c of this lane at chunk(c): areas of `per_area` chunks x 32 lanes,
+// `stride` bytes apart, realigned by the lengths' offset in their first chunk.
 struct SmemLens {
-  const uint4* lo;  // chunks 0..15: lo[32 * c]
-  const uint4* hi;  // chunk 16
-  int q, bs;        // word / bit offset of the first length in chunk 0
+  const uint8_t* base;  // this lane's chunk 0
+  uint32_t stride, per_area;
+  int q, bs;            // word / bit offset of the first length in chunk 0
   int next;
-  __device__ __forceinline__ SmemLens(const uint4* l, const uint4* h, uintptr_t lens_addr)
-      : lo(l), hi(h), q(int((lens_addr >> 2) & 3)), bs(int(lens_addr & 3) * 8), next(0) {}
-  __device__ __forceinline__ uint4 chunk(int c) const { return c < 16 ? lo[32 * c] : *hi; }
+  __device__ __forceinline__ SmemLens(const uint8_t* b, uint32_t s, uint32_t pa, uintptr_t lens_addr)
+      : base(b), stride(s), per_area(pa), q(int((lens_addr >> 2) & 3)), bs(int(lens_addr & 3) * 8), next(0) {}
+  __device__ __forceinline__ uint4 chunk(int c) const {
+    const uint32_t a = uint32_t(c) / per_area, r = uint32_t(c) - a * per_area;
+    return *reinterpret_cast<const uint4*>(base + a * stride + r * 512);
+  }
   __device__ __forceinline__ uint4 at(int c) const {
     const uint4 r0 = chunk(c), r1 = chunk(c + 1);
     uint32_t w0 = r0.x, w1 = r0.y, w2 = r0.z, w3 = r0.w, w4 = r1.x, w5 = r1.y, w6 = r1.z, w7 = r1.w;
