@@ -72,6 +72,7 @@ struct GlobalLens {
   const uint8_t* lens;
   uint32_t (*save)[32];
   int lane;
+  static constexpr bool kZeroLut2 = false;  // the caller zeroes lut2 before the build
   __device__ __forceinline__ GlobalLens(const uint8_t* l, uint32_t (*s)[32], int ln) : lens(l), save(s), lane(ln) {
     rd.init(l, l + 256);
   }
@@ -98,6 +99,7 @@ struct GlobalLens {
 // chunk c of this lane at chunk(c): areas of `per_area` chunks x 32 lanes,
 // `stride` bytes apart, realigned by the lengths' offset in their first chunk.
 struct SmemLens {
+  static constexpr bool kZeroLut2 = false;  // the caller zeroes lut2 before the build
   const uint8_t* base;  // this lane's chunk 0
   uint32_t stride, per_area;
   int q, bs;            // word / bit offset of the first length in chunk 0
@@ -125,6 +127,79 @@ struct SmemLens {
   __device__ __forceinline__ uint4 kept(uint32_t, int c16) const { return at(c16); }
 };
 
+// Staged in the lane's own table memory, idle until the fill pass: chunks
+// 0-7 in the first-level table, 8-15 in the second-level table, 16 in the
+// long-symbol list (each as [chunk][lane] 16-byte cells; stage_lengths()
+// issues the copies).  The first three non-zero chunks are saved in 12 rows of
+// `save` during the count pass, later ones re-read from global memory, since
+// the fill pass overwrites the staging; the build zeroes this lane's column of
+// the second-level table after the count pass.
+template <class C>
+struct TabLens {
+  static constexpr bool kZeroLut2 = true;
+  const uint4* lo;  // chunks 0-7: lo[32 * c]
+  const uint4* mid; // chunks 8-15
+  const uint4* hi;  // chunk 16
+  const uint8_t* lens;
+  uint32_t (*save)[32];
+  int lane, q, bs, next;
+  __device__ __forceinline__ TabLens(Tables<C>& T, const uint8_t* l, uint32_t (*s)[32], int ln)
+      : lo(reinterpret_cast<const uint4*>(&T.lut[0][0]) + ln),
+        mid(reinterpret_cast<const uint4*>(&T.lut2[0][0]) + ln),
+        hi(reinterpret_cast<const uint4*>(&T.lsym[0][0]) + ln),
+        lens(l), save(s), lane(ln),
+        q(int((reinterpret_cast<uintptr_t>(l) >> 2) & 3)), bs(int(reinterpret_cast<uintptr_t>(l) & 3) * 8), next(0) {}
+  __device__ __forceinline__ uint4 chunk(int c) const { return c < 8 ? lo[32 * c] : c < 16 ? mid[32 * (c - 8)] : *hi; }
+  __device__ __forceinline__ uint4 take() {
+    const uint4 r0 = chunk(next), r1 = chunk(next + 1);
+    ++next;
+    uint32_t w0 = r0.x, w1 = r0.y, w2 = r0.z, w3 = r0.w, w4 = r1.x, w5 = r1.y, w6 = r1.z, w7 = r1.w;
+    if (q & 2) {
+      w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
+    }
+    if (q & 1) {
+      w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
+    }
+    return make_uint4(__funnelshift_r(w0, w1, bs), __funnelshift_r(w1, w2, bs), __funnelshift_r(w2, w3, bs),
+                      __funnelshift_r(w3, w4, bs));
+  }
+  __device__ __forceinline__ void keep(uint32_t k, const uint4& v) {
+    if (k < 3) {
+      const int r = 4 * int(k);
+      save[r][lane] = v.x;
+      save[r + 1][lane] = v.y;
+      save[r + 2][lane] = v.z;
+      save[r + 3][lane] = v.w;
+    }
+  }
+  __device__ __forceinline__ uint4 kept(uint32_t k, int c16) const {
+    if (k < 3) {
+      const int r = 4 * int(k);
+      return make_uint4(save[r][lane], save[r + 1][lane], save[r + 2][lane], save[r + 3][lane]);
+    }
+    return ld16_any(lens + 16 * c16);
+  }
+};
+
+// Issues the cp.async copies TabLens reads: the aligned 16-byte chunks that
+// hold the 256 code lengths at `lens` (the 17th only when the lengths are not
+// 16-byte aligned, so every chunk read holds a length byte).
+template <class C>
+__device__ __forceinline__ void stage_lengths(Tables<C>& T, const uint8_t* lens, int lane) {
+  static_assert(sizeof(T.lut) >= 8 * 512 && sizeof(T.lut2) >= 8 * 512 && sizeof(T.lsym) >= 512,
+                "the tables hold the 17 staged chunks");
+  static_assert(offsetof(Tables<C>, lut2) % 16 == 0 && offsetof(Tables<C>, lsym) % 16 == 0, "16-byte cells");
+  const uintptr_t a = reinterpret_cast<uintptr_t>(lens);
+  const uint8_t* c0 = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(15));
+  uint4* lo = reinterpret_cast<uint4*>(&T.lut[0][0]) + lane;
+  uint4* mid = reinterpret_cast<uint4*>(&T.lut2[0][0]) + lane;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) cp_async16(lo + 32 * c, c0 + 16 * c);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) cp_async16(mid + 32 * c, c0 + 128 + 16 * c);
+  if (a & 15) cp_async16(reinterpret_cast<uint4*>(&T.lsym[0][0]) + lane, c0 + 256);
+}
+
 // Builds lane `lane`'s tables from its 256 code lengths (read through `rd`).
 // Returns 0 when built, 1 when the codebook does not fit them (a length
 // above PK+PNL or more than PLONG long codes), -1 when the lengths are
@@ -132,7 +207,8 @@ struct SmemLens {
 // non-zero length bytes are visited (a codebook uses a few dozen symbols at
 // most).  Short-length counters and fill cursors are 8-bit fields of two
 // registers (lengths 1-4 | 5-6); a field that wraps (256 codes of one
-// length) shows as a count mismatch.  The caller zeroes lut2 first.
+// length) shows as a count mismatch.  lut2 starts all zero: zeroed by the
+// caller before the build, or here after the count pass (R::kZeroLut2).
 template <class C, class R>
 __device__ int build_tables(R& rd, Tables<C>& T, uint8_t (*lpos)[32], int lane, uint32_t& F, int& maxlen,
                             uint32_t& Lout) {
@@ -200,6 +276,9 @@ __device__ int build_tables(R& rd, Tables<C>& T, uint8_t (*lpos)[32], int lane, 
   }
   if (maxlen > PK && used > (1ull << maxlen)) return -1;
   F = L << 1;
+  if (R::kZeroLut2) {  // the second level held staged lengths until now
+    for (int r = 0; r < C::NROW2; ++r) T.lut2[r][lane] = 0;
+  }
   // fill pass over the non-zero chunks again
   uint32_t k = 0;
   while (nz) {
@@ -235,7 +314,7 @@ __device__ int build_tables(R& rd, Tables<C>& T, uint8_t (*lpos)[32], int lane, 
   }
   // rows past the short codes: prefixes of long codes or unused code space
   for (uint32_t z = L; z < (1u << PK); ++z) T.lut[z][lane] = 0;
-  // second level (zeroed by the caller before the build): codes of length
+  // second level (zeroed before the fill): codes of length
   // PK+1..PK+K2 whose (PK+K2)-bit prefixes fall in the first NE escape prefixes
   uint32_t cf = F, idx = 0;
   const uint32_t base = L << K2;

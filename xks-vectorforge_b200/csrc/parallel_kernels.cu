@@ -267,18 +267,22 @@ __global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 8 : 1)
       if (uint64_t(lane) * 128 < (nsize < 288 ? nsize : 288)) prefetch_l2(np + 128 * lane);
       if (40 + 8 * uint64_t(lane) <= nsize) nlen = ld8_any(np + 32 + 8 * lane, np + nsize);
     }
-    // ---- container header (cuda/parallel.cu:34-36) ----
+    // ---- container header (cuda/parallel.cu:34-36) and, in the same round
+    // trip, this lane's substream-table entry (read when it lies inside the
+    // slab; the header checks below decide whether it is one) ----
     bool ok = n >= 32;
-    uint64_t rows = 0, cols = 0, chunks = 0;
+    uint64_t rows = 0, cols = 0, chunks = 0, entry = 0;
     if (ok) {
       // header fields through aligned 8-byte loads (the slab may sit at any
       // byte offset; n >= 32 keeps every read inside the slab's words)
       const uint8_t* pe = p + n;
-      ok = ld8_any(p, pe) == 0x0000003250534B58ull;  // "XKSP2\0\0\0"
+      const uint64_t magic = ld8_any(p, pe);
       rows = ld8_any(p + 8, pe);
       cols = ld8_any(p + 16, pe);
       chunks = ld8_any(p + 24, pe);
-      ok = ok && rows && rows <= 16 && cols && chunks && chunks <= 32 &&
+      if (40 + 8 * uint64_t(lane) <= n) entry = ld8_any(p + 32 + 8 * lane, pe);
+      ok = magic == 0x0000003250534B58ull &&  // "XKSP2\0\0\0"
+           rows && rows <= 16 && cols && chunks && chunks <= 32 &&
            cols <= ~0ull / rows && chunks <= rows * cols && rows * cols <= n &&
            rows * cols <= ~0ull / 32 && n >= 32 + 8 * chunks && rows == sd.rows &&
            cols == sd.cols;
@@ -294,38 +298,10 @@ __global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 8 : 1)
     // ---- substream table (cuda/parallel.cu:39-51) ----
     const uint32_t total = uint32_t(rows * cols);
     const bool active = uint64_t(lane) < chunks;
-    const uint64_t len = active ? ld8_any(p + 32 + 8 * lane, p + n) : 0;
+    const uint64_t len = active ? entry : 0;  // n >= 32 + 8 * chunks: every active entry was read
     bool lok = !active || (len >= kHdr && len <= n);
     const uint64_t incl = warp_incl_scan(lok ? len : 0, lane);
     const uint64_t base = 32 + 8 * chunks + incl - len;
-    Seg s{};
-    if (active && lok) {
-      lok = base + len <= n;
-      if (lok) {
-        const uint8_t* q = p + base;
-        const uint64_t count = ld8_any(q, p + n);
-        s.nbits = ld8_any(q + 8, p + n);
-        s.start = uint32_t(uint64_t(total) * uint64_t(lane) / chunks);
-        const uint64_t expect = uint64_t(total) * uint64_t(lane + 1) / chunks - s.start;
-        s.ebytes = s.nbits / 8 + (s.nbits % 8 != 0);
-        lok = count == expect && count <= len - kHdr && s.ebytes == len - kHdr - count;
-        s.count = uint32_t(count);
-        s.lens = q + 16;
-        s.sm = q + kHdr;
-        s.bits = q + kHdr + count;
-      }
-    }
-    const uint64_t end_all = __shfl_sync(0xffffffffu, base + len, int(chunks - 1));
-    if (!(__all_sync(0xffffffffu, lok) && end_all == n)) {
-      if (lane == 0) atomicOr(status, kStatusHeader);
-      continue;
-    }
-    // bit positions are 32-bit (the slab format bounds them far lower: a
-    // substream's bits fit in its slab, and compiled slabs are <= 1 MiB)
-    if (__any_sync(0xffffffffu, s.nbits >= (1ull << 32) - 256)) {
-      if (lane == 0) atomicOr(status, kStatusInternal);
-      continue;
-    }
     Out o;
     o.out = reinterpret_cast<uint16_t*>(out + sd.dst);
     o.x = MODE == 1 ? x + sd.xoff * ld : nullptr;
@@ -338,29 +314,61 @@ __global__ void __launch_bounds__(PWARPS * 32, MODE == 0 ? 8 : 1)
     o.out32 = (reinterpret_cast<uintptr_t>(o.out) & 31) == 0;
     const bool nice = rows == 16 && (cols & 15) == 0 &&
                       (MODE == 1 || (reinterpret_cast<uintptr_t>(o.out) & 15) == 0);
+    Seg s{};
+    s.start = uint32_t(uint64_t(total) * uint64_t(lane) / chunks);
+    const uint64_t expect = uint64_t(total) * uint64_t(lane + 1) / chunks - s.start;
     const bool rows16 = nice && (s.start & 15) == 0;
-    // ---- first bit and sign/mantissa loads, overlapping the table build ----
     ldec::Stream b;
     ldec::SmStream smr;
-    if (active) {
-      b.start(s.bits, s.ebytes);
-      if (rows16) smr.init(W.smring, lane, s.sm, s.sm + s.count);
+    if (active && lok) {
+      lok = base + len <= n;
+      if (lok) {
+        const uint8_t* q = p + base;
+        // one round trip for the substream's header, its code lengths (into
+        // the warp's table memory, idle until the fill pass) and its first
+        // sign/mantissa chunks (the substream holds `expect` of them when
+        // the slab is well formed; the copies stay inside the slab anyway)
+        ldec::stage_lengths<PCfg>(W.t, q + 16, lane);
+        if (rows16) {
+          const uint8_t* sm = q + kHdr;
+          const uint8_t* sme = sm + expect <= p + n ? sm + expect : p + n;
+          smr.init(W.smring, lane, sm, sme > sm ? sme : sm + 1);
+        }
+        const uint64_t count = ld8_any(q, p + n);
+        s.nbits = ld8_any(q + 8, p + n);
+        s.ebytes = s.nbits / 8 + (s.nbits % 8 != 0);
+        lok = count == expect && count <= len - kHdr && s.ebytes == len - kHdr - count;
+        s.count = uint32_t(count);
+        s.lens = q + 16;
+        s.sm = q + kHdr;
+        s.bits = q + kHdr + count;
+      }
     }
     cp_async_commit();
-    // ---- per-lane tables ----
-    // the second-level table starts all zero: 16-byte stores by the warp
-    {
-      using Tabs = ldec::Tables<PCfg>;
-      static_assert(sizeof(Tabs::lut2) % 16 == 0 && offsetof(Tabs, lut2) % 16 == 0, "lut2 as uint4");
-      uint4* z = reinterpret_cast<uint4*>(&W.t.lut2[0][0]);
-      for (uint32_t k = lane; k < sizeof(Tabs::lut2) / 16; k += 32) z[k] = make_uint4(0, 0, 0, 0);
+    const uint64_t end_all = __shfl_sync(0xffffffffu, base + len, int(chunks - 1));
+    if (!(__all_sync(0xffffffffu, lok) && end_all == n)) {
+      cp_async_wait_all();
       __syncwarp();
+      if (lane == 0) atomicOr(status, kStatusHeader);
+      continue;
     }
+    // bit positions are 32-bit (the slab format bounds them far lower: a
+    // substream's bits fit in its slab, and compiled slabs are <= 1 MiB)
+    if (__any_sync(0xffffffffu, s.nbits >= (1ull << 32) - 256)) {
+      cp_async_wait_all();
+      __syncwarp();
+      if (lane == 0) atomicOr(status, kStatusInternal);
+      continue;
+    }
+    // ---- first bit loads, overlapping the table build ----
+    if (active) b.start(s.bits, s.ebytes);
+    // ---- per-lane tables, from the staged lengths ----
+    cp_async_wait_all();
     ldec::Code lc{0, 0, 0};
     uint32_t L = 0;
     int tb = 0;
     if (active) {
-      ldec::GlobalLens lens(s.lens, &W.ring[kSaveChunk], lane);
+      ldec::TabLens<PCfg> lens(W.t, s.lens, &W.ring[kSaveChunk], lane);
       tb = ldec::build_tables<PCfg>(lens, W.t, W.lpos, lane, lc.F, lc.maxlen, L);
     }
     lc.L2 = L << PCfg::K2;
