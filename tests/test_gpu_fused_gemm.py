@@ -111,18 +111,22 @@ def test_fused_gemm_long_slabs(xg):
     plan.close()
 
 
-def test_fused_gemm_reports_bad_codebook(xg):
-    """Code lengths corrupted after the index was built (same payload
-    pointer): the fused kernel's table build rejects them, the CTA aborts
-    without issuing an MMA and the plan reports the error."""
-    payload, entries, ws, xn, yn = archive(xg, [(64, 1024, 0)], seed=9)
+def test_fused_gemm_reports_bad_stream(xg):
+    """A bit stream changed after the index was built (same payload pointer;
+    the index and the lane tables describe the old contents): a one-symbol
+    codebook (code 0) meets 1 bits, which no code starts with; the fused kernel
+    reports the stream error."""
+    payload, entries, ws, xn, yn = archive(xg, [(64, 1024, 0)], seed=9, dist="single")
     d_payload = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
     plan = xg.Plan(entries)
     assert plan.index(d_payload) == 0 and plan.fused_ready(d_payload)
-    o = entries[1]["src_offset"]
-    d_payload[o + 16:o + 20] = torch.tensor([1, 1, 1, 1], dtype=torch.uint8, device="cuda")
     x = torch.randn(xn, 16, device="cuda")
     y = torch.empty(yn, 16, device="cuda")
+    plan.gemm(d_payload, x, y, 16)
+    assert plan.status() == 0
+    e = entries[1]
+    bits = e["src_offset"] + 272 + e["rows"] * e["cols"]  # header + lengths, sign/mantissa bytes, then bits
+    d_payload[bits:bits + 8] = 0xFF
     plan.gemm(d_payload, x, y, 16)
     assert plan.status() == 1
     plan.close()

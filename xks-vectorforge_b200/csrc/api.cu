@@ -218,6 +218,7 @@ struct xksv_plan {
   xksv::FusedTask* d_ftasks = nullptr;
   xksv::FusedGroup* d_fgroups = nullptr;
   uint32_t* d_fmembers = nullptr;
+  void* d_ftabs = nullptr;  // per group: its lane tables, built with the index
   uint64_t* d_hash_ranges = nullptr;  // per slab in creation order: {dst, decoded bytes}
   // xksv_plan_decode_host: copy stream and per-chunk events (created on first use)
   cudaStream_t copy_st = nullptr;
@@ -236,6 +237,8 @@ void free_index(xksv_plan* p) {
   if (p->d_ftasks) cudaFree(p->d_ftasks);
   if (p->d_fgroups) cudaFree(p->d_fgroups);
   if (p->d_fmembers) cudaFree(p->d_fmembers);
+  if (p->d_ftabs) cudaFree(p->d_ftabs);
+  p->d_ftabs = nullptr;
   p->d_fseg0 = nullptr;
   p->d_ftasks = nullptr;
   p->d_fgroups = nullptr;
@@ -777,6 +780,7 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, size_t payload_si
     f.tbase = p->d_tbase;
     f.tidx = p->d_tidx;
     f.tmid = p->d_tmid;
+    f.tabs = p->d_ftabs;
     f.payload = pay;
     f.xt = p->d_xt;
     f.xt_ld = p->x_cols;
@@ -943,8 +947,9 @@ int xksv_plan_sha256(const xksv_plan* p, const void* d_out, size_t out_size, voi
 
 // After a successful index: the fused decode -> tensor-core GEMM applies
 // when every slab of the plan is on the tile path, the plan has a
-// tensor-core path and every codebook fits the fused decoder's tables.  Any
-// failure here only leaves the fused route off.
+// tensor-core path and every codebook fits the fused decoder's tables; each
+// group's lane tables are built here, once.  Any failure here only leaves
+// the fused route off.
 static void setup_fused(xksv_plan* p, const uint8_t* d_payload, cudaStream_t st) {
   const uint32_t n = p->n_ser + p->n_par + p->n_raw;
   if (!p->tc_ok || !n || p->n_ser_idx != n) return;
@@ -975,13 +980,22 @@ static void setup_fused(xksv_plan* p, const uint8_t* d_payload, cudaStream_t st)
                          st) == cudaSuccess &&
          cudaMemcpyAsync(p->d_fmembers, members.data(), members.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
                          st) == cudaSuccess &&
-         cudaStreamSynchronize(st) == cudaSuccess;
+         cudaMalloc(&p->d_ftabs, groups.size() * fused_tables_bytes()) == cudaSuccess &&
+         cudaMemsetAsync(p->d_status, 0, sizeof(int), st) == cudaSuccess &&
+         launch_fused_tables(p->d_fgroups, uint32_t(groups.size()), p->d_fmembers, p->d_slabs, d_payload, p->d_ftabs,
+                             p->d_status, st) == cudaSuccess &&
+         cudaMemcpyAsync(p->h_status, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+         cudaStreamSynchronize(st) == cudaSuccess && *p->h_status == 0;
+  cudaMemsetAsync(p->d_status, 0, sizeof(int), st);
+  cudaStreamSynchronize(st);
   if (!good) {
     if (p->d_fseg0) cudaFree(p->d_fseg0);
     p->d_fseg0 = nullptr;
     if (p->d_ftasks) cudaFree(p->d_ftasks);
     if (p->d_fgroups) cudaFree(p->d_fgroups);
     if (p->d_fmembers) cudaFree(p->d_fmembers);
+    if (p->d_ftabs) cudaFree(p->d_ftabs);
+    p->d_ftabs = nullptr;
     p->d_ftasks = nullptr;
     p->d_fgroups = nullptr;
     p->d_fmembers = nullptr;

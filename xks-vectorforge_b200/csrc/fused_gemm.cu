@@ -56,15 +56,20 @@ constexpr int FMAXP = 19;                       // producer warps at most (20 wa
 constexpr int FTHREADS = (FMAXP + 1) * 32;      // + the MMA warp
 constexpr uint32_t kStageBytes = 128 * 16 * 2;  // 128 rows x K 16, BF16
 constexpr size_t kSmemLimit = 232448;           // dynamic shared memory per CTA (227 KB)
-constexpr uint32_t kLensPerArea = FR * kStageBytes / 512;  // length chunks (x 32 lanes) per stage area
-constexpr uint32_t kLensAreas = (17 + kLensPerArea - 1) / kLensPerArea;
 constexpr uint32_t kIdleLimit = 1u << 21;       // MMA-thread polls without progress: about a second
 
-struct FusedShared {
+// A group's lane tables (lane j: slab j), built once per plan when the tile
+// index is built (fused_tables_kernel) and copied into each CTA's shared
+// memory at its start.
+struct FusedTabs {
   ldec::Tables<FCfg> T;
-  uint8_t lpos[FCfg::PNL][32];
   uint32_t F[32], L2[32];
   int maxlen[32];
+};
+static_assert(sizeof(FusedTabs) % 16 == 0, "copied as 16-byte chunks");
+
+struct FusedShared {
+  FusedTabs tabs;
   uint32_t hb[FMAXP + 1];  // producer warp w decodes half tiles [hb[w], hb[w + 1]) of the segment
   uint32_t mc[FMAXP];      // MMA thread: stages of warp w consumed in earlier segments
   uint32_t mi[FMAXP];      // MMA thread: stages of warp w issued in this segment
@@ -131,10 +136,6 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
   uint8_t* bring = wr + FR * kStageBytes;                            // [2][npad * 32]
   ldec::Ring ring = reinterpret_cast<ldec::Ring>(bring + 2 * npad * 32);
   ldec::SmRing smring = reinterpret_cast<ldec::SmRing>(bring + 2 * npad * 32 + BR * 32 * 4);
-  // a segment's code lengths are staged in the stage areas of warps 1, 2, ..
-  // (kLensPerArea chunks of 32 lanes each)
-  uint8_t* const lens_area = smem + kHdrBytes + 1 * warp_bytes(npad);
-  const uint32_t lens_stride = uint32_t(warp_bytes(npad));
   const bool prod = warp < P;
 
   if (warp == P) {
@@ -201,41 +202,14 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
       // a half tile's 128 sign/mantissa bytes follow the previous half's
       smr.init(smring, lane, sm + 128 * uint64_t(ha), sm + 128 * uint64_t(hb));
     }
-    // the group's code lengths, as the 17 aligned 16-byte chunks that cover
-    // each slab's, into the stage areas of warps 1, 2, .. ([chunk][lane] in
-    // each), idle until decoding starts: one memory round trip
-    if (warp >= 1 && warp <= kLensAreas && lane < grp.nslabs) {
-      const uintptr_t la = reinterpret_cast<uintptr_t>(a.payload + a.slabs[a.members[grp.m0 + lane]].src + 16);
-      const uint8_t* c0 = reinterpret_cast<const uint8_t*>(la & ~uintptr_t(15));
-      uint8_t* area = lens_area + (warp - 1) * lens_stride;
-      for (uint32_t c = (warp - 1) * kLensPerArea; c < warp * kLensPerArea && c < 17; ++c)
-        cp_async16(area + ((c - (warp - 1) * kLensPerArea) * 32 + lane) * 16, c0 + 16 * c);
+    // the group's lane tables, built when the index was: one round trip
+    {
+      const uint4* src = static_cast<const uint4*>(a.tabs) + size_t(task.group) * (sizeof(FusedTabs) / 16);
+      uint4* dst = reinterpret_cast<uint4*>(&S.tabs);
+      for (uint32_t i = threadIdx.x; i < sizeof(FusedTabs) / 16; i += blockDim.x) cp_async16(dst + i, src + i);
     }
     cp_async_commit();
-    if (warp == 0) {  // lut2 starts all zero; the lanes' builds share no row of it
-      uint4* z = reinterpret_cast<uint4*>(&S.T.lut2[0][0]);
-      static_assert(sizeof(S.T.lut2) % 16 == 0 && offsetof(ldec::Tables<FCfg>, lut2) % 16 == 0, "lut2 as uint4");
-      for (uint32_t k = lane; k < sizeof(S.T.lut2) / 16; k += 32) z[k] = make_uint4(0, 0, 0, 0);
-    }
     cp_async_wait_all();
-    __syncthreads();
-    // ---- warp 0: the group's tables, lane j for slab j ----
-    if (warp == 0) {
-      uint32_t F = 0, L = 0;
-      int mx = 0, tb = 0;
-      if (lane < grp.nslabs) {
-        const uintptr_t la = reinterpret_cast<uintptr_t>(a.payload + a.slabs[a.members[grp.m0 + lane]].src + 16);
-        ldec::SmemLens lens(lens_area + lane * 16, lens_stride, kLensPerArea, la);
-        tb = ldec::build_tables<FCfg>(lens, S.T, S.lpos, int(lane), F, mx, L);
-      }
-      S.F[lane] = F;
-      S.L2[lane] = L << FCfg::K2;
-      S.maxlen[lane] = mx;
-      if (tb != 0) {
-        atomicOr(a.status, tb < 0 ? kStatusCodebook : kStatusInternal);
-        S.abort_flag = 1;
-      }
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -246,7 +220,7 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
 
     if (prod && go && ha < hb) {
       // ---- decode tile rows into the stage ring ----
-      const ldec::Code lc{S.F[lane], S.L2[lane], S.maxlen[lane]};
+      const ldec::Code lc{S.tabs.F[lane], S.tabs.L2[lane], S.tabs.maxlen[lane]};
       if (active) b.init_ring(ring, int(lane));
       load_b(ha >> 1, 0);  // later tiles' slices are loaded eight rows ahead
       bool bad = false, ok = true;
@@ -264,7 +238,7 @@ __global__ void __launch_bounds__(FTHREADS, 1) fused_gemm_kernel(FusedArgs a, ui
             uint32_t e[16];
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              ldec::dec4<FCfg>(b, ring, S.T, int(lane), lc, bad, e[4 * q], e[4 * q + 1], e[4 * q + 2], e[4 * q + 3]);
+              ldec::dec4<FCfg>(b, ring, S.tabs.T, int(lane), lc, bad, e[4 * q], e[4 * q + 1], e[4 * q + 2], e[4 * q + 3]);
             ldec::merge16(e, s16, v0, v1);
           }
           const uint32_t slot = gm % FR;
@@ -411,6 +385,38 @@ __global__ void fused_prep_kernel(const float* __restrict__ x, uint32_t ld, uint
   }
 }
 
+// One warp per group: lane j builds slab j's tables (the codes of its 256
+// lengths, read from the payload) and the warp writes the group's FusedTabs.
+// A lane whose codebook does not fit or is oversubscribed sets the status.
+__global__ void __launch_bounds__(32) fused_tables_kernel(const FusedGroup* __restrict__ groups,
+                                                          const uint32_t* __restrict__ members,
+                                                          const Slab* __restrict__ slabs,
+                                                          const uint8_t* __restrict__ payload, FusedTabs* tabs,
+                                                          int* status) {
+  __shared__ __align__(16) FusedTabs t;
+  __shared__ uint8_t lpos[FCfg::PNL][32];
+  __shared__ uint32_t save[12][32];
+  const int lane = threadIdx.x;
+  const FusedGroup g = groups[blockIdx.x];
+  uint4* z = reinterpret_cast<uint4*>(&t.T.lut2[0][0]);
+  for (uint32_t k = lane; k < sizeof(t.T.lut2) / 16; k += 32) z[k] = make_uint4(0, 0, 0, 0);
+  __syncwarp();
+  uint32_t F = 0, L = 0;
+  int mx = 0, tb = 0;
+  if (uint32_t(lane) < g.nslabs) {
+    ldec::GlobalLens lens(payload + slabs[members[g.m0 + lane]].src + 16, save, lane);
+    tb = ldec::build_tables<FCfg>(lens, t.T, lpos, lane, F, mx, L);
+  }
+  t.F[lane] = F;
+  t.L2[lane] = L << FCfg::K2;
+  t.maxlen[lane] = mx;
+  if (tb != 0) atomicOr(status, tb < 0 ? kStatusCodebook : kStatusInternal);
+  __syncwarp();
+  const uint4* src = reinterpret_cast<const uint4*>(&t);
+  uint4* dst = reinterpret_cast<uint4*>(tabs + blockIdx.x);
+  for (uint32_t i = lane; i < sizeof(FusedTabs) / 16; i += 32) dst[i] = src[i];
+}
+
 // ok[i] = 1 when slab i's codebook fits the fused decoder's lane tables
 // (lengths <= PK + PNL, at most PLONG codes longer than PK).
 __global__ void fused_check_kernel(const Slab* __restrict__ slabs, uint32_t n, const uint8_t* __restrict__ payload,
@@ -436,6 +442,16 @@ uint32_t fused_producers(uint32_t npad, size_t* smem_bytes) {
   if (p < 4) return 0;  // the epilogue needs warps 0-3
   if (smem_bytes) *smem_bytes = kHdrBytes + p * per;
   return p;
+}
+
+size_t fused_tables_bytes() { return sizeof(FusedTabs); }
+
+cudaError_t launch_fused_tables(const FusedGroup* groups, uint32_t ngroups, const uint32_t* members,
+                                const Slab* slabs, const uint8_t* payload, void* tabs, int* status,
+                                cudaStream_t st) {
+  if (!ngroups) return cudaSuccess;
+  fused_tables_kernel<<<ngroups, 32, 0, st>>>(groups, members, slabs, payload, static_cast<FusedTabs*>(tabs), status);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_fused_check(const Slab* slabs, uint32_t n, const uint8_t* payload, uint8_t* ok,

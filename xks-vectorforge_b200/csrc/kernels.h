@@ -123,6 +123,7 @@ struct FusedArgs {
   const uint64_t* tbase;
   const uint32_t* tidx;
   const uint32_t* tmid;  // row-8 offsets of the tiles
+  const void* tabs;      // per group: its lane tables (launch_fused_tables)
   const uint8_t* payload;
   const void* xt;        // BF16 X^T [npad][xt_ld]
   uint64_t xt_ld;
@@ -133,6 +134,12 @@ struct FusedArgs {
 // Producer warps and dynamic shared memory for a batch pass of npad columns
 // (16 <= npad <= 128, a multiple of 16); 0 producers when it does not fit.
 uint32_t fused_producers(uint32_t npad, size_t* smem_bytes);
+// Bytes of one group's lane tables, and their build (one warp per group, at
+// index time; a codebook that does not fit sets the status word).
+size_t fused_tables_bytes();
+cudaError_t launch_fused_tables(const FusedGroup* groups, uint32_t ngroups, const uint32_t* members,
+                                const Slab* slabs, const uint8_t* payload, void* tabs, int* status,
+                                cudaStream_t st);
 // The codebook of every slab fits the fused decoder's lane tables: ok[i] = 1.
 cudaError_t launch_fused_check(const Slab* slabs, uint32_t n, const uint8_t* payload, uint8_t* ok,
                                cudaStream_t st);
