@@ -31,6 +31,7 @@
 #include <atomic>
 
 #include "kernels.h"
+#include "tcgen05.cuh"
 #include "xksv_device.cuh"
 
 namespace xksv {
@@ -676,7 +677,7 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
 constexpr int GT = 256;                  // threads (tiles) per GEMV CTA
 constexpr int GPAD = 160;                // zero words past a round: one row of 16 maximal codes + window
 constexpr int GWINW = 6144 + GPAD;       // staged bit words per round
-constexpr uint32_t GCAP = uint32_t(GWINW - GPAD - 1) * 32;  // bits per round
+constexpr uint32_t GCAP = uint32_t(GWINW - GPAD - 9) * 32;  // bits per round (+ up to 4 words of alignment)
 constexpr int GNB = 4;                   // batch columns per pass
 
 struct GemvShared {
@@ -811,25 +812,26 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
         if (t == 0) atomicOr(a.status, kStatusInternal);
         break;
       }
-      const uint32_t nw = (end_bit - base_bit + 31) / 32 + GPAD;
-      for (uint32_t j = t; j < nw; j += GT) {
-        const uint8_t* q = bits + (base_bit >> 3) + 4 * j;
-        uint32_t v = 0;
-        if (q < end) {
-          const uintptr_t qa = reinterpret_cast<uintptr_t>(q);
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
-          const int sh = int(qa & 3) * 8;
-          const uint32_t lo = __ldg(qw);
-          const uint32_t hi =
-              (sh && reinterpret_cast<const uint8_t*>(qw + 1) < end) ? __ldg(qw + 1) : 0u;
-          v = bswap32(sh ? __funnelshift_r(lo, hi, sh) : lo);
-        }
-        S.win[j] = v;
+      // the round's bits as the 16-byte aligned chunks that hold them: one
+      // round trip of cp.async (bytes past the slab read as zero), then every
+      // word byte-swapped in place into the window's big-endian words
+      const uintptr_t qa = reinterpret_cast<uintptr_t>(bits + (base_bit >> 3));
+      const uint8_t* qc = reinterpret_cast<const uint8_t*>(qa & ~uintptr_t(15));
+      const uint32_t slack = uint32_t(qa & 15) * 8;  // staged bits before the round's first bit
+      const uint32_t nc = ((end_bit - base_bit + slack + 31) / 32 + GPAD + 3) / 4;
+      for (uint32_t c = t; c < nc; c += GT) {
+        const uint8_t* src = qc + 16 * c;
+        const uint32_t valid = src >= end ? 0u : end - src >= 16 ? 16u : uint32_t(end - src);
+        cp_async16_zfill(smem_addr(&S.win[4 * c]), valid ? src : qc, valid);
       }
+      cp_async_commit();
+      cp_async_wait_all();
+      __syncthreads();
+      for (uint32_t j = t; j < 4 * nc; j += GT) S.win[j] = bswap32(S.win[j]);
       __syncthreads();
       bool act = mine && uint32_t(t) >= ta && uint32_t(t) < tb && b0 >= base_bit && b1 >= b0;
       SmemWin96 r;
-      r.init(S.win, act ? b0 - base_bit : 0u);
+      r.init(S.win, act ? b0 - base_bit + slack : 0u);
       bool dead = false;
       // sign/mantissa rows loaded one row ahead of use
       uint4 nlo = ldg16(sq), nhi = soff ? ldg16(sq + 1) : make_uint4(0, 0, 0, 0);
@@ -842,7 +844,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
 #pragma unroll
         for (int b = 0; b < NB; ++b) acc[b] = 0.f;
         // a row starts inside the staged bits: its 16 codes stay inside GPAD
-        if (act && r.pos() > b1 - base_bit) {
+        if (act && r.pos() > b1 - base_bit + slack) {
           atomicOr(a.status, kStatusStream);
           act = false;
         }
