@@ -756,13 +756,6 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
       for (uint64_t off = pb0 + uint64_t(t) * 128; off < pb1; off += uint64_t(GT) * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(bp + off));
     }
-    if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
-      if (t == 0) atomicOr(a.status, kStatusCodebook);
-      __syncthreads();
-      continue;
-    }
-    if (NB > 0)
-      for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
     const uint32_t* ti = a.tidx + a.tbase[it.slab];
     const uint8_t* sm = p + kHdr;
     const uint8_t* bits = sm + count;
@@ -770,6 +763,51 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const bool mine = uint32_t(t) < it.ntiles;
     const uint32_t tile = it.tile0 + uint32_t(mine ? t : 0);
     const uint32_t b0 = ti[tile], b1 = ti[tile + 1];
+    // A round: the tiles [ta, tb) whose bits fit the window, staged as the
+    // 16-byte aligned chunks that hold them by cp.async (bytes past the slab
+    // read as zero); the first round's copies overlap the table build.
+    struct Round {
+      uint32_t tb, base_bit, slack;
+      bool ok;
+    };
+    auto issue_round = [&](uint32_t ta) {
+      Round rd;
+      rd.base_bit = ti[it.tile0 + ta] & ~31u;
+      const bool fits = mine && uint32_t(t) >= ta && b1 - rd.base_bit <= GCAP;
+      rd.tb = ta + uint32_t(__syncthreads_count(fits));
+      const uint32_t end_bit = ti[it.tile0 + rd.tb];
+      // an index that does not describe this payload fails here (uniformly)
+      rd.ok = !(rd.tb == ta || end_bit < rd.base_bit || end_bit - rd.base_bit > GCAP);
+      const uintptr_t qa = reinterpret_cast<uintptr_t>(bits + (rd.base_bit >> 3));
+      const uint8_t* qc = reinterpret_cast<const uint8_t*>(qa & ~uintptr_t(15));
+      rd.slack = uint32_t(qa & 15) * 8;  // staged bits before the round's first bit
+      const uint32_t nc = rd.ok ? ((end_bit - rd.base_bit + rd.slack + 31) / 32 + GPAD + 3) / 4 : 0u;
+      for (uint32_t c = t; c < nc; c += GT) {
+        const uint8_t* src = qc + 16 * c;
+        const uint32_t valid = src >= end ? 0u : end - src >= 16 ? 16u : uint32_t(end - src);
+        cp_async16_zfill(smem_addr(&S.win[4 * c]), valid ? src : qc, valid);
+      }
+      cp_async_commit();
+      return rd;
+    };
+    // every staged word byte-swapped in place into the window's big-endian words
+    auto finish_round = [&](const Round& rd) {
+      const uint32_t end_bit = ti[it.tile0 + rd.tb];
+      const uint32_t nc = ((end_bit - rd.base_bit + rd.slack + 31) / 32 + GPAD + 3) / 4;
+      cp_async_wait_all();
+      __syncthreads();
+      for (uint32_t j = t; j < 4 * nc; j += GT) S.win[j] = bswap32(S.win[j]);
+      __syncthreads();
+    };
+    Round rd = issue_round(0);
+    if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
+      if (t == 0) atomicOr(a.status, kStatusCodebook);
+      cp_async_wait_all();
+      __syncthreads();
+      continue;
+    }
+    if (NB > 0)
+      for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
     // x for this tile's 16 columns
     const float* xs = a.x + (sd.xoff + uint64_t(tile) * 16) * a.ld;
     // x[c][b] for the tile's 16 columns and the pass's nb <= NB batch columns
@@ -803,32 +841,14 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const bool ostore32 = NB == 0 && ((reinterpret_cast<uintptr_t>(a.out + sd.dst) | (sd.cols * 2)) & 31) == 0;
     uint32_t ta = 0;
     while (ta < it.ntiles) {  // rounds (one, unless the tiles' bits exceed GCAP)
-      const uint32_t base_bit = ti[it.tile0 + ta] & ~31u;
-      const bool fits = mine && uint32_t(t) >= ta && b1 - base_bit <= GCAP;
-      const uint32_t tb = ta + uint32_t(__syncthreads_count(fits));
-      const uint32_t end_bit = ti[it.tile0 + tb];
-      if (tb == ta || end_bit < base_bit || end_bit - base_bit > GCAP) {
-        // an index that does not describe this payload (uniform branch)
+      if (ta) rd = issue_round(ta);
+      if (!rd.ok) {
         if (t == 0) atomicOr(a.status, kStatusInternal);
+        cp_async_wait_all();
         break;
       }
-      // the round's bits as the 16-byte aligned chunks that hold them: one
-      // round trip of cp.async (bytes past the slab read as zero), then every
-      // word byte-swapped in place into the window's big-endian words
-      const uintptr_t qa = reinterpret_cast<uintptr_t>(bits + (base_bit >> 3));
-      const uint8_t* qc = reinterpret_cast<const uint8_t*>(qa & ~uintptr_t(15));
-      const uint32_t slack = uint32_t(qa & 15) * 8;  // staged bits before the round's first bit
-      const uint32_t nc = ((end_bit - base_bit + slack + 31) / 32 + GPAD + 3) / 4;
-      for (uint32_t c = t; c < nc; c += GT) {
-        const uint8_t* src = qc + 16 * c;
-        const uint32_t valid = src >= end ? 0u : end - src >= 16 ? 16u : uint32_t(end - src);
-        cp_async16_zfill(smem_addr(&S.win[4 * c]), valid ? src : qc, valid);
-      }
-      cp_async_commit();
-      cp_async_wait_all();
-      __syncthreads();
-      for (uint32_t j = t; j < 4 * nc; j += GT) S.win[j] = bswap32(S.win[j]);
-      __syncthreads();
+      finish_round(rd);
+      const uint32_t tb = rd.tb, base_bit = rd.base_bit, slack = rd.slack;
       bool act = mine && uint32_t(t) >= ta && uint32_t(t) < tb && b0 >= base_bit && b1 >= b0;
       SmemWin96 r;
       r.init(S.win, act ? b0 - base_bit + slack : 0u);
