@@ -55,7 +55,7 @@ struct SerialShared {
   alignas(16) uint16_t cnt[256];  // codes per length
   uint16_t offs[257];     // index in sorted[] of the first code of length l
   uint8_t sorted[256];    // symbols in canonical (length, symbol) order
-  alignas(16) uint32_t win[WINW];  // the round's bits, big-endian words
+  alignas(16) uint32_t win[WINW + 16];  // the round's bits, big-endian words (+ room for the raw copy's offset)
   union {
     struct {
       uint16_t pos[REC][ST];  // lookup start, relative to the thread's range start
@@ -394,20 +394,43 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
     const uint32_t cnt32 = uint32_t(count);
     while (R0 < nb32) {
       // ---- 1. the round's bits into shared memory (zero past the slab) ----
+      // The 16-byte aligned chunks that hold them arrive by cp.async four
+      // words into the window (one memory round trip), then passes of 1024
+      // words realign them to the round's first byte and byte-swap them into
+      // big-endian words: each pass reads 4+ words ahead of what it writes,
+      // and writes after a barrier, so the window is rewritten in place.
       const uint32_t nw = round_bits / 32 + PADW;
-      for (uint32_t j = t; j < nw; j += ST) {
-        const uint8_t* q = bits + (R0 >> 3) + 4 * j;
-        uint32_t v = 0;
-        if (q < end) {
-          const uintptr_t qa = reinterpret_cast<uintptr_t>(q);
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(qa & ~uintptr_t(3));
-          const int sh = int(qa & 3) * 8;
-          const uint32_t lo = __ldg(qw);
-          const uint32_t hi =
-              (sh && reinterpret_cast<const uint8_t*>(qw + 1) < end) ? __ldg(qw + 1) : 0u;
-          v = bswap32(sh ? __funnelshift_r(lo, hi, sh) : lo);
+      {
+        const uintptr_t qa = reinterpret_cast<uintptr_t>(bits + (R0 >> 3));
+        const uint8_t* qc = reinterpret_cast<const uint8_t*>(qa & ~uintptr_t(15));
+        const uint32_t sb = uint32_t(qa & 15);  // bytes of the first chunk before the round
+        const uint32_t nc = (4 * nw + sb + 4 + 15) / 16;
+        for (uint32_t c = t; c < nc; c += ST) {
+          const uint8_t* src = qc + 16 * c;
+          const uint32_t valid = src >= end ? 0u : end - src >= 16 ? 16u : uint32_t(end - src);
+          cp_async16_zfill(smem_addr(&S.win[4 + 4 * c]), valid ? src : qc, valid);
         }
-        S.win[j] = v;
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+        const uint32_t wq = 4 + (sb >> 2), sh = (sb & 3) * 8;
+        for (uint32_t j0 = 0; j0 < nw; j0 += 4 * ST) {
+          uint32_t v[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t j = j0 + uint32_t(t) + uint32_t(k) * ST;
+            if (j < nw) {
+              const uint32_t lo = S.win[wq + j], hi = S.win[wq + j + 1];
+              v[k] = bswap32(sh ? __funnelshift_r(lo, hi, sh) : lo);
+            }
+          }
+          __syncthreads();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t j = j0 + uint32_t(t) + uint32_t(k) * ST;
+            if (j < nw) S.win[j] = v[k];
+          }
+        }
       }
       const uint32_t lim_rel = min(nb32 - R0, round_bits);
       const uint32_t my_lo = uint32_t(t) * S_bits;
