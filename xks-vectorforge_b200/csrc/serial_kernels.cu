@@ -756,6 +756,9 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
   extern __shared__ __align__(16) uint8_t smem_raw[];
   GemvShared& S = *reinterpret_cast<GemvShared*>(smem_raw);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  // the stream's next kernel may start launching once every CTA of this one
+  // has started (it waits for this grid before touching what it shares)
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   for (uint32_t ii = blockIdx.x; ii < a.nitems; ii += gridDim.x) {
     const GemvItem it = a.items[ii];
     const Slab sd = a.slabs[it.slab];
@@ -831,6 +834,11 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     }
     if (NB > 0)
       for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
+    // Launched behind the stream's previous kernel (programmatic dependent
+    // launch), everything above read only the payload, the index and the
+    // plan; x, Y, the partials and the output are touched after that kernel
+    // has completed and its writes are visible.
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
     // x for this tile's 16 columns
     const float* xs = a.x + (sd.xoff + uint64_t(tile) * 16) * a.ld;
     // x[c][b] for the tile's 16 columns and the pass's nb <= NB batch columns
@@ -1085,25 +1093,37 @@ cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* pa
   return cudaGetLastError();
 }
 
+// The indexed kernel is launched with programmatic stream serialisation: its
+// CTAs may start (table build, bit staging) while the stream's previous
+// kernel finishes, and wait for it before touching shared data.
+template <int NB>
+cudaError_t launch_tile_kernel(const GemvArgs& args, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(args.nitems);
+  cfg.blockDim = dim3(GT);
+  cfg.dynamicSmemBytes = sizeof(GemvShared);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, serial_tile_gemv_kernel<NB>, args);
+}
+
 cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
   if (args.nb < 1 || args.nb > uint32_t(GNB)) return cudaErrorInvalidValue;
   serial_set_attr();
-  const uint32_t g = args.nitems;
-  if (args.nb == 1)
-    serial_tile_gemv_kernel<1><<<g, GT, sizeof(GemvShared), st>>>(args);
-  else if (args.nb == 2)
-    serial_tile_gemv_kernel<2><<<g, GT, sizeof(GemvShared), st>>>(args);
-  else
-    serial_tile_gemv_kernel<4><<<g, GT, sizeof(GemvShared), st>>>(args);
-  return cudaGetLastError();
+  if (args.nb == 1) return launch_tile_kernel<1>(args, st);
+  if (args.nb == 2) return launch_tile_kernel<2>(args, st);
+  return launch_tile_kernel<4>(args, st);
 }
 
 cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
   serial_set_attr();
-  serial_tile_gemv_kernel<0><<<args.nitems, GT, sizeof(GemvShared), st>>>(args);
-  return cudaGetLastError();
+  return launch_tile_kernel<0>(args, st);
 }
 
 cudaError_t launch_tp_wait(const uint32_t* flags, uint32_t world, const uint32_t* epoch, int* status,
