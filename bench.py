@@ -1131,6 +1131,24 @@ def tp_gemv(args, dev, stream, threads, rank, world):
     own = bool(torch.equal(g0["yfull"][rank * g0["rows"]:(rank + 1) * g0["rows"]], g0["y"]))
     ms = t / args.gemv_steps * 1e3
 
+    # the same plans without any gather: the all-gather's share of a token
+    def forward_local():
+        for g in groups:
+            g["plan"].gemm(d_payload, x, g["y"], 1, h)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            forward_local()
+    stream.synchronize()
+    bad += sum(g["plan"].status(h) for g in groups)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        tl = time_steps(forward_local, args.gemv_steps, stream)
+    tt = torch.tensor([tl], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_l = float(tt.item()) / args.gemv_steps * 1e3
+
     # fused all-gather: the GEMV epilogue stores rows into every rank's gathered
     # buffer over NVLink, then a bounded flag wait (xksv_tp_fused_gemm)
     fused = xksv_gpu.TPFused(rank, world, max(g["rows"] for g in groups), 1)
@@ -1167,10 +1185,12 @@ def tp_gemv(args, dev, stream, threads, rank, world):
                 ms_per_token=round(ms_f, 4), n_gpus=world, compressed_bytes_per_rank=int(payload.nbytes),
                 launches_per_token=2 * len(groups), status_errors=int(bad), matches_nccl_path=fused_match,
                 nccl_allgather=dict(value=round(1e3 / ms, 2), ms_per_token=round(ms, 4),
-                                    own_shard_gathered=own),
+                                    own_shard_gathered=own, allgather_share=round(1 - ms_l / ms, 3)),
+                local_gemv_ms_per_token=round(ms_l, 4), allgather_share=round(1 - ms_l / ms_f, 3),
                 note="rows sharded per GPU in whole slabs; value: xksv_tp_fused_gemm (GEMV epilogue stores "
                      "rows into every rank's buffer over NVLink + flag wait); nccl_allgather: xksv_tp_gemm "
-                     "(plan GEMV + ncclAllGather)")
+                     "(plan GEMV + ncclAllGather); local_gemv_ms_per_token: the same plans with no gather "
+                     "(max over ranks); allgather_share = 1 - local / path")
 
 
 def main():
@@ -1218,6 +1238,10 @@ def main():
     dev = f"cuda:{local}"
     if world > 1:
         import datetime
+        # NCCL's init lines (ranks, transports, NVLS) on stderr, so the run's
+        # rank count and collective path are on record
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device(dev))
     xksv_gpu.load()
@@ -1416,8 +1440,8 @@ def main():
                       samples=sum(c["samples"] for c in allc))
     if rank == 0:
         line = dict(
-            metric=METRIC, value=round(value, 2), unit="GB/s", n_gpus=world, steps=args.steps,
-            warmup=args.warmup, ms_per_step=round(t / args.steps * 1e3, 4), higher_is_better=True,
+            metric=METRIC, value=round(value, 2), unit="GB/s", n_gpus=world, per_gpu_gbs=round(value / world, 2),
+            steps=args.steps, warmup=args.warmup, ms_per_step=round(t / args.steps * 1e3, 4), higher_is_better=True,
             scaling="weak", vs_baseline=None, dtype="bf16",
             data="synthetic: seeded BF16 N(0,0.02) Llama-1.1B-shaped weights, norms 1.0 (no checkpoint download)",
             config=workload_config(world),
