@@ -6,29 +6,30 @@
 // runs on the CUDA cores and the multiply on the 5th-generation tensor cores
 // of the same SM:
 //   * a CTA owns a group of up to 32 slabs that read the same X columns and a
-//     range of their 16-column tiles; lane j of every producer warp decodes
-//     slab j (lane-private canonical tables in shared memory, shared by the
-//     CTA's warps and built once per CTA; the bit stream of the warp's tile
-//     range starts at the tile index's recorded offset and runs contiguously
-//     through the following tiles);
-//   * every producer warp splits the CTA's tiles into its own contiguous run
-//     and decodes tile rows in lock step over its lanes: after row s of a
-//     tile, lane j holds the 16 BF16 weights of row 16 j' + s (j' = its slab)
-//     for the tile's 16 columns and stores them as row 32 (s % 4) + j of a
-//     128 x 16 stage in the UMMA canonical K-major layout, so four tile rows
+//     run of their half tiles (8 rows x 16 columns); lane j of every producer
+//     warp decodes slab j with the lane-private canonical tables of
+//     lane_decode.cuh, built once per group when the tile index is built and
+//     copied into the CTA's shared memory (one set, shared by its warps); a
+//     warp's bit stream starts at the tile index's offset of its first half
+//     tile and runs contiguously through the following ones;
+//   * every producer warp takes its own contiguous share of the CTA's half
+//     tiles and decodes tile rows in lock step over its lanes: after row s of
+//     a tile, lane j holds the 16 BF16 weights of row 16 j' + s (j' = its
+//     slab) for the tile's 16 columns and stores them as row 32 (s % 4) + j of
+//     a 128 x 16 stage in the UMMA canonical K-major layout, so four tile rows
 //     of 32 slabs fill one stage: the A operand of one M = 128, K = 16 MMA;
 //   * stage q (rows 4q .. 4q+3 of every slab) of every tile accumulates into
 //     TMEM accumulator D_q (four of them, 128 lanes x npad FP32 columns);
 //     B is the tile's 16 rows of X^T (BF16), staged per warp by cp.async;
-//   * one thread issues every MMA in a fixed order (stage m of warp 0, 1, ...
-//     then stage m + 1), so a CTA's sums are reproducible, and commits each
-//     stage back to its producer through an mbarrier; producers run up to two
-//     stages ahead;
+//   * one thread issues each warp's stages in that warp's order, serving the
+//     warps as their stages become ready, and commits each stage back to its
+//     producer through an mbarrier (one stage slot per warp: the MMA finishes
+//     while the producer decodes its next row);
 //   * the epilogue reads D_q with tcgen05.ld (warp r of the first four holds
 //     TMEM lanes 32 r .., i.e. row 4q + r of every slab) and adds into Y
 //     (several CTAs share a group's rows when its tiles are split).
-// Shared memory holds the tables once and, per producer warp, two stages,
-// two B slices and the lane rings; no decoded tile is buffered whole, so 16
+// Shared memory holds the tables once and, per producer warp, one stage, two
+// B slices and the lane rings; no decoded tile is buffered whole, so 19
 // producer warps fit one SM beside the stages.  Every wait is bounded: on a
 // timeout the CTA sets an error bit, lets its issued MMAs drain, frees its
 // TMEM and returns.
