@@ -35,10 +35,12 @@
 // A substream whose codebook the compact tables cannot hold (a length above
 // PK+PNL or more than PLONG long codes, e.g. near-uniform exponents) is decoded
 // afterwards by lane 0 with the bit-serial canonical decoder.
-// A slab's setup is a chain of dependent loads (container header, substream
-// table, substream headers, length tables); while one slab's tables are built
-// the warp already reads its next slab's substream table and prefetches that
-// slab's substream headers and length tables into L2.
+// A slab's setup takes two memory round trips: the container header together
+// with each lane's substream-table entry, then each lane's substream header
+// together with its 256 code lengths (cp.async copies into the lane's own
+// table memory, idle until the tables are filled) and its first sign/mantissa
+// chunks.  A warp that goes on to another slab (grids smaller than the slab
+// count) prefetches that slab's headers and length tables into L2 meanwhile.
 #include <atomic>
 
 #include "kernels.h"
