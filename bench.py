@@ -1239,9 +1239,10 @@ def main():
     if world > 1:
         import datetime
         # NCCL's init lines (ranks, transports, NVLS) on stderr, so the run's
-        # rank count and collective path are on record
+        # rank count and collective path are on record (stdout keeps the one
+        # JSON line)
         os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device(dev))
     xksv_gpu.load()
