@@ -194,6 +194,7 @@ struct xksv_plan {
   const void* indexed_payload = nullptr;
   uint32_t* d_tidx = nullptr;
   uint32_t* d_tmid = nullptr;  // row-8 offsets of the tiles (fused GEMM work split)
+  xksv::GemvTabs* d_gtabs = nullptr;  // per indexed slab: the tile GEMV kernel's tables
   uint64_t* d_tbase = nullptr;
   xksv::GemvItem* d_items = nullptr;
   uint32_t n_items = 0;
@@ -229,6 +230,7 @@ namespace {
 void free_index(xksv_plan* p) {
   if (p->d_tidx) cudaFree(p->d_tidx);
   if (p->d_tmid) cudaFree(p->d_tmid);
+  if (p->d_gtabs) cudaFree(p->d_gtabs);
   if (p->d_tbase) cudaFree(p->d_tbase);
   if (p->d_items) cudaFree(p->d_items);
   if (p->d_partials) cudaFree(p->d_partials);
@@ -247,6 +249,7 @@ void free_index(xksv_plan* p) {
   p->fused_ok = false;
   p->d_tidx = nullptr;
   p->d_tmid = nullptr;
+  p->d_gtabs = nullptr;
   p->d_tbase = nullptr;
   p->d_items = nullptr;
   p->d_partials = nullptr;
@@ -619,6 +622,7 @@ cudaError_t tile_decode(xksv_plan* p, const xksv::Slab* slabs, const uint8_t* pa
   g.slabs = slabs;
   g.tbase = p->d_tbase;
   g.tidx = p->d_tidx;
+  g.gtabs = p->d_gtabs;
   g.payload = pay;
   g.status = p->d_status;
   g.out = out;
@@ -848,6 +852,7 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, size_t payload_si
       g.slabs = p->d_slabs;
       g.tbase = p->d_tbase;
       g.tidx = p->d_tidx;
+      g.gtabs = p->d_gtabs;
       g.payload = pay;
       g.x = d_x + b0;
       g.y = d_y + b0;
@@ -1039,6 +1044,7 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, vo
   bool ok = cudaMalloc(&p->d_tidx, total * sizeof(uint32_t)) == cudaSuccess &&
             cudaMalloc(&p->d_tmid, total * sizeof(uint32_t)) == cudaSuccess &&
             cudaMalloc(&p->d_tbase, n * sizeof(uint64_t)) == cudaSuccess &&
+            cudaMalloc(&p->d_gtabs, n * sizeof(GemvTabs)) == cudaSuccess &&
             cudaMalloc(&p->d_items, items.size() * sizeof(GemvItem)) == cudaSuccess &&
             cudaMalloc(&p->d_partials, items.size() * 16 * 4 * sizeof(float)) == cudaSuccess &&
             cudaMalloc(&p->d_counters, n * sizeof(uint32_t)) == cudaSuccess &&
@@ -1050,7 +1056,7 @@ int xksv_plan_index(xksv_plan* p, const void* d_payload, size_t payload_size, vo
             cudaMemsetAsync(p->d_status, 0, sizeof(int), st) == cudaSuccess;
   if (ok)
     ok = launch_serial_index(p->d_slabs, n, static_cast<const uint8_t*>(d_payload), p->d_tidx, p->d_tmid,
-                             p->d_tbase, p->d_status, st) == cudaSuccess;
+                             p->d_tbase, p->d_gtabs, p->d_status, st) == cudaSuccess;
   if (ok)
     ok = cudaMemcpyAsync(p->h_status, p->d_status, sizeof(int), cudaMemcpyDeviceToHost, st) == cudaSuccess &&
          cudaStreamSynchronize(st) == cudaSuccess;
@@ -1164,6 +1170,7 @@ int xksv_tp_fused_gemm(xksv_tp_fused* c, const xksv_plan* pc, const void* d_payl
   g.slabs = p->d_slabs;
   g.tbase = p->d_tbase;
   g.tidx = p->d_tidx;
+  g.gtabs = p->d_gtabs;
   g.payload = static_cast<const uint8_t*>(d_payload);
   g.x = d_x;
   g.ld = uint32_t(batch);

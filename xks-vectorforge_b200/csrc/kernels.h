@@ -12,6 +12,8 @@ size_t parallel_smem_bytes();
 size_t serial_smem_bytes();
 
 // Decode slabs[0..n) from payload into out (+ slab.dst bytes each).
+struct GemvTabs;
+
 cudaError_t launch_parallel_decode(const Slab* slabs, uint32_t n, const uint8_t* payload,
                                    uint8_t* out, int* status, int grid, cudaStream_t st);
 cudaError_t launch_serial_decode(const Slab* slabs, uint32_t n, const uint8_t* payload,
@@ -35,8 +37,24 @@ cudaError_t launch_raw_gemm(const Slab* slabs, uint32_t n, const uint8_t* payloa
 // tile k's first code in slab i's stream, tidx[tbase[i] + tiles] = bit count;
 // tmid[tbase[i] + k] = bit offset of tile k's row 8 (its 129th code).
 cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* payload,
-                                uint32_t* tidx, uint32_t* tmid, const uint64_t* tbase, int* status,
-                                cudaStream_t st);
+                                uint32_t* tidx, uint32_t* tmid, const uint64_t* tbase, GemvTabs* gtabs,
+                                int* status, cudaStream_t st);
+
+// A 16-row serial-codec slab's decode tables as the tile GEMV kernel holds
+// them in shared memory: the 2^11-entry single-code table (exponent << 7 |
+// length; 0 = longer code) and the canonical data of longer codes (limits,
+// first codes, counts, offsets, symbols in (length, symbol) order).  Written
+// once per slab by the tile-index pass (xksv_plan_index) and copied in by each
+// GEMV item instead of being rebuilt from the code lengths.
+struct alignas(16) GemvTabs {
+  uint16_t lut[1 << 11];
+  uint64_t lim[33];
+  uint64_t firstc[33];
+  alignas(16) uint16_t cnt[256];
+  uint16_t offs[257];
+  uint8_t sorted[256];
+  int maxlen, minlen;
+};
 
 struct GemvArgs {
   const GemvItem* items;
@@ -52,6 +70,7 @@ struct GemvArgs {
   uint32_t* counters;      // per slab, zero between launches
   int* status;
   uint8_t* out;            // indexed decode: output base (slab dst = byte offset)
+  const GemvTabs* gtabs;   // per slab: its tables (from the index pass); nullptr = build them
   // fused tensor-parallel all-gather (npeers > 0): output rows go to this
   // rank's block (rows peer_row0 ..) of its own gathered buffer; the grid's
   // last CTA copies the block into every other rank's buffer over NVLink and

@@ -289,6 +289,7 @@ struct SerialArgs {
   uint32_t* tidx;         // MODE 2: tile index (bit offset of each 16x16 tile's first code)
   const uint64_t* tbase;  // MODE 2: first index entry of each slab
   uint32_t* tmid;         // MODE 2: bit offset of each tile's row 8 (same entry positions)
+  GemvTabs* gtabs;        // MODE 2: each slab's tables for the tile GEMV kernel
 };
 
 struct SOut {
@@ -357,6 +358,23 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       __syncthreads();
       continue;
+    }
+    if (MODE == 2) {  // the tile GEMV kernel's copy of the tables (the same layout)
+      GemvTabs& g = a.gtabs[si];
+      for (int k = t; k < (1 << SK); k += ST) g.lut[k] = S.lut[k];
+      for (int k = t; k < 33; k += ST) {
+        g.lim[k] = S.lim[k];
+        g.firstc[k] = S.firstc[k];
+      }
+      for (int k = t; k < 256; k += ST) {
+        g.cnt[k] = S.cnt[k];
+        g.sorted[k] = S.sorted[k];
+      }
+      for (int k = t; k < 257; k += ST) g.offs[k] = S.offs[k];
+      if (t == 0) {
+        g.maxlen = S.maxlen;
+        g.minlen = S.minlen;
+      }
     }
     const uint8_t* sm = p + kHdr;
     const uint8_t* bits = p + kHdr + count;
@@ -703,18 +721,15 @@ constexpr int GWINW = 6144 + GPAD;       // staged bit words per round
 constexpr uint32_t GCAP = uint32_t(GWINW - GPAD - 9) * 32;  // bits per round (+ up to 4 words of alignment)
 constexpr int GNB = 4;                   // batch columns per pass
 
-struct GemvShared {
-  uint16_t lut[1 << SK];  // exponent << 7 | length; 0 = none (16-bit: fewer bank conflicts)
-  uint64_t lim[33];
-  uint64_t firstc[33];
-  alignas(16) uint16_t cnt[256];
-  uint16_t offs[257];
-  uint8_t sorted[256];
+// The tables (16-bit single-code entries: fewer bank conflicts) lead, in the
+// layout the index pass writes them to global memory.
+static_assert((1 << SK) == sizeof(GemvTabs::lut) / 2, "the exported table has SK bits");
+struct GemvShared : GemvTabs {
   alignas(16) uint32_t win[GWINW];
   uint8_t hist[8][256];
   uint32_t warpsum[GT / 32];
   float red[16][GT / 32][GNB];
-  int maxlen, minlen, flag;
+  int flag;
 };
 
 // FP32 weight from a table entry (exponent at bit 7, length in bits 0-4) and
@@ -826,7 +841,14 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
       __syncthreads();
     };
     Round rd = issue_round(0);
-    if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
+    if (a.gtabs) {
+      // the slab's tables from the index pass, landing with the round's bits
+      // (the previous item's last barrier has retired every read of them)
+      const uint4* src = reinterpret_cast<const uint4*>(a.gtabs + it.slab);
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<GemvTabs*>(&S));
+      for (int k = t; k < int(sizeof(GemvTabs) / 16); k += GT) cp_async16(dst + k, src + k);
+      cp_async_commit();
+    } else if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
       if (t == 0) atomicOr(a.status, kStatusCodebook);
       cp_async_wait_all();
       __syncthreads();
@@ -1085,10 +1107,11 @@ cudaError_t launch_serial_gemm(const Slab* slabs, uint32_t n, const uint8_t* pay
 }
 
 cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* payload,
-                                uint32_t* tidx, uint32_t* tmid, const uint64_t* tbase, int* status, cudaStream_t st) {
+                                uint32_t* tidx, uint32_t* tmid, const uint64_t* tbase, GemvTabs* gtabs,
+                                int* status, cudaStream_t st) {
   if (!n) return cudaSuccess;
   serial_set_attr();
-  SerialArgs a{payload, nullptr, nullptr, nullptr, 1, 1, status, tidx, tbase, tmid};
+  SerialArgs a{payload, nullptr, nullptr, nullptr, 1, 1, status, tidx, tbase, tmid, gtabs};
   serial_slab_kernel<2><<<n, ST, sizeof(SerialShared), st>>>(slabs, n, a);
   return cudaGetLastError();
 }
