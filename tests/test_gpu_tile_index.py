@@ -216,3 +216,41 @@ def test_indexed_decode_bit_exact(xg, kind):
         for e, raw in zip(entries, raws):
             assert got[e["dst_offset"]:e["dst_offset"] + len(raw)] == raw, e
     plan.close()
+
+
+def test_indexed_one_and_two_threads_per_tile(xg):
+    """At batch 1 (and for decode) a launch whose items fill under one wave of
+    256-thread CTAs decodes each tile with two threads (rows 0-7 and 8-15, the
+    second from the index's row-8 offset); a larger launch uses one.  A plan of
+    700 slabs (700 items: one thread per tile) and one of its first 200 (two
+    per tile): GEMV against FP32, decode bit-exact, on both."""
+    rng = np.random.default_rng(41)
+    R, C = 700 * 16, 256
+    w = words_for("student3", R * C, rng).reshape(R, C)
+    payload = bytearray(b"\x00" * 7)
+    entries = []
+    for r0 in range(0, R, 16):
+        blob = xg.host_pack(w[r0:r0 + 16].astype("<u2").tobytes(), 16, C, 1)
+        entries.append(dict(src_offset=len(payload), src_size=len(blob), rows=16, cols=C,
+                            dst_offset=r0, x_offset=0, codec=1))
+        payload += blob + b"\x00" * (r0 % 3)
+    d_payload = torch.frombuffer(payload, dtype=torch.uint8).cuda()
+    x = torch.randn(C, 1, device="cuda")
+    W = torch.from_numpy(bf16_to_f32(w)).cuda()
+    for n in (700, 200):
+        plan = xg.Plan(entries[:n])
+        assert plan.index(d_payload) == 0
+        for _ in range(2):
+            y = torch.full((16 * n, 1), float("nan"), device="cuda")
+            plan.gemm(d_payload, x, y, 1)
+            assert plan.status() == 0 and plan.launches() == 1
+            assert rel_l2(y.cpu(), (W[:16 * n] @ x).cpu()) < 1e-5
+        dec = [dict(e, dst_offset=2 * C * e["dst_offset"]) for e in entries[:n]]
+        dplan = xg.Plan(dec)
+        assert dplan.index(d_payload) == 0
+        d_out = torch.full((32 * C * n,), 0xAB, dtype=torch.uint8, device="cuda")
+        dplan.decode(d_payload, d_out)
+        assert dplan.status() == 0
+        assert d_out.cpu().numpy().tobytes() == w[:16 * n].astype("<u2").tobytes()
+        dplan.close()
+        plan.close()

@@ -623,6 +623,7 @@ cudaError_t tile_decode(xksv_plan* p, const xksv::Slab* slabs, const uint8_t* pa
   g.tbase = p->d_tbase;
   g.tidx = p->d_tidx;
   g.gtabs = p->d_gtabs;
+  g.tmid = p->d_tmid;
   g.payload = pay;
   g.status = p->d_status;
   g.out = out;
@@ -853,6 +854,7 @@ int xksv_plan_gemm(const xksv_plan* pc, const void* d_payload, size_t payload_si
       g.tbase = p->d_tbase;
       g.tidx = p->d_tidx;
       g.gtabs = p->d_gtabs;
+      g.tmid = p->d_tmid;
       g.payload = pay;
       g.x = d_x + b0;
       g.y = d_y + b0;
@@ -1171,6 +1173,7 @@ int xksv_tp_fused_gemm(xksv_tp_fused* c, const xksv_plan* pc, const void* d_payl
   g.tbase = p->d_tbase;
   g.tidx = p->d_tidx;
   g.gtabs = p->d_gtabs;
+  g.tmid = p->d_tmid;
   g.payload = static_cast<const uint8_t*>(d_payload);
   g.x = d_x;
   g.ld = uint32_t(batch);

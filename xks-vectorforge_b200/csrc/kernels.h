@@ -70,7 +70,8 @@ struct GemvArgs {
   uint32_t* counters;      // per slab, zero between launches
   int* status;
   uint8_t* out;            // indexed decode: output base (slab dst = byte offset)
-  const GemvTabs* gtabs;   // per slab: its tables (from the index pass); nullptr = build them
+  const GemvTabs* gtabs;   // per slab: its tables (from the index pass)
+  const uint32_t* tmid;    // bit offset of each tile's row 8 (tile-index positions)
   // fused tensor-parallel all-gather (npeers > 0): output rows go to this
   // rank's block (rows peer_row0 ..) of its own gathered buffer; the grid's
   // last CTA copies the block into every other rank's buffer over NVLink and

@@ -715,20 +715,26 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
 // registers, then a warp sum per row.  Slabs split over several CTAs combine
 // their row sums in a fixed order in the last CTA to finish (deterministic,
 // and Y is overwritten as cuda/decode.cu:31 requires).
-constexpr int GT = 256;                  // threads (tiles) per GEMV CTA
+constexpr int GT = 256;                  // tiles per GEMV item (CTA)
 constexpr int GPAD = 160;                // zero words past a round: one row of 16 maximal codes + window
 constexpr int GWINW = 6144 + GPAD;       // staged bit words per round
 constexpr uint32_t GCAP = uint32_t(GWINW - GPAD - 9) * 32;  // bits per round (+ up to 4 words of alignment)
 constexpr int GNB = 4;                   // batch columns per pass
+// Threads per tile (SPLIT): one, or, for launches at batch <= 1 whose items
+// fill under one wave of 256-thread CTAs, two -- rows 0-7 from the tile's
+// first code and rows 8-15 from its row-8 offset (both in the index) -- so
+// that such a launch has twice the threads (a 4096 x 4096 weight is 65536
+// tiles, under half of the 148 x 1024 threads the GPU holds).  Measured on
+// 16 x 4096 slabs at batch 1: 256 slabs 31.2 us split against 50.0; 1024
+// slabs (1.7 waves) 102.5 against 97.7, hence one thread per tile there.
+constexpr int GTMAX = 2 * GT;            // threads per CTA at most
 
 // The tables (16-bit single-code entries: fewer bank conflicts) lead, in the
 // layout the index pass writes them to global memory.
 static_assert((1 << SK) == sizeof(GemvTabs::lut) / 2, "the exported table has SK bits");
 struct GemvShared : GemvTabs {
   alignas(16) uint32_t win[GWINW];
-  uint8_t hist[8][256];
-  uint32_t warpsum[GT / 32];
-  float red[16][GT / 32][GNB];
+  float red[16][GTMAX / 32][GNB];
   int flag;
 };
 
@@ -766,11 +772,16 @@ __device__ __forceinline__ void fma4(float* acc, uint32_t e0, uint32_t e1, uint3
 }
 
 // NB == 0: decode mode (BF16 tile rows to a.out + slab dst); NB >= 1: GEMV/GEMM.
-template <int NB>
-__global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(GemvArgs a) {
+template <int NB, int SPLIT>
+__global__ void __launch_bounds__(GT * SPLIT, SPLIT == 2 || NB > 1 ? 2 : 4) serial_tile_gemv_kernel(GemvArgs a) {
+  static_assert(SPLIT == 1 || (SPLIT == 2 && NB <= 1), "two threads per tile at batch <= 1");
+  constexpr int NT = GT * SPLIT;   // threads
+  constexpr int RPT = 16 / SPLIT;  // tile rows per thread
   extern __shared__ __align__(16) uint8_t smem_raw[];
   GemvShared& S = *reinterpret_cast<GemvShared*>(smem_raw);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int tl = t % GT;    // this thread's tile of the item
+  const int part = t / GT;  // and its rows: part * RPT .. + RPT - 1
   // the stream's next kernel may start launching once every CTA of this one
   // has started (it waits for this grid before touching what it shares)
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
@@ -788,22 +799,24 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     {
       const uint8_t* smp = p + kHdr + uint64_t(it.tile0) * 256;
       const uint64_t smn = uint64_t(it.ntiles) * 256;
-      for (uint64_t off = uint64_t(t) * 128; off < smn; off += uint64_t(GT) * 128)
+      for (uint64_t off = uint64_t(t) * 128; off < smn; off += uint64_t(NT) * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(smp + off));
       const uint32_t* tix = a.tidx + a.tbase[it.slab];
       const uint64_t nbb = sd.size - kHdr - count;
       const uint64_t pb0 = tix[it.tile0] >> 3, pb1 = min(uint64_t(tix[it.tile0 + it.ntiles] + 7) >> 3, nbb);
       const uint8_t* bp = p + kHdr + count;
-      for (uint64_t off = pb0 + uint64_t(t) * 128; off < pb1; off += uint64_t(GT) * 128)
+      for (uint64_t off = pb0 + uint64_t(t) * 128; off < pb1; off += uint64_t(NT) * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(bp + off));
     }
     const uint32_t* ti = a.tidx + a.tbase[it.slab];
     const uint8_t* sm = p + kHdr;
     const uint8_t* bits = sm + count;
     const uint8_t* end = p + sd.size;
-    const bool mine = uint32_t(t) < it.ntiles;
-    const uint32_t tile = it.tile0 + uint32_t(mine ? t : 0);
+    const bool mine = uint32_t(tl) < it.ntiles;
+    const uint32_t tile = it.tile0 + uint32_t(mine ? tl : 0);
     const uint32_t b0 = ti[tile], b1 = ti[tile + 1];
+    // where this thread's rows start: the tile's first code, or its row 8
+    const uint32_t bs = part ? a.tmid[a.tbase[it.slab] + tile] : b0;
     // A round: the tiles [ta, tb) whose bits fit the window, staged as the
     // 16-byte aligned chunks that hold them by cp.async (bytes past the slab
     // read as zero); the first round's copies overlap the table build.
@@ -814,7 +827,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     auto issue_round = [&](uint32_t ta) {
       Round rd;
       rd.base_bit = ti[it.tile0 + ta] & ~31u;
-      const bool fits = mine && uint32_t(t) >= ta && b1 - rd.base_bit <= GCAP;
+      const bool fits = mine && part == 0 && uint32_t(tl) >= ta && b1 - rd.base_bit <= GCAP;
       rd.tb = ta + uint32_t(__syncthreads_count(fits));
       const uint32_t end_bit = ti[it.tile0 + rd.tb];
       // an index that does not describe this payload fails here (uniformly)
@@ -823,7 +836,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
       const uint8_t* qc = reinterpret_cast<const uint8_t*>(qa & ~uintptr_t(15));
       rd.slack = uint32_t(qa & 15) * 8;  // staged bits before the round's first bit
       const uint32_t nc = rd.ok ? ((end_bit - rd.base_bit + rd.slack + 31) / 32 + GPAD + 3) / 4 : 0u;
-      for (uint32_t c = t; c < nc; c += GT) {
+      for (uint32_t c = t; c < nc; c += NT) {
         const uint8_t* src = qc + 16 * c;
         const uint32_t valid = src >= end ? 0u : end - src >= 16 ? 16u : uint32_t(end - src);
         cp_async16_zfill(smem_addr(&S.win[4 * c]), valid ? src : qc, valid);
@@ -837,25 +850,20 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
       const uint32_t nc = ((end_bit - rd.base_bit + rd.slack + 31) / 32 + GPAD + 3) / 4;
       cp_async_wait_all();
       __syncthreads();
-      for (uint32_t j = t; j < 4 * nc; j += GT) S.win[j] = bswap32(S.win[j]);
+      for (uint32_t j = t; j < 4 * nc; j += NT) S.win[j] = bswap32(S.win[j]);
       __syncthreads();
     };
     Round rd = issue_round(0);
-    if (a.gtabs) {
+    {
       // the slab's tables from the index pass, landing with the round's bits
       // (the previous item's last barrier has retired every read of them)
       const uint4* src = reinterpret_cast<const uint4*>(a.gtabs + it.slab);
       uint4* dst = reinterpret_cast<uint4*>(static_cast<GemvTabs*>(&S));
-      for (int k = t; k < int(sizeof(GemvTabs) / 16); k += GT) cp_async16(dst + k, src + k);
+      for (int k = t; k < int(sizeof(GemvTabs) / 16); k += NT) cp_async16(dst + k, src + k);
       cp_async_commit();
-    } else if (!build_tables<7, false, GT>(S, p + 16)) {  // validated when the index was built
-      if (t == 0) atomicOr(a.status, kStatusCodebook);
-      cp_async_wait_all();
-      __syncthreads();
-      continue;
     }
     if (NB > 0)
-      for (int k = t; k < 16 * (GT / 32) * GNB; k += GT) (&S.red[0][0][0])[k] = 0.f;
+      for (int k = t; k < 16 * (GTMAX / 32) * GNB; k += NT) (&S.red[0][0][0])[k] = 0.f;
     // Launched behind the stream's previous kernel (programmatic dependent
     // launch), everything above read only the payload, the index and the
     // plan; x, Y, the partials and the output are touched after that kernel
@@ -902,13 +910,15 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
       }
       finish_round(rd);
       const uint32_t tb = rd.tb, base_bit = rd.base_bit, slack = rd.slack;
-      bool act = mine && uint32_t(t) >= ta && uint32_t(t) < tb && b0 >= base_bit && b1 >= b0;
+      bool act = mine && uint32_t(tl) >= ta && uint32_t(tl) < tb && b0 >= base_bit && b1 >= b0 && bs >= b0 &&
+                 bs <= b1;
       SmemWin96 r;
-      r.init(S.win, act ? b0 - base_bit + slack : 0u);
+      r.init(S.win, act ? bs - base_bit + slack : 0u);
       bool dead = false;
       // sign/mantissa rows loaded one row ahead of use
-      uint4 nlo = ldg16(sq), nhi = soff ? ldg16(sq + 1) : make_uint4(0, 0, 0, 0);
-      for (int row = 0; row < 16; ++row) {
+      const int row0 = part * RPT;
+      uint4 nlo = ldg16(sq + row0), nhi = soff ? ldg16(sq + row0 + 1) : make_uint4(0, 0, 0, 0);
+      for (int row = row0; row < row0 + RPT; ++row) {
         const uint4 lo = nlo, hi = nhi;
         const int nr = row < 15 ? row + 1 : 15;
         nlo = ldg16(sq + nr);
@@ -990,7 +1000,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
     const uint32_t rr = uint32_t(t) / a.nb, bb = uint32_t(t) - rr * a.nb;
     float v = 0.f;
     if (comb)
-      for (int w = 0; w < GT / 32; ++w) v += S.red[rr][w][bb];
+      for (int w = 0; w < NT / 32; ++w) v += S.red[rr][w][bb];
     if (it.nitems == 1) {
       if (comb) store_y(a, sd.dst + rr, bb, v);
     } else {
@@ -1024,7 +1034,7 @@ __global__ void __launch_bounds__(GT, NB <= 1 ? 4 : 2) serial_tile_gemv_kernel(G
       __threadfence();
       const uint64_t n = a.peer_rows * a.ld, off = a.peer_row0 * a.ld;
       const float* src = a.peer_y[a.rank] + off;
-      for (uint64_t i = t; i < n; i += GT) {
+      for (uint64_t i = t; i < n; i += NT) {
         const float v = __ldcg(src + i);
         for (uint32_t g = 0; g < a.npeers; ++g)
           if (g != a.rank) a.peer_y[g][off + i] = v;
@@ -1074,10 +1084,12 @@ void serial_set_attr() {
   cudaFuncSetAttribute(serial_slab_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
   cudaFuncSetAttribute(serial_slab_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(SerialShared)));
-  cudaFuncSetAttribute(serial_tile_gemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
-  cudaFuncSetAttribute(serial_tile_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
-  cudaFuncSetAttribute(serial_tile_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
-  cudaFuncSetAttribute(serial_tile_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<0, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
+  cudaFuncSetAttribute(serial_tile_gemv_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(GemvShared)));
   if (bit) done.fetch_or(bit, std::memory_order_release);
 }
 
@@ -1119,11 +1131,11 @@ cudaError_t launch_serial_index(const Slab* slabs, uint32_t n, const uint8_t* pa
 // The indexed kernel is launched with programmatic stream serialisation: its
 // CTAs may start (table build, bit staging) while the stream's previous
 // kernel finishes, and wait for it before touching shared data.
-template <int NB>
+template <int NB, int SPLIT>
 cudaError_t launch_tile_kernel(const GemvArgs& args, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(args.nitems);
-  cfg.blockDim = dim3(GT);
+  cfg.blockDim = dim3(GT * SPLIT);
   cfg.dynamicSmemBytes = sizeof(GemvShared);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1131,22 +1143,37 @@ cudaError_t launch_tile_kernel(const GemvArgs& args, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, serial_tile_gemv_kernel<NB>, args);
+  return cudaLaunchKernelEx(&cfg, serial_tile_gemv_kernel<NB, SPLIT>, args);
+}
+
+// Two threads per tile when the items fill under one wave of 256-thread CTAs
+// (4 per SM).
+bool tile_split(uint32_t nitems) {
+  static std::atomic<int> sms{0};
+  int n = sms.load(std::memory_order_relaxed);
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms.store(n, std::memory_order_relaxed);
+  }
+  return nitems <= uint32_t(4 * n);
 }
 
 cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
   if (args.nb < 1 || args.nb > uint32_t(GNB)) return cudaErrorInvalidValue;
   serial_set_attr();
-  if (args.nb == 1) return launch_tile_kernel<1>(args, st);
-  if (args.nb == 2) return launch_tile_kernel<2>(args, st);
-  return launch_tile_kernel<4>(args, st);
+  if (args.nb == 1)
+    return tile_split(args.nitems) ? launch_tile_kernel<1, 2>(args, st) : launch_tile_kernel<1, 1>(args, st);
+  if (args.nb == 2) return launch_tile_kernel<2, 1>(args, st);
+  return launch_tile_kernel<4, 1>(args, st);
 }
 
 cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
   serial_set_attr();
-  return launch_tile_kernel<0>(args, st);
+  return tile_split(args.nitems) ? launch_tile_kernel<0, 2>(args, st) : launch_tile_kernel<0, 1>(args, st);
 }
 
 cudaError_t launch_tp_wait(const uint32_t* flags, uint32_t world, const uint32_t* epoch, int* status,
