@@ -33,6 +33,9 @@ sys.path.insert(0, str(ROOT / "xks-vectorforge_b200"))
 
 METRIC = "decode GB/s (BF16 out) vs HBM roofline; fused-GEMV tok/s Llama-8B b=1"
 HBM_FALLBACK_GBS = 6650.0
+# bytes of one 16-row serial slab's GEMV tables kept by xksv_plan_index
+# (sizeof(GemvTabs) in the library: 2048 16-bit entries + long-code data)
+GEMV_TABLE_BYTES = 5920
 
 
 def llama_tensors(hidden, layers, q_heads, kv_heads, head_dim, ffn, vocab, tied=False):
@@ -475,7 +478,8 @@ def fused_gemv(args, dev, stream, threads):
                 ms_per_token=round(ms, 4), codec="dfloat11", compressed_bytes=comp_bytes,
                 hbm_gbs=round(comp_bytes / (ms / 1e3) / 1e9, 1), launches_per_token=launches,
                 index_build_s=round(index_s, 3),
-                index_bytes=4 * sum(t["n"] * (t["cols"] // 16 + 1) for t in info),
+                index_bytes=8 * sum(t["n"] * (t["cols"] // 16 + 1) for t in info),
+                table_bytes=GEMV_TABLE_BYTES * sum(t["n"] for t in info),
                 rel_l2_layer0_down=rel, status_errors=bad, batch16=b16,
                 note="per token: 128 dependent plan launches (qkv, o, gate+up, down per layer) in one CUDA graph; "
                      "lm_head excluded as in runtime.py:258; batch16: the same plans at batch 16 on the tensor cores "
@@ -547,7 +551,9 @@ def run_case(args):
     line = dict(case=args.case, slabs=nslabs, compressed_bytes=len(payload), out_bytes=out,
                 ms_per_launch=round(ms, 5))
     if gemv:
-        idx = nslabs * (cols // 16 + 1) * 4
+        # read per call: each tile's first-code offset (and row-8 offset when a
+        # tile takes two threads) and each slab's tables from the index pass
+        idx = nslabs * ((cols // 16 + 1) * 8 + GEMV_TABLE_BYTES)
         line.update(batch=args.batch, launches=launches, route=args.route,
                     tflops=round(2 * (out / 2) * args.batch / ms / 1e9, 2),
                     gweights_per_s=round(out / 2 / ms / 1e6, 1),

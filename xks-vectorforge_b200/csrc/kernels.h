@@ -55,6 +55,7 @@ struct alignas(16) GemvTabs {
   uint8_t sorted[256];
   int maxlen, minlen;
 };
+static_assert(sizeof(GemvTabs) == 5920, "per-slab table bytes, as documented and counted by bench.py");
 
 struct GemvArgs {
   const GemvItem* items;
