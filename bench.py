@@ -1219,6 +1219,17 @@ def main():
                          "gemv-serial:16x4096:1024 runs the indexed batch-1 GEMV instead")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    # stdout carries the JSON line(s) alone: Python's prints keep the real
+    # stdout, while file descriptor 1, where native libraries (NCCL's version
+    # and debug lines among them) write, goes to stderr
+    sys.stdout.flush()
+    real_stdout = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(real_stdout, "w", buffering=1)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # NCCL's init lines (ranks, transports, NVLS) on record, on stderr; set
+        # before torch loads NCCL, which reads it once
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
     named = {"runtime": run_runtime, "config4-decode": run_config4_decode,
              "config4-gemv": run_config4_gemv, "config5": run_config5}
     if args.case in named:
@@ -1244,11 +1255,6 @@ def main():
     dev = f"cuda:{local}"
     if world > 1:
         import datetime
-        # NCCL's init lines (ranks, transports, NVLS) on stderr, so the run's
-        # rank count and collective path are on record (stdout keeps the one
-        # JSON line)
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device(dev))
     xksv_gpu.load()
