@@ -792,11 +792,11 @@ __global__ void __launch_bounds__(GT * SPLIT, SPLIT == 2 || NB > 1 ? 2 : 4) seri
     const uint32_t count = uint32_t(sd.rows * sd.cols);
     const uint32_t nbits = uint32_t(ld_le64(p + 8));
     // warm L2 with the item's sign/mantissa tiles and bit range (the tile
-    // index bounds it; clamped to the slab) while the tables are built.
-    // Measured on the Llama-3-8B forward of linears: +3 % tokens/s, the gain
-    // coming from its launches of under one wave; a full 1024-slab launch
-    // loses ~3 % to the extra L2 requests.
-    {
+    // index bounds it; clamped to the slab) while its tables arrive, in
+    // launches of under one wave (two threads per tile): measured on the
+    // Llama-3-8B forward of linears +3 % tokens/s from those launches, while a
+    // full 1024-slab launch loses ~3 % to the extra L2 requests.
+    if (SPLIT == 2) {
       const uint8_t* smp = p + kHdr + uint64_t(it.tile0) * 256;
       const uint64_t smn = uint64_t(it.ntiles) * 256;
       for (uint64_t off = uint64_t(t) * 128; off < smn; off += uint64_t(NT) * 128)
