@@ -121,7 +121,11 @@ def measured_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling under load.  The sampler is started
+    before the warm-up and waits for its first sample; the summary covers the
+    samples taken from mark() (the start of the warm-up steps) to the end of
+    the timed steps, at 10 ms intervals: the timed region alone is a few tens
+    of milliseconds, shorter than nvidia-smi's start-up."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -131,17 +135,24 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.mark_at = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.gpu)],
+                 "-lms", "10", "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
+            t0 = time.time()
+            while not self.lines and self.proc.poll() is None and time.time() - t0 < 5.0:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
+
+    def mark(self):
+        self.mark_at = len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -149,7 +160,9 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
-            time.sleep(0.25)
+            t0 = time.time()  # at least two samples from the loaded window
+            while len(self.lines) < self.mark_at + 2 and self.proc.poll() is None and time.time() - t0 < 1.0:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -159,7 +172,8 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = self.lines[self.mark_at:] or self.lines
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -172,7 +186,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=mx or None,
-                    reasons=sorted(reasons), samples=len(sm))
+                    reasons=sorted(reasons), samples=len(sm), window="warm-up and timed steps, 10 ms interval")
 
 
 def time_steps(fn, steps, stream):
@@ -1292,18 +1306,19 @@ def main():
         checked += rows * cols * 2
     assert checked == out_bytes
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
-    stream.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        clk.mark()
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
         t = time_steps(step, args.steps, stream)
         torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
     assert plan.status(h) == 0
     launches = plan.launches() * args.steps
     if world > 1:
