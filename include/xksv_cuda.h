@@ -155,10 +155,12 @@ int xksv_plan_launches(const xksv_plan* plan);
 
 /* Builds the plan's tile index for resident weights: one decode pass over
  * the plan's 16-row serial-codec slabs with cols % 16 == 0 records the bit
- * offset at which every 16x16 tile's codes start (4 bytes per tile, kept on
- * the device with the plan).  Afterwards xksv_plan_gemm with the same
- * d_payload pointer decodes those slabs tile-parallel, one thread per tile,
- * instead of re-synchronising each slab's single bit stream on every call.
+ * offsets at which every 16x16 tile's codes and its row 8 start (8 bytes per
+ * tile) and each slab's decode tables (5920 bytes per slab), all kept on the
+ * device with the plan.  Afterwards xksv_plan_gemm and xksv_plan_decode with
+ * the same d_payload pointer decode those slabs tile-parallel (one or two
+ * threads per tile) instead of re-synchronising each slab's single bit
+ * stream on every call.
  * The index describes the payload's contents at this call: rebuild it if they
  * change.  No reference counterpart (the reference decodes every slab from
  * its first bit, cuda/decode.cu:12-45); it is an acceleration structure on
