@@ -1163,6 +1163,7 @@ bool tile_split(uint32_t nitems) {
 cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
   if (args.nb < 1 || args.nb > uint32_t(GNB)) return cudaErrorInvalidValue;
+  if (!args.gtabs || !args.tmid) return cudaErrorInvalidValue;  // the index pass's tables and row-8 offsets
   serial_set_attr();
   if (args.nb == 1)
     return tile_split(args.nitems) ? launch_tile_kernel<1, 2>(args, st) : launch_tile_kernel<1, 1>(args, st);
@@ -1172,6 +1173,7 @@ cudaError_t launch_serial_tile_gemm(const GemvArgs& args, cudaStream_t st) {
 
 cudaError_t launch_serial_tile_decode(const GemvArgs& args, cudaStream_t st) {
   if (!args.nitems) return cudaSuccess;
+  if (!args.gtabs || !args.tmid) return cudaErrorInvalidValue;
   serial_set_attr();
   return tile_split(args.nitems) ? launch_tile_kernel<0, 2>(args, st) : launch_tile_kernel<0, 1>(args, st);
 }
