@@ -705,16 +705,18 @@ __global__ void __launch_bounds__(ST, 3) serial_slab_kernel(const Slab* __restri
 }
 
 // ------------------------------------------------ indexed tile GEMV ------
-// With a tile index (the bit offset of every 16x16 tile's first code, built
-// once per plan by serial_slab_kernel<2>), every tile of a 16-row slab can be
-// decoded on its own: one thread per tile, no speculative pass.  A CTA takes
-// up to GT consecutive tiles of one slab, stages their bits in shared memory
-// (in several rounds when they do not fit), and each thread walks its tile
-// row by row: 16 codes, 16 FP32 weights assembled from the table entry
-// (exponent at bit 23) and the sign/mantissa bytes, 16 FMAs with x held in
-// registers, then a warp sum per row.  Slabs split over several CTAs combine
-// their row sums in a fixed order in the last CTA to finish (deterministic,
-// and Y is overwritten as cuda/decode.cu:31 requires).
+// With a tile index (the bit offsets of every 16x16 tile's first code and of
+// its row 8, and each slab's decode tables, built once per plan by
+// serial_slab_kernel<2>), every tile of a 16-row slab can be decoded on its
+// own: one thread per tile (or two, rows 0-7 and 8-15), no speculative pass.
+// A CTA takes up to GT consecutive tiles of one slab, copies the slab's
+// tables and stages the tiles' bits in shared memory (in several rounds when
+// they do not fit), and each thread walks its rows: 16 codes a row, 16 FP32
+// weights assembled from the table entry (exponent at bit 23) and the
+// sign/mantissa bytes, 16 FMAs with x held in registers, then a warp sum per
+// row.  Slabs split over several CTAs combine their row sums in a fixed order
+// in the last CTA to finish (deterministic, and Y is overwritten as
+// cuda/decode.cu:31 requires).
 constexpr int GT = 256;                  // tiles per GEMV item (CTA)
 constexpr int GPAD = 160;                // zero words past a round: one row of 16 maximal codes + window
 constexpr int GWINW = 6144 + GPAD;       // staged bit words per round
