@@ -34,3 +34,13 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["kind"] == "reference" and d["cpu_baseline"]["bytes_match"] is True
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
     assert "workload" in d["config"]
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun the reference arm runs on rank 0 alone; any other rank
+    exits 0 without work or output."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", WORLD_SIZE="2", RANK="1", LOCAL_RANK="1")
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "3",
+                        "--warmup", "3"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout == ""
